@@ -1,0 +1,352 @@
+"""Benchmark of the fused diffusion stencil (one JSON line on rank 0).
+
+Workload (default, "fused_fwd"): the single-GPU fused forward of the stencil
+on bf16 x[B=1, L, D=512] ~ N(0,1), alpha = 0.1, `--stencil-steps` steps in ONE
+launch ([B, L, D] layout, the model / serving layout).  One bench step = one
+fused call over one batch.  Inputs and outputs rotate through a pool of
+buffers larger than L2, so every call streams from HBM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--L 65536] [--stencil-steps 4] [--no-sweep]
+
+N > 1 (torchrun, one rank per GPU): every rank runs the same per-GPU workload
+on its own GPU (independent replicas, weak scaling; the stencil of one
+sequence shards only with the L-sharded workload, `--workload sharded`).
+
+Reported: `value` tokens/s with inputs resident in HBM (device-timed, max over
+ranks); `e2e` the same through the public API with pinned host buffers
+(H2D + kernel + D2H each step); `roofline` of the fused kernel against the
+measured HBM copy bandwidth; `cpu_baseline` the CPU oracle (the reference's
+algorithm in PyTorch) on the host cores; `clocks` sampled during timing.
+`--impl reference` times that CPU implementation alone.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO), str(REPO / "continuous-time-attention_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "fused diffusion stencil tokens/s & HBM GB/s (% of peak) at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def _ncu_traffic(key: str):
+    p = REPO / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(key)
+    except Exception:  # noqa: BLE001
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [v.strip() for v in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle (the reference's algorithm) on the host cores
+# ---------------------------------------------------------------------------
+def cpu_reference_rate(L: int, D: int, steps: int, seconds: float = 12.0, max_calls: int = 64):
+    """Tokens/s of the CPU oracle on row windows of the [1, L, D] bf16 workload."""
+    from oracle import diffusion_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows = min(L, 4096)
+    torch.manual_seed(0)
+    x = torch.randn(1, rows + 2 * steps, D).to(torch.bfloat16)
+    O.steps_bld(x, alpha=0.1, steps=steps)  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_calls and (time.perf_counter() - t0) < seconds:
+        O.steps_bld(x, alpha=0.1, steps=steps)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {
+        "value": rows * n / dt,
+        "unit": "tokens/s",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"{n} calls of the oracle (reference algorithm, torch CPU fp32) on {rows}-row windows "
+                  f"(+{steps}-row halos) of the bf16 [1, {L}, {D}] input, {dt:.1f} s",
+    }
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    from oracle import diffusion_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    L, D, S = args.L, args.D, args.stencil_steps
+    rows = min(L, 1024)
+    torch.manual_seed(0)
+    x = torch.randn(1, rows + 2 * S, D).to(torch.bfloat16)
+    for _ in range(args.warmup):
+        O.steps_bld(x, alpha=0.1, steps=S)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.steps_bld(x, alpha=0.1, steps=S)
+    dt = time.perf_counter() - t0
+    v = rows * args.steps / dt
+    cores = torch.get_num_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": _config(args),
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"each step: {rows}-row window (+{S}-row halos) of the bf16 [1, {L}, {D}] "
+                                   f"input through the CPU oracle (reference algorithm, torch fp32)"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _config(args):
+    return {"workload": "fused_fwd_bld", "B": 1, "L": args.L, "D": args.D, "steps": args.stencil_steps,
+            "alpha": 0.1, "layout": "bld", "global_batch": args.gpus, "seq_len": args.L,
+            "parallelism": f"replicas x{args.gpus}",
+            "l2": "rotating input/output buffers, >= 4x L2 per rank"}
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+def _time_launches(fn, n: int, stream) -> float:
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(n):
+        fn(i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / 1e3
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import torch.distributed as dist
+
+    from cta_b200 import _lib, ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L, D, S = args.L, args.D, args.stencil_steps
+    esize = 2
+    tensor_bytes = L * D * esize
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    nbuf = max(2, min(64, (4 * l2) // tensor_bytes + 1))
+    torch.manual_seed(1234 + rank)
+    xs = [torch.randn(1, L, D, device=dev, dtype=torch.bfloat16) for _ in range(nbuf)]
+    ys = [torch.empty_like(xs[0]) for _ in range(nbuf)]
+    alphas = [0.1] * S
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        ops.bld_forward(xs[i % nbuf], alphas, S, out=ys[i % nbuf])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    elapsed = _time_launches(step, args.steps, stream)
+    if sampler:
+        sampler.__exit__(None, None, None)
+    if world > 1:
+        t = torch.tensor([elapsed], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+        dist.barrier()
+    per_call = elapsed / args.steps
+    tokens_per_step = L * world
+    value = tokens_per_step / per_call
+
+    # e2e through the public API: pinned host in -> device -> kernel -> host out, each step
+    hx = torch.randn(1, L, D, dtype=torch.bfloat16).pin_memory()
+    hy = torch.empty_like(hx).pin_memory()
+    dx_in = torch.empty(1, L, D, device=dev, dtype=torch.bfloat16)
+
+    def e2e_step(_i):
+        dx_in.copy_(hx, non_blocking=True)
+        y = ops.bld_forward(dx_in, alphas, S)
+        hy.copy_(y, non_blocking=True)
+
+    k_e2e = max(3, min(args.steps, 30))
+    for i in range(2):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    e2e_t = _time_launches(e2e_step, k_e2e, stream)
+    if world > 1:
+        t = torch.tensor([e2e_t], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_t = float(t.item())
+    e2e_value = L * world / (e2e_t / k_e2e)
+
+    peak, peak_kind = _peaks()
+    algo_bytes = 2 * tensor_bytes
+    achieved = algo_bytes / per_call / 1e9
+    traffic = _ncu_traffic(f"fused_fwd_bld_L{L}_D{D}_S{S}")
+
+    sweep = None
+    if not args.no_sweep and world == 1:
+        sweep = []
+        for Ls in (4096, 16384, 65536):
+            nb = max(2, min(64, (4 * l2) // (Ls * D * esize) + 1))
+            bx = [torch.randn(1, Ls, D, device=dev, dtype=torch.bfloat16) for _ in range(nb)]
+            by = [torch.empty_like(bx[0]) for _ in range(nb)]
+            for Ss in (2, 4, 8):
+                fn = (lambda i, bx=bx, by=by, Ss=Ss, nb=nb: ops.bld_forward(bx[i % nb], [0.1] * Ss, Ss, out=by[i % nb]))
+                for i in range(5):
+                    fn(i)
+                n = 200
+                t = _time_launches(fn, n, stream) / n
+                gbs = 2 * Ls * D * esize / t / 1e9
+                sweep.append({"L": Ls, "steps": Ss, "us_per_call": round(t * 1e6, 2), "GB/s": round(gbs, 1),
+                              "frac": round(gbs / peak, 3), "tokens/s": round(Ls / t)})
+            del bx, by
+
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        cpu = cpu_reference_rate(L, D, S)
+
+    if rank == 0:
+        clocks = sampler.summary() if sampler else None
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": per_call * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": _config(args),
+            "hbm_gbs": achieved, "hbm_frac": achieved / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_kind": f"{peak_kind} STREAM copy (MEASURED_PEAKS.json hbm_gbs)"
+                         if peak_kind == "measured" else "fallback 6650 GB/s",
+                         "algorithmic_bytes_per_launch": algo_bytes},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": tensor_bytes,
+                    "d2h_bytes_per_step": tensor_bytes},
+            "gpu_launches": args.steps,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        if sweep is not None:
+            line["sweep"] = sweep
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--L", type=int, default=65536)
+    ap.add_argument("--D", type=int, default=512)
+    ap.add_argument("--stencil-steps", type=int, default=4)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,505 @@
+// C ABI of libcta_stencil.so: argument validation, tile sizing, TMA tensor-map
+// encoding and kernel dispatch.  Declarations and contracts live in
+// include/cta_stencil.h.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "cta_stencil.h"
+#include "kernels.h"
+
+using namespace cta;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(CTA_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int ok() {
+  return CTA_OK;
+}
+
+size_t dtype_size(int dtype) { return dtype == CTA_F32 ? 4 : 2; }
+
+bool valid_dtype(int dtype) { return dtype == CTA_F32 || dtype == CTA_BF16 || dtype == CTA_F16; }
+
+bool valid_mask_dtype(int d) { return d >= CTA_MASK_U8 && d <= CTA_MASK_F16; }
+
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+// ---------------------------------------------------------------------------
+// TMA tensor maps
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D map over a [nb, rows, D] tensor with element strides (sB, sL, 1); box is
+// kBldRC rows x kBldDT columns.  Returns false when TMA cannot address it.
+bool make_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t rows, int64_t D, int64_t sB,
+              int64_t sL) {
+  auto fn = encode_fn();
+  if (fn == nullptr || base == nullptr) return false;
+  const int64_t es = static_cast<int64_t>(dtype_size(dtype));
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return false;
+  if ((sL * es) % 16 != 0 || sL < D) return false;
+  if (rows >= (1LL << 31) - 4096 || D >= (1LL << 31) || nb >= (1LL << 31)) return false;
+  int64_t bstride = sB * es;
+  if (nb == 1) bstride = ((rows * sL * es + 15) / 16) * 16;
+  if (bstride % 16 != 0 || bstride <= 0) return false;
+  if (sL * es >= (1LL << 40) || bstride >= (1LL << 40)) return false;
+  cuuint64_t gdim[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(nb)};
+  cuuint64_t gstride[2] = {static_cast<cuuint64_t>(sL * es), static_cast<cuuint64_t>(bstride)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBldDT), static_cast<cuuint32_t>(kBldRC), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapDataType dt = dtype == CTA_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == CTA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(m, dt, 3, const_cast<void*>(base), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------------------
+// tile sizing: enough CTAs for ~kCtasPerSm resident per SM, tiles long enough
+// that the 2*steps halo rows stay a small overhead
+// ---------------------------------------------------------------------------
+struct Tuning {
+  int ctas_per_sm = 6;
+  int tl_override = 0;
+};
+Tuning g_tuning;
+
+int pick_tl(int64_t rows, int64_t parallel_ctas, int steps) {
+  if (g_tuning.tl_override > 0) return std::min(kBldMaxTL, ((g_tuning.tl_override + kBldRC - 1) / kBldRC) * kBldRC);
+  const int64_t target = static_cast<int64_t>(num_sms()) * g_tuning.ctas_per_sm;
+  int64_t tl = (rows * std::max<int64_t>(parallel_ctas, 1) + target - 1) / target;
+  tl = ((tl + kBldRC - 1) / kBldRC) * kBldRC;
+  const int64_t min_tl = steps >= 6 ? 64 : 32;
+  tl = std::max(tl, min_tl);
+  tl = std::min<int64_t>(tl, kBldMaxTL);
+  return static_cast<int>(tl);
+}
+
+void fill_alpha(BldArgs& a, int steps, const float* alpha, const void* const* alpha_dev, int alpha_dev_dtype) {
+  for (int k = 0; k < kMaxSteps; ++k) {
+    a.alpha[k] = (alpha != nullptr && k < steps) ? alpha[k] : 0.f;
+    a.alpha_dev[k] = (alpha_dev != nullptr && k < steps) ? alpha_dev[k] : nullptr;
+  }
+  a.alpha_dev_dtype = alpha_dev_dtype;
+}
+
+int check_alpha(int steps, const float* alpha, const void* const* alpha_dev, int alpha_dev_dtype) {
+  if (alpha == nullptr && alpha_dev == nullptr) return fail(CTA_EINVAL, "alpha: need host or device coefficients");
+  if (alpha == nullptr) {
+    for (int k = 0; k < steps; ++k)
+      if (alpha_dev[k] == nullptr) return fail(CTA_EINVAL, "alpha_dev[%d] is NULL and no host alpha given", k);
+  }
+  if (alpha_dev != nullptr && !valid_dtype(alpha_dev_dtype))
+    return fail(CTA_EINVAL, "alpha_dev_dtype %d is not a float dtype", alpha_dev_dtype);
+  return CTA_OK;
+}
+
+int check_common(int dtype, int steps) {
+  if (!valid_dtype(dtype)) return fail(CTA_EINVAL, "unsupported dtype code %d", dtype);
+  if (steps < 1 || steps > kMaxSteps)
+    return fail(CTA_EINVAL, "steps must be in 1..%d for a fused launch, got %d", kMaxSteps, steps);
+  return CTA_OK;
+}
+
+BldArgs blank_bld() {
+  BldArgs a;
+  std::memset(&a, 0, sizeof(a));
+  return a;
+}
+
+int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int64_t tile_rows, cudaStream_t st,
+               const CUtensorMap& xmap) {
+  const int64_t ntl = (tile_rows + a.TL - 1) / a.TL;
+  const int64_t ndt = (a.D + kBldDT - 1) / kBldDT;
+  if (ntl <= 0 || nbatch <= 0) return ok();
+  if (ntl > 0x7fffffffLL || ndt > 65535 || nbatch > 65535)
+    return fail(CTA_EUNSUPPORTED, "grid too large (tiles %lld, D tiles %lld, batch %lld)", (long long)ntl,
+                (long long)ndt, (long long)nbatch);
+  dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(nbatch));
+  const cudaError_t e = launch_bld_fwd(a, &xmap, dtype, steps, causal, grid, bld_smem_bytes(dtype, 0), st);
+  if (e != cudaSuccess) return cuda_fail(e, "bld forward launch");
+  return ok();
+}
+
+int64_t dalpha_max_ctas(int64_t B, int64_t L, int64_t D) {
+  const int64_t ntl = (L + 31) / 32;  // pick_tl never goes below 32 rows
+  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
+  return ntl * ndt * B;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cta_abi_version(void) { return CTA_ABI_VERSION; }
+
+const char* cta_last_error(void) { return t_last_error.c_str(); }
+
+int cta_device_error(int clear) {
+  const int a = read_device_error_bld_fwd(clear);
+  const int b = read_device_error_bld_bwd(clear);
+  const int c = read_device_error_bdl(clear);
+  if (a < 0 || b < 0 || c < 0) return -1;
+  return a != 0 ? a : (b != 0 ? b : c);
+}
+
+// Tuning hook used by the benchmark sweeps (key 0: CTAs per SM target,
+// key 1: forced tile rows, 0 = automatic).  Returns the previous value.
+int cta_set_tuning(int key, int value) {
+  int prev = 0;
+  if (key == 0) {
+    prev = g_tuning.ctas_per_sm;
+    g_tuning.ctas_per_sm = value > 0 ? value : 6;
+  } else if (key == 1) {
+    prev = g_tuning.tl_override;
+    g_tuning.tl_override = value > 0 ? value : 0;
+  }
+  return prev;
+}
+
+// ---------------------------------------------------------------------------
+// [B, D, L]
+// ---------------------------------------------------------------------------
+int cta_diffusion_bdl_ex(const void* in, void* out, int64_t B, int64_t D, int64_t L, int64_t in_row_stride,
+                         int64_t out_row_stride, int dtype, int steps, int causal, int backward, const float* alpha,
+                         const void* const* alpha_dev, int alpha_dev_dtype, const void* mask, int mask_dtype,
+                         int64_t mask_sB, int64_t mask_sL, void* stream) {
+  int rc = check_common(dtype, steps);
+  if (rc) return rc;
+  rc = check_alpha(steps, alpha, alpha_dev, alpha_dev_dtype);
+  if (rc) return rc;
+  if (B < 0 || D < 0 || L < 0) return fail(CTA_EINVAL, "negative shape");
+  if (B == 0 || D == 0 || L == 0) return ok();
+  if (in == nullptr || out == nullptr) return fail(CTA_EINVAL, "null tensor pointer");
+  if (in_row_stride < L || out_row_stride < L) return fail(CTA_EINVAL, "row stride smaller than L");
+  if (mask != nullptr && !valid_mask_dtype(mask_dtype)) return fail(CTA_EINVAL, "bad mask dtype %d", mask_dtype);
+  if (L < 3) return fail(CTA_EINVAL, "L < 3 is the identity; handled by the caller");
+  BdlArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.in = in;
+  a.out = out;
+  a.rows = B * D;
+  a.D = D;
+  a.L = L;
+  a.in_rs = in_row_stride;
+  a.out_rs = out_row_stride;
+  const size_t es = dtype_size(dtype);
+  a.vec_ok = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
+             ((in_row_stride * static_cast<int64_t>(es)) % 16 == 0) &&
+             ((out_row_stride * static_cast<int64_t>(es)) % 16 == 0);
+  a.mask = mask;
+  a.mask_dtype = mask_dtype;
+  a.msB = mask_sB;
+  a.msL = mask_sL;
+  for (int k = 0; k < kMaxSteps; ++k) {
+    a.alpha[k] = (alpha != nullptr && k < steps) ? alpha[k] : 0.f;
+    a.alpha_dev[k] = (alpha_dev != nullptr && k < steps) ? alpha_dev[k] : nullptr;
+  }
+  a.alpha_dev_dtype = alpha_dev_dtype;
+  const cudaError_t e = launch_bdl(a, dtype, steps, causal ? 1 : 0, backward ? 1 : 0, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bdl launch");
+  return ok();
+}
+
+int cta_diffusion_fwd_bdl(const void* x, void* y, int64_t B, int64_t D, int64_t L, int64_t row_stride, int dtype,
+                          int steps, float alpha, void* stream) {
+  float al[kMaxSteps];
+  for (int k = 0; k < kMaxSteps; ++k) al[k] = alpha;
+  return cta_diffusion_bdl_ex(x, y, B, D, L, row_stride, row_stride, dtype, steps, 0, 0, al, nullptr, CTA_F32,
+                              nullptr, 0, 0, 0, stream);
+}
+
+int cta_diffusion_bwd_bdl(const void* grad_out, void* grad_in, int64_t B, int64_t D, int64_t L, int64_t row_stride,
+                          int dtype, int steps, float alpha, void* stream) {
+  float al[kMaxSteps];
+  for (int k = 0; k < kMaxSteps; ++k) al[k] = alpha;
+  return cta_diffusion_bdl_ex(grad_out, grad_in, B, D, L, row_stride, row_stride, dtype, steps, 0, 1, al, nullptr,
+                              CTA_F32, nullptr, 0, 0, 0, stream);
+}
+
+// ---------------------------------------------------------------------------
+// [B, L, D]
+// ---------------------------------------------------------------------------
+int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t D, int64_t x_sB, int64_t x_sL,
+                          int64_t y_sB, int64_t y_sL, int dtype, int steps, int causal, const float* alpha,
+                          const void* const* alpha_dev, int alpha_dev_dtype, const void* mask, int mask_dtype,
+                          int64_t mask_sB, int64_t mask_sL, void* stream) {
+  int rc = check_common(dtype, steps);
+  if (rc) return rc;
+  rc = check_alpha(steps, alpha, alpha_dev, alpha_dev_dtype);
+  if (rc) return rc;
+  if (B < 0 || L < 0 || D < 0) return fail(CTA_EINVAL, "negative shape");
+  if (B == 0 || L == 0 || D == 0) return ok();
+  if (L < 3) return fail(CTA_EINVAL, "L < 3 is the identity; handled by the caller");
+  if (x == nullptr || y == nullptr) return fail(CTA_EINVAL, "null tensor pointer");
+  if (x_sL < D || y_sL < D) return fail(CTA_EINVAL, "row stride smaller than D");
+  if (mask != nullptr && !valid_mask_dtype(mask_dtype)) return fail(CTA_EINVAL, "bad mask dtype %d", mask_dtype);
+  BldArgs a = blank_bld();
+  a.x = x;
+  a.y = y;
+  a.xsB = x_sB;
+  a.xsL = x_sL;
+  a.ysB = y_sB;
+  a.ysL = y_sL;
+  a.L = L;
+  a.D = static_cast<int>(D);
+  a.nbatch = static_cast<int>(B);
+  a.pos_offset = 0;
+  a.global_len = L;
+  a.mask = mask;
+  a.mask_dtype = mask_dtype;
+  a.msB = mask_sB;
+  a.msL = mask_sL;
+  fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
+  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
+  a.TL = pick_tl(L, ndt * B, steps);
+  a.out_begin = 0;
+  a.out_end = L;
+  CUtensorMap xmap;
+  std::memset(&xmap, 0, sizeof(xmap));
+  a.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL) ? 1 : 0;
+  return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), xmap);
+}
+
+int64_t cta_diffusion_bwd_bld_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype, int steps, int causal) {
+  (void)dtype;
+  (void)causal;
+  if (B <= 0 || L <= 0 || D <= 0 || steps < 1 || steps > kMaxSteps) return 256;
+  return 256 + dalpha_max_ctas(B, L, D) * steps * static_cast<int64_t>(sizeof(float));
+}
+
+int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, float* dalpha, void* workspace,
+                          int64_t workspace_bytes, int64_t B, int64_t L, int64_t D, int64_t g_sB, int64_t g_sL,
+                          int64_t x_sB, int64_t x_sL, int64_t d_sB, int64_t d_sL, int dtype, int steps, int causal,
+                          const float* alpha, const void* const* alpha_dev, int alpha_dev_dtype, const void* mask,
+                          int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream) {
+  int rc = check_common(dtype, steps);
+  if (rc) return rc;
+  rc = check_alpha(steps, alpha, alpha_dev, alpha_dev_dtype);
+  if (rc) return rc;
+  if (B < 0 || L < 0 || D < 0) return fail(CTA_EINVAL, "negative shape");
+  if (L > 0 && L < 3) return fail(CTA_EINVAL, "L < 3 is the identity; handled by the caller");
+  if (grad_out == nullptr || grad_in == nullptr) return fail(CTA_EINVAL, "null tensor pointer");
+  if (g_sL < D || d_sL < D) return fail(CTA_EINVAL, "row stride smaller than D");
+  if (mask != nullptr && !valid_mask_dtype(mask_dtype)) return fail(CTA_EINVAL, "bad mask dtype %d", mask_dtype);
+  const bool da = dalpha != nullptr;
+  if (da) {
+    if (x == nullptr) return fail(CTA_EINVAL, "dalpha requested without the forward input x");
+    if (x_sL < D) return fail(CTA_EINVAL, "x row stride smaller than D");
+    if (workspace == nullptr || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+      return fail(CTA_EINVAL, "dalpha needs a 256-byte aligned workspace");
+    if (workspace_bytes < cta_diffusion_bwd_bld_workspace_bytes(B, L, D, dtype, steps, causal))
+      return fail(CTA_EINVAL, "workspace too small: %lld < %lld bytes", (long long)workspace_bytes,
+                  (long long)cta_diffusion_bwd_bld_workspace_bytes(B, L, D, dtype, steps, causal));
+  }
+  if (B == 0 || L == 0 || D == 0) {
+    if (da) {
+      const cudaError_t e = cudaMemsetAsync(dalpha, 0, sizeof(float) * steps, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e, "dalpha clear");
+    }
+    return ok();
+  }
+  BldArgs a = blank_bld();
+  a.g = grad_out;
+  a.x = x;
+  a.y = grad_in;
+  a.gsB = g_sB;
+  a.gsL = g_sL;
+  a.xsB = x_sB;
+  a.xsL = x_sL;
+  a.ysB = d_sB;
+  a.ysL = d_sL;
+  a.L = L;
+  a.D = static_cast<int>(D);
+  a.nbatch = static_cast<int>(B);
+  a.global_len = L;
+  a.mask = mask;
+  a.mask_dtype = mask_dtype;
+  a.msB = mask_sB;
+  a.msL = mask_sL;
+  fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
+  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
+  a.TL = std::max(pick_tl(L, ndt * B, steps), 32);
+  a.out_begin = 0;
+  a.out_end = L;
+  const int64_t ntl = (L + a.TL - 1) / a.TL;
+  if (ntl > 0x7fffffffLL || ndt > 65535 || B > 65535) return fail(CTA_EUNSUPPORTED, "grid too large");
+  dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(B));
+  CUtensorMap gmap, xmap;
+  std::memset(&gmap, 0, sizeof(gmap));
+  std::memset(&xmap, 0, sizeof(xmap));
+  bool tma = make_map(&gmap, grad_out, dtype, B, L, D, g_sB, g_sL);
+  if (da) tma = tma && make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL);
+  else xmap = gmap;
+  a.use_tma = tma ? 1 : 0;
+  if (da) {
+    a.num_ctas = static_cast<int>(ntl * ndt * B);
+    a.counter = static_cast<unsigned int*>(workspace);
+    a.dalpha_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+    a.dalpha = dalpha;
+  }
+  const cudaError_t e = launch_bld_bwd(a, &gmap, &xmap, dtype, steps, causal ? 1 : 0, da ? 1 : 0, grid,
+                                       bld_smem_bytes(dtype, da ? 1 : 0), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "bld backward launch");
+  return ok();
+}
+
+int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t D, int64_t x_sL, int64_t y_sL,
+                             const int32_t* cu_seqlens, int64_t nseq, int64_t max_len, int pad_to_max, int dtype,
+                             int steps, float alpha, void* stream) {
+  int rc = check_common(dtype, steps);
+  if (rc) return rc;
+  if (total_rows < 0 || D < 0 || nseq < 0 || max_len < 0) return fail(CTA_EINVAL, "negative shape");
+  if (total_rows == 0 || D == 0 || nseq == 0 || max_len == 0) return ok();
+  if (x == nullptr || y == nullptr || cu_seqlens == nullptr) return fail(CTA_EINVAL, "null pointer");
+  if (x_sL < D || y_sL < D) return fail(CTA_EINVAL, "row stride smaller than D");
+  if (nseq > 65535) return fail(CTA_EUNSUPPORTED, "at most 65535 sequences per call, got %lld", (long long)nseq);
+  BldArgs a = blank_bld();
+  a.x = x;
+  a.y = y;
+  a.xsL = x_sL;
+  a.ysL = y_sL;
+  a.xsB = 0;
+  a.ysB = 0;
+  a.L = total_rows;
+  a.D = static_cast<int>(D);
+  a.nbatch = static_cast<int>(nseq);
+  a.cu_seqlens = cu_seqlens;
+  a.pad_to_max = pad_to_max ? 1 : 0;
+  a.max_len = max_len;
+  for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
+  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
+  // tiles are cut per sequence: size them from the average sequence length
+  const int64_t avg = std::max<int64_t>(1, total_rows / nseq);
+  a.TL = pick_tl(avg, ndt * nseq, steps);
+  a.out_begin = 0;
+  a.out_end = max_len;
+  CUtensorMap xmap;
+  std::memset(&xmap, 0, sizeof(xmap));
+  a.use_tma = make_map(&xmap, x, dtype, 1, total_rows, D, 0, x_sL) ? 1 : 0;
+  return launch_fwd(a, dtype, steps, 0, nseq, max_len, static_cast<cudaStream_t>(stream), xmap);
+}
+
+int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_local, int64_t D, int64_t pos_offset,
+                            int64_t global_len, const void* lo_halo, int64_t lo_rows, const void* hi_halo,
+                            int64_t hi_rows, int part, int dtype, int steps, int causal, int backward, float alpha,
+                            void* stream) {
+  int rc = check_common(dtype, steps);
+  if (rc) return rc;
+  if (B < 0 || L_local < 0 || D < 0 || pos_offset < 0) return fail(CTA_EINVAL, "negative shape");
+  if (B == 0 || L_local == 0 || D == 0) return ok();
+  if (in == nullptr || out == nullptr) return fail(CTA_EINVAL, "null tensor pointer");
+  if (pos_offset + L_local > global_len) return fail(CTA_EINVAL, "shard exceeds the global sequence");
+  if (global_len < 3) return fail(CTA_EINVAL, "global length < 3 is the identity; handled by the caller");
+  const int hl = causal ? (backward ? 0 : 2 * steps) : steps;
+  const int hr = causal ? (backward ? 2 * steps : 0) : steps;
+  const bool has_lo = pos_offset > 0;
+  const bool has_hi = pos_offset + L_local < global_len;
+  const int64_t ib = has_lo ? std::min<int64_t>(hl, L_local) : 0;
+  const int64_t ie = has_hi ? std::max<int64_t>(L_local - hr, ib) : L_local;
+  int64_t ob = 0, oe = 0;
+  if (part == CTA_SHARD_INTERIOR) {
+    ob = ib;
+    oe = ie;
+  } else if (part == CTA_SHARD_LO_EDGE) {
+    ob = 0;
+    oe = ib;
+  } else if (part == CTA_SHARD_HI_EDGE) {
+    ob = ie;
+    oe = L_local;
+  } else {
+    return fail(CTA_EINVAL, "bad shard part %d", part);
+  }
+  if (oe <= ob) return ok();
+  const bool edge = part != CTA_SHARD_INTERIOR;
+  if (edge) {
+    // an edge tile may reach past both shard ends when the shard is short: both halos must be present
+    if (has_lo && hl > 0 && (lo_halo == nullptr || lo_rows < hl))
+      return fail(CTA_EINVAL, "lo halo missing or shorter than %d rows", hl);
+    if (has_hi && hr > 0 && (hi_halo == nullptr || hi_rows < hr))
+      return fail(CTA_EINVAL, "hi halo missing or shorter than %d rows", hr);
+    if (lo_rows < 0 || hi_rows < 0 || lo_rows > (1 << 20) || hi_rows > (1 << 20))
+      return fail(CTA_EINVAL, "bad halo row counts");
+  }
+  BldArgs a = blank_bld();
+  if (backward) a.g = in;
+  else a.x = in;
+  a.y = out;
+  a.xsB = a.gsB = a.ysB = L_local * D;
+  a.xsL = a.gsL = a.ysL = D;
+  a.L = L_local;
+  a.D = static_cast<int>(D);
+  a.nbatch = static_cast<int>(B);
+  a.pos_offset = pos_offset;
+  a.global_len = global_len;
+  if (edge) {
+    a.lo_ext = has_lo ? lo_halo : nullptr;
+    a.hi_ext = has_hi ? hi_halo : nullptr;
+    a.hext_lo = a.lo_ext ? static_cast<int>(lo_rows) : 0;
+    a.hext_hi = a.hi_ext ? static_cast<int>(hi_rows) : 0;
+  }
+  for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
+  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
+  a.TL = edge ? static_cast<int>(std::min<int64_t>(kBldMaxTL, ((oe - ob + kBldRC - 1) / kBldRC) * kBldRC))
+              : pick_tl(oe - ob, ndt * B, steps);
+  a.out_begin = ob;
+  a.out_end = oe;
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  a.use_tma = (!edge && make_map(&map, in, dtype, B, L_local, D, L_local * D, D)) ? 1 : 0;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!backward) return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, oe - ob, st, map);
+  const int64_t ntl = (oe - ob + a.TL - 1) / a.TL;
+  if (ntl > 0x7fffffffLL || ndt > 65535 || B > 65535) return fail(CTA_EUNSUPPORTED, "grid too large");
+  dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(B));
+  const cudaError_t e = launch_bld_bwd(a, &map, &map, dtype, steps, causal ? 1 : 0, 0, grid, bld_smem_bytes(dtype, 0), st);
+  if (e != cudaSuccess) return cuda_fail(e, "shard backward launch");
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,98 @@
+// Internal launch descriptors shared by the C ABI (capi.cu) and the kernel
+// translation units.  Host-only code sees plain structs; nothing here is part
+// of the public ABI (that is include/cta_stencil.h).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cta {
+
+constexpr int kMaxSteps = 8;
+
+// ---------------------------------------------------------------------------
+// [B, L, D] layout (feature axis contiguous): TMA-fed march along L
+// ---------------------------------------------------------------------------
+constexpr int kBldThreads = 128;              // 4 warps, all spread along D
+constexpr int kBldVec = 2;                    // columns per thread (one float2)
+constexpr int kBldDT = kBldThreads * kBldVec;  // 256 columns per CTA (TMA box inner extent)
+constexpr int kBldRC = 16;                    // rows per pipeline chunk
+constexpr int kBldStages = 4;                 // chunks in flight per CTA
+constexpr int kBldMaxTL = 2048;               // max output rows per CTA tile
+constexpr int kBldMaxWords = (kBldMaxTL + 2 * 2 * kMaxSteps + kBldRC + 31) / 32 + 1;
+
+struct BldArgs {
+  // streams (element pointers); columns are contiguous
+  const void* x;  // forward: input u_0.  backward: x for d(alpha) (nullable)
+  const void* g;  // backward: grad of the output (level S)
+  void* y;        // forward: output.  backward: grad of the input
+  int64_t xsB, xsL, gsB, gsL, ysB, ysL;  // element strides (batch, row)
+  int64_t L;      // rows of the addressed tensor (dense: rows per batch; varlen: packed rows)
+  int D;          // columns
+  int nbatch;     // dense: B.  varlen: number of sequences
+  // varlen segmentation (cu_seqlens on the device, int32, nbatch+1 entries)
+  const int32_t* cu_seqlens;
+  int pad_to_max;   // emulate zero padding up to max_len (reference packed-prefill rule)
+  int64_t max_len;
+  // global row position of local row 0 and the global sequence length
+  // (L-sharding: rows outside [0, L) come from the neighbour halos below)
+  int64_t pos_offset, global_len;
+  const void* lo_ext;  // [nbatch, hext_lo, D] rows just before local row 0 (nullable)
+  const void* hi_ext;  // [nbatch, hext_hi, D] rows just after local row L-1 (nullable)
+  int hext_lo, hext_hi;
+  // attention mask [B, L] (nullable): a row updates only if its 3 stencil rows are valid
+  const void* mask;
+  int mask_dtype;
+  int64_t msB, msL;
+  // tiling: output rows [out_begin, out_end) in tiles of TL rows
+  int TL;
+  int64_t out_begin, out_end;
+  int use_tma;
+  // per-step coefficients: host values, or device scalars when alpha_dev[k] != nullptr
+  float alpha[kMaxSteps];
+  const void* alpha_dev[kMaxSteps];
+  int alpha_dev_dtype;
+  // backward with d(alpha): per-CTA partial sums + completion counter (caller scratch)
+  float* dalpha_partial;   // [num_ctas * steps]
+  unsigned int* counter;   // zero on entry, left zero on exit
+  float* dalpha;           // [steps] fp32 result
+  int num_ctas;
+};
+
+// ---------------------------------------------------------------------------
+// [B, D, L] layout (sequence axis contiguous): warp windows with shuffles
+// ---------------------------------------------------------------------------
+constexpr int kBdlThreads = 256;  // 8 warps, each owns two 256-wide windows
+constexpr int kBdlElems = 8;      // positions per lane
+constexpr int kBdlOut = 240;      // output positions per window (30 lanes)
+
+struct BdlArgs {
+  const void* in;   // forward: x.  backward: grad_out
+  void* out;
+  int64_t rows;     // B * D
+  int64_t D;        // to map row -> batch for the mask
+  int64_t L;
+  int64_t in_rs, out_rs;  // row strides (elements)
+  int vec_ok;             // 16-byte vector access is legal for every row
+  const void* mask;
+  int mask_dtype;
+  int64_t msB, msL;
+  float alpha[kMaxSteps];
+  const void* alpha_dev[kMaxSteps];
+  int alpha_dev_dtype;
+};
+
+// launchers (return cudaError_t of the launch)
+cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, int dtype, int steps, int causal,
+                           dim3 grid, size_t smem, cudaStream_t st);
+cudaError_t launch_bld_bwd(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap, int dtype,
+                           int steps, int causal, int with_dalpha, dim3 grid, size_t smem, cudaStream_t st);
+cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st);
+
+size_t bld_smem_bytes(int dtype, int with_x_stream);
+int read_device_error_bld_fwd(int clear);
+int read_device_error_bld_bwd(int clear);
+int read_device_error_bdl(int clear);
+
+}  // namespace cta

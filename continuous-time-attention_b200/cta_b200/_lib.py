@@ -1,0 +1,144 @@
+"""ctypes binding of libcta_stencil.so (the C ABI in include/cta_stencil.h).
+
+Every entry point takes raw device pointers, sizes and element strides plus the
+caller's CUDA stream; this module turns torch tensors into those arguments and
+maps the library's status codes onto the exceptions the reference raises
+(``ValueError`` for invalid arguments, ``RuntimeError`` otherwise).
+
+There is no fallback: if the shared library is missing or fails to load, every
+operator raises ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import POINTER, c_float, c_int, c_int64, c_void_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().with_name("libcta_stencil.so")
+
+CTA_OK, CTA_EINVAL, CTA_EUNSUPPORTED, CTA_ECUDA = 0, 1, 2, 3
+SHARD_INTERIOR, SHARD_LO_EDGE, SHARD_HI_EDGE = 0, 1, 2
+MAX_STEPS = 8
+
+_DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+_MASK_CODES = {
+    torch.bool: 0,
+    torch.uint8: 0,
+    torch.int8: 0,
+    torch.int32: 1,
+    torch.int64: 2,
+    torch.float32: 3,
+    torch.bfloat16: 4,
+    torch.float16: 5,
+}
+
+# name -> (restype, argtypes); mirrors include/cta_stencil.h
+_SIGNATURES = {
+    "cta_abi_version": (c_int, []),
+    "cta_last_error": (ctypes.c_char_p, []),
+    "cta_device_error": (c_int, [c_int]),
+    "cta_set_tuning": (c_int, [c_int, c_int]),
+    "cta_diffusion_fwd_bdl": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_float,
+                                      c_void_p]),
+    "cta_diffusion_bwd_bdl": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_float,
+                                      c_void_p]),
+    "cta_diffusion_bdl_ex": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+                                     c_int, c_int, POINTER(c_float), POINTER(c_void_p), c_int, c_void_p, c_int,
+                                     c_int64, c_int64, c_void_p]),
+    "cta_diffusion_fwd_bld": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
+                                      c_int64, c_int, c_int, c_int, POINTER(c_float), POINTER(c_void_p), c_int,
+                                      c_void_p, c_int, c_int64, c_int64, c_void_p]),
+    "cta_diffusion_bwd_bld_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64, c_int, c_int, c_int]),
+    "cta_diffusion_bwd_bld": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                      c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+                                      c_int, POINTER(c_float), POINTER(c_void_p), c_int, c_void_p, c_int, c_int64,
+                                      c_int64, c_void_p]),
+    "cta_diffusion_fwd_varlen": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64,
+                                         c_int64, c_int, c_int, c_int, c_float, c_void_p]),
+    "cta_diffusion_shard_bld": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p,
+                                        c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_float,
+                                        c_void_p]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the shared library; raise if it is unavailable."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH.name} is not built (expected at {LIB_PATH}); run `python -m cta_b200.build`"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            if lib.cta_abi_version() != 1:
+                raise RuntimeError(f"{LIB_PATH.name}: unexpected ABI version {lib.cta_abi_version()}")
+            _lib = lib
+    return _lib
+
+
+def check(rc: int) -> None:
+    """Raise the reference's exception type for a non-zero status."""
+    if rc == CTA_OK:
+        return
+    msg = load().cta_last_error().decode(errors="replace")
+    if rc == CTA_EINVAL:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[dt]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dt}; expected float32, bfloat16 or float16") from None
+
+
+def mask_code(dt: torch.dtype) -> int:
+    try:
+        return _MASK_CODES[dt]
+    except KeyError:
+        raise ValueError(f"unsupported attention_mask dtype {dt}") from None
+
+
+def stream_ptr(t: torch.Tensor) -> c_void_p:
+    return c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def ptr(t: torch.Tensor | None) -> c_void_p:
+    return c_void_p(t.data_ptr() if t is not None else 0)
+
+
+def float_array(vals) -> ctypes.Array:
+    arr = (c_float * MAX_STEPS)()
+    for i, v in enumerate(vals):
+        arr[i] = float(v)
+    return arr
+
+
+def ptr_array(tensors) -> ctypes.Array:
+    arr = (c_void_p * MAX_STEPS)()
+    for i, t in enumerate(tensors):
+        arr[i] = t.data_ptr()
+    return arr
+
+
+def device_error(clear: bool = True) -> int:
+    """Device-side error word (0 = ok, 1 = a bounded in-kernel wait timed out)."""
+    return int(load().cta_device_error(1 if clear else 0))
+
+
+def set_tuning(key: int, value: int) -> int:
+    return int(load().cta_set_tuning(int(key), int(value)))

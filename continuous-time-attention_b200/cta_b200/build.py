@@ -1,0 +1,108 @@
+"""Build libcta_stencil.so (sm_100a) in-tree with nvcc.
+
+The shared library is the only native artefact of the package: the CUDA
+kernels (``csrc/*.cu``) and the C ABI declared in ``include/cta_stencil.h``.
+It links the CUDA runtime statically, so it has no dependency on the CUDA
+runtime that PyTorch ships; both share the device's primary context.
+
+Usage: ``python -m cta_b200.build [--force] [--verbose]``.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+SRC_ROOT = PKG_DIR.parent                     # continuous-time-attention_b200/
+CSRC = SRC_ROOT / "csrc"
+REPO_ROOT = SRC_ROOT.parent
+INCLUDE = REPO_ROOT / "include"
+BUILD_DIR = SRC_ROOT / "_build"
+LIB_NAME = "libcta_stencil.so"
+LIB_PATH = PKG_DIR / LIB_NAME
+
+SOURCES = ["capi.cu", "bld_fwd.cu", "bld_bwd.cu", "stencil_bdl.cu"]
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+CFLAGS = [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xcompiler",
+    "-fPIC",
+    "-Xcompiler",
+    "-Wall",
+]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found: set NVCC or put the CUDA toolkit on PATH")
+
+
+def _inputs() -> list[Path]:
+    files = [CSRC / s for s in SOURCES]
+    files += sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
+    return files
+
+
+def is_stale() -> bool:
+    if not LIB_PATH.exists():
+        return True
+    t = LIB_PATH.stat().st_mtime
+    return any(f.stat().st_mtime > t for f in _inputs())
+
+
+def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -> Path:
+    """Compile every kernel translation unit for sm_100a and link the library."""
+    if not force and not is_stale():
+        return LIB_PATH
+    nvcc = _nvcc()
+    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    incs = ["-I", str(INCLUDE), "-I", str(CSRC)]
+
+    def compile_one(name: str) -> Path:
+        obj = BUILD_DIR / (Path(name).stem + ".o")
+        cmd = [nvcc, *ARCH_FLAGS, *CFLAGS, *incs, "-c", str(CSRC / name), "-o", str(obj)]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+            print(" ".join(cmd), flush=True)
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed for {name}:\n{res.stdout}\n{res.stderr}")
+        if verbose and (res.stdout or res.stderr):
+            print(res.stdout + res.stderr, flush=True)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=jobs or min(len(SOURCES), os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(compile_one, SOURCES))
+
+    tmp = LIB_PATH.with_suffix(".so.tmp")
+    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs),
+           "-Xlinker", f"-soname={LIB_NAME}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    args = ap.parse_args(argv)
+    path = build(force=args.force, verbose=args.verbose)
+    print(path)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

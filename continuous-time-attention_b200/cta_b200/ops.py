@@ -1,0 +1,280 @@
+"""Functional wrappers over the C ABI: torch tensors in, torch tensors out.
+
+These are the single-launch building blocks used by the reference-compatible
+modules (``diffusion_triton``, ``pde_layers``, ``transformers``,
+``serving_vllm``, ``sharded``).  They validate shapes, allocate outputs with
+torch (the library itself never allocates) and enqueue one kernel on the
+current CUDA stream.  Callers handle the identity cases (``steps == 0``,
+sequence length < 3) with the reference's aliasing rules before calling here.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence, Union
+
+import torch
+
+from . import _lib
+
+AlphaLike = Union[float, torch.Tensor]
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be on CUDA")
+
+
+def _alpha_args(alphas: Sequence[AlphaLike], steps: int, device: torch.device):
+    """Host floats -> (float array, NULL); device scalars -> (NULL, pointer array)."""
+    if len(alphas) != steps:
+        raise ValueError(f"expected {steps} alpha values, got {len(alphas)}")
+    if all(not isinstance(a, torch.Tensor) for a in alphas):
+        return _lib.float_array(alphas), None, 0, []
+    tens = []
+    for a in alphas:
+        if not isinstance(a, torch.Tensor):
+            a = torch.tensor([float(a)], dtype=torch.float32, device=device)
+        if a.device != device:
+            raise ValueError(f"alpha on {a.device}, expected {device}")
+        if a.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+            a = a.float()
+        if a.numel() < 1:
+            raise ValueError("alpha tensor is empty")
+        a = a.detach()
+        if not a.is_contiguous():
+            a = a.contiguous()
+        tens.append(a)
+    code = _lib.dtype_code(tens[0].dtype)
+    if any(t.dtype != tens[0].dtype for t in tens):
+        tens = [t.float() for t in tens]
+        code = 0
+    return None, _lib.ptr_array(tens), code, tens  # keep tensors alive for the call
+
+
+def _mask_args(mask: Optional[torch.Tensor], B: int, L: int, device: torch.device):
+    if mask is None:
+        return None, 0, 0, 0
+    if mask.dim() != 2 or mask.shape[0] != B or mask.shape[1] != L:
+        raise ValueError(f"attention_mask must be ({B}, {L}), got {tuple(mask.shape)}")
+    if mask.device != device:
+        raise ValueError(f"attention_mask on {mask.device}, expected {device}")
+    if mask.dtype == torch.bool:
+        mask = mask.view(torch.uint8)
+    return mask, _lib.mask_code(mask.dtype), mask.stride(0), mask.stride(1)
+
+
+# ---------------------------------------------------------------------------
+# [B, D, L]
+# ---------------------------------------------------------------------------
+def bdl(
+    x: torch.Tensor,
+    alphas: Sequence[AlphaLike],
+    steps: int,
+    *,
+    causal: bool = False,
+    backward: bool = False,
+    mask: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """`steps` fused steps (or their adjoint) on a contiguous [B, D, L] tensor."""
+    _require_cuda(x, "x")
+    if x.dim() != 3:
+        raise ValueError("x must have shape (B, D, L)")
+    if x.stride(2) != 1 or x.stride(0) != x.shape[1] * x.stride(1):
+        x = x.contiguous()
+    B, D, L = x.shape
+    y = torch.empty_like(x, memory_format=torch.contiguous_format) if out is None else out
+    fa, pa, pcode, keep = _alpha_args(alphas, steps, x.device)
+    m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.cta_diffusion_bdl_ex(
+            _lib.ptr(x), _lib.ptr(y), B, D, L, x.stride(1), y.stride(1), _lib.dtype_code(x.dtype), steps,
+            int(causal), int(backward), fa, pa, pcode, _lib.ptr(m), mcode, msb, msl, _lib.stream_ptr(x),
+        )
+    del keep
+    _lib.check(rc)
+    return y
+
+
+def bdl_simple(x: torch.Tensor, alpha: float, steps: int, backward: bool = False) -> torch.Tensor:
+    """Reference kernel API path: one host alpha, no mask, non-causal."""
+    _require_cuda(x, "x")
+    if not x.is_contiguous():
+        x = x.contiguous()
+    B, D, L = x.shape
+    y = torch.empty_like(x)
+    lib = _lib.load()
+    fn = lib.cta_diffusion_bwd_bdl if backward else lib.cta_diffusion_fwd_bdl
+    with torch.cuda.device(x.device):
+        rc = fn(_lib.ptr(x), _lib.ptr(y), B, D, L, L, _lib.dtype_code(x.dtype), steps, float(alpha),
+                _lib.stream_ptr(x))
+    _lib.check(rc)
+    return y
+
+
+# ---------------------------------------------------------------------------
+# [B, L, D]
+# ---------------------------------------------------------------------------
+def _bld_view(x: torch.Tensor) -> torch.Tensor:
+    if x.stride(2) != 1:
+        x = x.contiguous()
+    return x
+
+
+def bld_forward(
+    x: torch.Tensor,
+    alphas: Sequence[AlphaLike],
+    steps: int,
+    *,
+    causal: bool = False,
+    mask: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """`steps` fused steps on [B, L, D] (feature axis contiguous), one launch."""
+    _require_cuda(x, "x")
+    if x.dim() != 3:
+        raise ValueError("x must have shape (B, L, D)")
+    x = _bld_view(x)
+    B, L, D = x.shape
+    y = torch.empty((B, L, D), dtype=x.dtype, device=x.device) if out is None else out
+    fa, pa, pcode, keep = _alpha_args(alphas, steps, x.device)
+    m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.cta_diffusion_fwd_bld(
+            _lib.ptr(x), _lib.ptr(y), B, L, D, x.stride(0), x.stride(1), y.stride(0), y.stride(1),
+            _lib.dtype_code(x.dtype), steps, int(causal), fa, pa, pcode, _lib.ptr(m), mcode, msb, msl,
+            _lib.stream_ptr(x),
+        )
+    del keep
+    _lib.check(rc)
+    return y
+
+
+_WS: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-initialised scratch for the d(alpha) reduction, one per (device, stream).
+
+    The kernel leaves its completion counter at zero, so the buffer stays
+    reusable without clearing between calls on the same stream.
+    """
+    key = (device, torch.cuda.current_stream(device).cuda_stream)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+def bld_backward(
+    grad_out: torch.Tensor,
+    alphas: Sequence[AlphaLike],
+    steps: int,
+    *,
+    x: Optional[torch.Tensor] = None,
+    causal: bool = False,
+    mask: Optional[torch.Tensor] = None,
+    need_dalpha: bool = False,
+):
+    """grad_in = A_1^T .. A_S^T grad_out; with need_dalpha also d(alpha_k) (fp32 [steps])."""
+    _require_cuda(grad_out, "grad_out")
+    g = _bld_view(grad_out)
+    B, L, D = g.shape
+    dx = torch.empty((B, L, D), dtype=g.dtype, device=g.device)
+    fa, pa, pcode, keep = _alpha_args(alphas, steps, g.device)
+    m, mcode, msb, msl = _mask_args(mask, B, L, g.device)
+    lib = _lib.load()
+    dalpha = None
+    ws = None
+    ws_bytes = 0
+    xs = None
+    if need_dalpha:
+        if x is None:
+            raise ValueError("need_dalpha requires the forward input x")
+        xs = _bld_view(x)
+        if xs.dtype != g.dtype or tuple(xs.shape) != (B, L, D):
+            raise ValueError("x must match grad_out in shape and dtype")
+        dalpha = torch.empty(steps, dtype=torch.float32, device=g.device)
+        ws_bytes = int(lib.cta_diffusion_bwd_bld_workspace_bytes(B, L, D, _lib.dtype_code(g.dtype), steps,
+                                                                 int(causal)))
+        ws = _workspace(g.device, ws_bytes)
+    with torch.cuda.device(g.device):
+        rc = lib.cta_diffusion_bwd_bld(
+            _lib.ptr(g), _lib.ptr(dx), _lib.ptr(xs), _lib.ptr(dalpha), _lib.ptr(ws), ws_bytes, B, L, D,
+            g.stride(0), g.stride(1), xs.stride(0) if xs is not None else 0, xs.stride(1) if xs is not None else 0,
+            dx.stride(0), dx.stride(1), _lib.dtype_code(g.dtype), steps, int(causal), fa, pa, pcode, _lib.ptr(m),
+            mcode, msb, msl, _lib.stream_ptr(g),
+        )
+    del keep
+    _lib.check(rc)
+    return dx, dalpha
+
+
+def varlen_forward(
+    x: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    max_len: int,
+    alpha: float,
+    steps: int,
+    *,
+    pad_to_max: bool,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Packed [T, D] prefill with device cu_seqlens (int32, nseq+1); one launch."""
+    _require_cuda(x, "x")
+    if x.dim() != 2:
+        raise ValueError("x must have shape (T, D)")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if cu_seqlens.device != x.device:
+        raise ValueError("cu_seqlens must be on the same device as x")
+    if cu_seqlens.dtype != torch.int32:
+        cu_seqlens = cu_seqlens.to(torch.int32)
+    if not cu_seqlens.is_contiguous():
+        cu_seqlens = cu_seqlens.contiguous()
+    T, D = x.shape
+    y = torch.empty((T, D), dtype=x.dtype, device=x.device) if out is None else out
+    nseq = cu_seqlens.numel() - 1
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        rc = lib.cta_diffusion_fwd_varlen(
+            _lib.ptr(x), _lib.ptr(y), T, D, x.stride(0), y.stride(0), _lib.ptr(cu_seqlens), nseq, int(max_len),
+            int(pad_to_max), _lib.dtype_code(x.dtype), steps, float(alpha), _lib.stream_ptr(x),
+        )
+    _lib.check(rc)
+    return y
+
+
+def shard_part(
+    x_local: torch.Tensor,
+    out: torch.Tensor,
+    part: int,
+    *,
+    pos_offset: int,
+    global_len: int,
+    alpha: float,
+    steps: int,
+    causal: bool = False,
+    backward: bool = False,
+    lo_halo: Optional[torch.Tensor] = None,
+    hi_halo: Optional[torch.Tensor] = None,
+    stream: Optional[torch.cuda.Stream] = None,
+) -> None:
+    """One launch over a part (interior / lo edge / hi edge) of an L-shard."""
+    B, Lloc, D = x_local.shape
+    for h in (lo_halo, hi_halo):
+        if h is not None and (not h.is_contiguous() or h.shape[0] != B or h.shape[2] != D or h.dtype != x_local.dtype):
+            raise ValueError("halo must be a contiguous (B, rows, D) tensor of the shard's dtype")
+    lo_rows = lo_halo.shape[1] if lo_halo is not None else 0
+    hi_rows = hi_halo.shape[1] if hi_halo is not None else 0
+    st = stream if stream is not None else torch.cuda.current_stream(x_local.device)
+    lib = _lib.load()
+    with torch.cuda.device(x_local.device):
+        rc = lib.cta_diffusion_shard_bld(
+            _lib.ptr(x_local), _lib.ptr(out), B, Lloc, D, int(pos_offset), int(global_len), _lib.ptr(lo_halo),
+            lo_rows, _lib.ptr(hi_halo), hi_rows, int(part), _lib.dtype_code(x_local.dtype), steps, int(causal),
+            int(backward), float(alpha), _lib.c_void_p(st.cuda_stream),
+        )
+    _lib.check(rc)

@@ -1,0 +1,222 @@
+"""PDE refinement layers backed by the fused sm_100a stencil kernels.
+
+Drop-in for the diffusion family of the reference's src/models/pde_layers.py:
+
+* ``DiffusionPDELayer(hidden_size, alpha_init=0.10, layout="bdl", causal=False)``
+  -- one refinement step, ``forward(x, attention_mask=None)``; same parameter
+  (``alpha``, shape [1]), same layouts, causal stencil and mask rule
+  (pde_layers.py:39-64,113-188,195-219), one kernel launch forward and one
+  backward (which also returns d(alpha)).
+* ``WavePDELayer`` -- the reference's wave layer updates by alpha**2 * lap
+  (pde_layers.py:244-246), i.e. a diffusion step with coefficient alpha**2.
+* ``create_pde_layer`` -- the reference factory (pde_layers.py:325-357).
+* ``diffusion_pde_stack(x, layers, attention_mask)`` -- runs a list of
+  consecutive layers (each with its own alpha) as ONE fused launch, keeping
+  fp32 between the layers; the reference applies the layers one by one and
+  rounds to the input dtype after each (identical in fp32; within 2e-2 in
+  bf16).
+
+Arithmetic follows the reference op by op (fp32, no fused multiply-add), so a
+single fp32 or bf16 layer step is bit-identical to the reference layer.
+The reaction-diffusion and advection-diffusion layers have different update
+rules and are not served by these kernels.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+import torch.nn as nn
+
+from . import _lib, ops
+
+__all__ = [
+    "DiffusionPDELayer",
+    "WavePDELayer",
+    "create_pde_layer",
+    "diffusion_pde_stack",
+    "diffusion_stack_function",
+]
+
+
+class _StackBLD(torch.autograd.Function):
+    """Fused forward/backward of `len(alphas)` layers on [B, L, D]."""
+
+    @staticmethod
+    def forward(ctx, x, mask, causal, *alphas):
+        steps = len(alphas)
+        y = ops.bld_forward(x, list(alphas), steps, causal=causal, mask=mask)
+        ctx.causal = causal
+        ctx.steps = steps
+        ctx.save_for_backward(x, mask, *alphas)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        x, mask, *alphas = ctx.saved_tensors
+        need_da = any(ctx.needs_input_grad[3:])
+        dx, da = ops.bld_backward(g, alphas, ctx.steps, x=x, causal=ctx.causal, mask=mask, need_dalpha=need_da)
+        dalphas = []
+        for k, a in enumerate(alphas):
+            if ctx.needs_input_grad[3 + k]:
+                dalphas.append(da[k : k + 1].reshape(a.shape).to(a.dtype))
+            else:
+                dalphas.append(None)
+        return (dx if ctx.needs_input_grad[0] else None), None, None, *dalphas
+
+
+class _StackBDL(torch.autograd.Function):
+    """Fused forward/backward of `len(alphas)` layers on [B, D, L].
+
+    The backward uses the [B, D, L] adjoint kernel; when d(alpha) is needed the
+    gradient and input are viewed in [B, L, D] order and sent through the
+    [B, L, D] adjoint kernel, which carries the d(alpha) reduction.
+    """
+
+    @staticmethod
+    def forward(ctx, x, mask, causal, *alphas):
+        steps = len(alphas)
+        y = ops.bdl(x, list(alphas), steps, causal=causal, mask=mask)
+        ctx.causal = causal
+        ctx.steps = steps
+        ctx.save_for_backward(x, mask, *alphas)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        x, mask, *alphas = ctx.saved_tensors
+        need_da = any(ctx.needs_input_grad[3:])
+        if need_da:
+            dx_bld, da = ops.bld_backward(
+                g.transpose(1, 2).contiguous(), alphas, ctx.steps, x=x.transpose(1, 2).contiguous(),
+                causal=ctx.causal, mask=mask, need_dalpha=True,
+            )
+            dx = dx_bld.transpose(1, 2).contiguous()
+        else:
+            dx = ops.bdl(g, alphas, ctx.steps, causal=ctx.causal, mask=mask, backward=True)
+            da = None
+        dalphas = []
+        for k, a in enumerate(alphas):
+            if ctx.needs_input_grad[3 + k]:
+                dalphas.append(da[k : k + 1].reshape(a.shape).to(a.dtype))
+            else:
+                dalphas.append(None)
+        return (dx if ctx.needs_input_grad[0] else None), None, None, *dalphas
+
+
+def diffusion_stack_function(
+    x: torch.Tensor,
+    alphas: Sequence[torch.Tensor],
+    *,
+    layout: str = "bld",
+    causal: bool = False,
+    attention_mask: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Apply len(alphas) diffusion steps (alpha_k a device scalar each) fused.
+
+    Groups of up to 8 steps run per launch; fp32 is kept within a group.
+    """
+    if layout not in {"bdl", "bld"}:
+        raise ValueError("layout must be 'bdl' or 'bld'")
+    seq_dim = 2 if layout == "bdl" else 1
+    if x.dim() != 3:
+        raise ValueError(f"expected a 3-D input, got {x.dim()}-D")
+    if x.size(seq_dim) < 3 or len(alphas) == 0:
+        return x
+    if x.device.type != "cuda":
+        raise ValueError("x must be on CUDA (the stencil runs only on the sm_100a kernels)")
+    fn = _StackBDL if layout == "bdl" else _StackBLD
+    mask = attention_mask
+    if mask is not None and mask.device != x.device:
+        mask = mask.to(x.device)
+    y = x
+    for i in range(0, len(alphas), _lib.MAX_STEPS):
+        y = fn.apply(y, mask, bool(causal), *alphas[i : i + _lib.MAX_STEPS])
+    return y
+
+
+class _DiffusionFamilyLayer(nn.Module):
+    """Shared layout/causal handling (src/models/pde_layers.py:71-88)."""
+
+    def __init__(self, hidden_size: int, layout: str = "bdl", causal: bool = False):
+        super().__init__()
+        if layout not in {"bdl", "bld"}:
+            raise ValueError("layout must be 'bdl' or 'bld'")
+        self.layout = layout
+        self.causal = causal
+
+    def effective_alpha(self) -> torch.Tensor:
+        """The coefficient multiplying the Laplacian, as an fp32 [1] tensor."""
+        raise NotImplementedError
+
+    def forward(self, x: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One refinement step (src/models/pde_layers.py:113-188)."""
+        return diffusion_stack_function(
+            x, [self.effective_alpha()], layout=self.layout, causal=self.causal, attention_mask=attention_mask
+        )
+
+
+class DiffusionPDELayer(_DiffusionFamilyLayer):
+    """Diffusion PDE ``du/dt = alpha * d2u/dx2`` (src/models/pde_layers.py:195-219)."""
+
+    def __init__(self, hidden_size: int, alpha_init: float = 0.10, layout: str = "bdl", causal: bool = False):
+        super().__init__(hidden_size, layout=layout, causal=causal)
+        self.alpha = nn.Parameter(torch.tensor([alpha_init]))
+
+    def effective_alpha(self) -> torch.Tensor:
+        # pde_layers.py:219 multiplies by alpha.to(float32); the kernel reads
+        # the parameter as stored and widens it to fp32 the same way
+        return self.alpha
+
+
+class WavePDELayer(_DiffusionFamilyLayer):
+    """Wave PDE, reference update ``alpha**2 * lap`` (src/models/pde_layers.py:222-246)."""
+
+    def __init__(self, hidden_size: int, alpha_init: float = 0.15, layout: str = "bdl", causal: bool = False):
+        super().__init__(hidden_size, layout=layout, causal=causal)
+        self.alpha = nn.Parameter(torch.tensor([alpha_init]))
+
+    def effective_alpha(self) -> torch.Tensor:
+        return self.alpha.to(dtype=torch.float32) ** 2
+
+
+_PDE_REGISTRY = {
+    "diffusion": DiffusionPDELayer,
+    "wave": WavePDELayer,
+}
+_NOT_SERVED = ("reaction-diffusion", "advection-diffusion")
+
+
+def create_pde_layer(pde_type: str, hidden_size: int, causal: bool = False, **kwargs) -> nn.Module:
+    """Factory with the reference's signature (src/models/pde_layers.py:333-357)."""
+    if pde_type in _NOT_SERVED:
+        raise NotImplementedError(f"PDE type {pde_type!r} has no fused kernel in this build")
+    if pde_type not in _PDE_REGISTRY:
+        raise ValueError(
+            f"Unknown PDE type: {pde_type}. Available types: {list(_PDE_REGISTRY.keys()) + list(_NOT_SERVED)}"
+        )
+    kwargs["causal"] = causal
+    return _PDE_REGISTRY[pde_type](hidden_size, **kwargs)
+
+
+def diffusion_pde_stack(
+    x: torch.Tensor, layers: Sequence[nn.Module], attention_mask: Optional[torch.Tensor] = None
+) -> torch.Tensor:
+    """Run consecutive diffusion-family layers as one fused launch.
+
+    Equivalent to ``for l in layers: x = l(x, attention_mask=attention_mask)``
+    except that fp32 is kept between the layers.  All layers must share layout
+    and causality.
+    """
+    layers = list(layers)
+    if not layers:
+        return x
+    layout, causal = layers[0].layout, layers[0].causal
+    for l in layers:
+        if not isinstance(l, _DiffusionFamilyLayer):
+            raise TypeError(f"{type(l).__name__} is not a diffusion-family layer")
+        if l.layout != layout or l.causal != causal:
+            raise ValueError("all layers of a fused stack must share layout and causality")
+    return diffusion_stack_function(
+        x, [l.effective_alpha() for l in layers], layout=layout, causal=causal, attention_mask=attention_mask
+    )

@@ -1,0 +1,219 @@
+"""CTA post-attention mixer for vLLM, served by the fused sm_100a kernels.
+
+Drop-in for src/cta/serving_vllm.py of the reference: ``CtaConfig`` (same
+fields, plus ``varlen_mode`` and ``fuse_any_steps``) and
+``CtaPostAttnMixer(config).forward(x, *, attn_metadata=None, is_prefill=None)``
+with the same gating (prefill inference :49-61, step policies :177-189).
+
+What changes:
+  * [B, L, D] inputs run the [B, L, D] kernel directly -- no BLD<->BDL
+    transposes or staging buffers (:234-266);
+  * packed 2-D inputs ([T, H] + ``query_start_loc``) run ONE varlen launch that
+    reads the offsets on the device: no host sync, no pad / unpack copies and no
+    Python loop over requests (:72-111, :275-303).  ``varlen_mode="reference"``
+    (default) reproduces the reference's zero-padding-to-``max_query_len`` rule
+    exactly; ``"sequence"`` gives every sequence its own copy boundary;
+  * every step count 1..8 is fused (the reference fuses only {1, 2, 4, 8} and
+    loops single steps, rounding each, otherwise); ``fuse_any_steps=False``
+    restores the reference's per-step rounding for the other counts.
+The kernels are the only compute path: ``use_triton`` is kept for config
+compatibility and a CPU tensor raises ``ValueError``.
+"""
+from __future__ import annotations
+
+import math
+from contextlib import nullcontext
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import _lib, ops
+from .diffusion import diffusion_triton
+
+try:
+    from torch.profiler import record_function
+except Exception:  # noqa: BLE001
+
+    def record_function(_name: str):  # type: ignore
+        return nullcontext()
+
+
+__all__ = ["CtaConfig", "CtaPostAttnMixer"]
+
+
+def _infer_prefill(attn_metadata: Optional[object]) -> bool:
+    """src/cta/serving_vllm.py:49-61."""
+    if attn_metadata is None:
+        return True
+    for attr in ("is_prefill", "prefill"):
+        val = getattr(attn_metadata, attr, None)
+        if isinstance(val, bool):
+            return val
+    num_prefill = getattr(attn_metadata, "num_prefill_tokens", None)
+    if isinstance(num_prefill, int):
+        return num_prefill > 0
+    if getattr(attn_metadata, "prefill_metadata", None) is not None:
+        return True
+    return True
+
+
+def _to_int(value: object) -> Optional[int]:
+    """src/cta/serving_vllm.py:64-69."""
+    if isinstance(value, int):
+        return value
+    if isinstance(value, torch.Tensor) and value.numel() == 1:
+        return int(value.item())
+    return None
+
+
+@dataclass
+class CtaConfig:
+    """src/cta/serving_vllm.py:135-150, plus two fields of this build."""
+
+    enabled: bool = True
+    prefill_only: bool = True
+    steps: int = 4
+    alpha: float = 0.10
+    layout: str = "bld"
+    use_triton: bool = True
+    fused: bool = True
+    allow_transpose: bool = True
+    min_seq_len: int = 0
+    steps_policy: str = "fixed"
+    steps_scale: int = 2048
+    max_steps: int = 8
+    use_buffer_pool: bool = False
+    trace: bool = True
+    # packed prefill rule: "reference" = zero padding to max_query_len, "sequence" = per-sequence boundary
+    varlen_mode: str = "reference"
+    # fuse step counts outside {1, 2, 4, 8} too (fp32 between steps)
+    fuse_any_steps: bool = True
+
+
+class CtaPostAttnMixer(nn.Module):
+    """Apply CTA diffusion after the attention output (prefill-only by default)."""
+
+    def __init__(self, config: CtaConfig):
+        super().__init__()
+        if config.layout not in {"bld", "bdl"}:
+            raise ValueError("layout must be 'bld' or 'bdl'")
+        if config.varlen_mode not in {"reference", "sequence"}:
+            raise ValueError("varlen_mode must be 'reference' or 'sequence'")
+        self.config = config
+        self._qsl_cache: dict = {}
+
+    def _resolve_steps(self, seq_len: int) -> int:
+        """src/cta/serving_vllm.py:177-189."""
+        if seq_len < self.config.min_seq_len:
+            return 0
+        policy = self.config.steps_policy
+        if policy == "fixed":
+            steps = self.config.steps
+        elif policy == "linear":
+            steps = max(1, seq_len // max(1, self.config.steps_scale))
+        elif policy == "log2":
+            steps = max(1, int(math.log2(max(2, seq_len))))
+        else:
+            steps = self.config.steps
+        return min(self.config.max_steps, int(steps))
+
+    def _fused_ok(self, steps: int) -> bool:
+        if not self.config.fused:
+            return False
+        if steps in (1, 2, 4, 8):
+            return True
+        return self.config.fuse_any_steps and 1 <= steps <= _lib.MAX_STEPS
+
+    def forward(  # type: ignore[override]
+        self,
+        x: torch.Tensor,
+        *,
+        attn_metadata: Optional[object] = None,
+        is_prefill: Optional[bool] = None,
+    ) -> torch.Tensor:
+        if x.ndim == 2:
+            return self._forward_packed(x, attn_metadata=attn_metadata, is_prefill=is_prefill)
+        if not self.config.enabled:
+            return x
+        if self.config.prefill_only:
+            if is_prefill is None:
+                is_prefill = _infer_prefill(attn_metadata)
+            if not is_prefill:
+                return x
+        seq_dim = 2 if self.config.layout == "bdl" else 1
+        steps = self._resolve_steps(x.size(seq_dim))
+        if steps <= 0:
+            return x
+        if x.device.type != "cuda":
+            raise ValueError("x must be on CUDA")
+        if x.ndim != 3:
+            raise ValueError(f"expected x.ndim == 3, got {x.ndim}")
+        if x.size(seq_dim) < 3:
+            return x
+        ctx = record_function("cta_post_attn_mixer") if self.config.trace else nullcontext()
+        alpha = float(self.config.alpha)
+        with ctx:
+            if self._fused_ok(steps):
+                out = x
+                for i in range(0, steps, _lib.MAX_STEPS):
+                    s = min(_lib.MAX_STEPS, steps - i)
+                    if self.config.layout == "bdl":
+                        out = ops.bdl_simple(out, alpha, s)
+                    else:
+                        out = ops.bld_forward(out, [alpha] * s, s)
+                return out
+            # reference's non-fused path: one step at a time, rounded each step
+            if self.config.layout == "bdl":
+                return diffusion_triton(x, alpha=alpha, steps=steps)
+            out = x
+            for _ in range(steps):
+                out = ops.bld_forward(out, [alpha], 1)
+            return out
+
+    def _device_qsl(self, qsl: object, device: torch.device) -> torch.Tensor:
+        if isinstance(qsl, torch.Tensor):
+            if qsl.device == device and qsl.dtype == torch.int32:
+                return qsl
+            return qsl.to(device=device, dtype=torch.int32, non_blocking=True)
+        return torch.tensor(list(qsl), dtype=torch.int32).to(device, non_blocking=True)
+
+    def _forward_packed(
+        self,
+        x: torch.Tensor,
+        *,
+        attn_metadata: Optional[object],
+        is_prefill: Optional[bool],
+    ) -> torch.Tensor:
+        """Packed [T, H] prefill (src/cta/serving_vllm.py:275-303), one launch."""
+        if not self.config.enabled:
+            return x
+        if attn_metadata is None:
+            return x
+        if self.config.prefill_only:
+            if is_prefill is None:
+                is_prefill = _infer_prefill(attn_metadata)
+            if not is_prefill:
+                return x
+        max_query_len = _to_int(getattr(attn_metadata, "max_query_len", None))
+        query_start_loc = getattr(attn_metadata, "query_start_loc", None)
+        if max_query_len is None or query_start_loc is None:
+            return x
+        if max_query_len < 3:
+            return x
+        steps = self._resolve_steps(max_query_len)
+        if steps <= 0:
+            return x
+        if x.device.type != "cuda":
+            raise ValueError("x must be on CUDA")
+        cu = self._device_qsl(query_start_loc, x.device)
+        pad = self.config.varlen_mode == "reference"
+        alpha = float(self.config.alpha)
+        ctx = record_function("cta_post_attn_mixer") if self.config.trace else nullcontext()
+        with ctx:
+            out = x
+            for i in range(0, steps, _lib.MAX_STEPS):
+                s = min(_lib.MAX_STEPS, steps - i)
+                out = ops.varlen_forward(out, cu, max_query_len, alpha, s, pad_to_max=pad)
+            return out

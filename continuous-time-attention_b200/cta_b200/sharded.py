@@ -1,0 +1,143 @@
+"""L-sharded diffusion stencil for sequences too long for one GPU.
+
+The sequence axis of a [B, L, D] tensor is split into contiguous shards, one
+per rank.  A fused forward (or adjoint) over `steps` steps needs, for every
+output row, the input rows within `steps` of it (2*steps on one side for the
+causal stencil and its adjoint), so each call:
+
+  1. posts the halo exchange -- the rows a neighbour needs are sent with NCCL
+     point-to-point (``batch_isend_irecv``) from a side stream;
+  2. meanwhile runs the interior kernel, which computes every output row whose
+     stencil stays inside the local shard;
+  3. waits for the halos and runs the two small edge kernels, which read the
+     received rows.
+
+Only the two global ends of the sequence use the copy boundary; shard edges
+are interior rows.  The reference has no multi-device path (it runs the
+stencil on one device); results are identical to the unsharded stencil.
+
+The compute step is injectable (``compute=``) so that the exchange protocol can
+be exercised on CPU ranks (gloo) in the tests; the default is the sm_100a
+kernels through :func:`cta_b200.ops.shard_part`.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+__all__ = ["ShardSpec", "halo_rows", "sharded_diffusion", "even_shards"]
+
+
+@dataclass(frozen=True)
+class ShardSpec:
+    rank: int
+    world: int
+    pos_offset: int   # global row of local row 0
+    local_len: int
+    global_len: int
+
+
+def even_shards(global_len: int, world: int, rank: int) -> ShardSpec:
+    """Contiguous split, the first (global_len % world) shards one row longer."""
+    base, rem = divmod(global_len, world)
+    lens = [base + (1 if r < rem else 0) for r in range(world)]
+    return ShardSpec(rank, world, sum(lens[:rank]), lens[rank], global_len)
+
+
+def halo_rows(steps: int, causal: bool, backward: bool) -> tuple[int, int]:
+    """(rows needed from the previous shard, rows needed from the next shard)."""
+    if causal:
+        return (0, 2 * steps) if backward else (2 * steps, 0)
+    return steps, steps
+
+
+def _default_compute(part, x_local, out, *, lo_halo, hi_halo, spec, alpha, steps, causal, backward):
+    from . import ops
+
+    ops.shard_part(x_local, out, part, pos_offset=spec.pos_offset, global_len=spec.global_len, alpha=alpha,
+                   steps=steps, causal=causal, backward=backward, lo_halo=lo_halo, hi_halo=hi_halo)
+
+
+def sharded_diffusion(
+    x_local: torch.Tensor,
+    spec: ShardSpec,
+    *,
+    alpha: float,
+    steps: int,
+    causal: bool = False,
+    backward: bool = False,
+    group: Optional[dist.ProcessGroup] = None,
+    comm_stream: Optional[torch.cuda.Stream] = None,
+    compute: Optional[Callable] = None,
+) -> torch.Tensor:
+    """Fused `steps`-step stencil (or its adjoint) of this rank's shard.
+
+    Every rank must call this with the same steps / causal / backward; ranks
+    exchange halos with their neighbours only.  Returns the local output shard.
+    """
+    if x_local.dim() != 3:
+        raise ValueError("x_local must be (B, L_local, D)")
+    if not 1 <= steps <= _lib.MAX_STEPS:
+        raise ValueError(f"steps must be in 1..{_lib.MAX_STEPS}, got {steps}")
+    B, Lloc, D = x_local.shape
+    if Lloc != spec.local_len:
+        raise ValueError(f"x_local has {Lloc} rows, spec says {spec.local_len}")
+    hl, hr = halo_rows(steps, causal, backward)
+    prev_rank = spec.rank - 1 if spec.rank > 0 else None
+    next_rank = spec.rank + 1 if spec.rank + 1 < spec.world else None
+    # a neighbour's request must be servable from one shard
+    if (prev_rank is not None and hr and Lloc < hr) or (next_rank is not None and hl and Lloc < hl):
+        raise ValueError("shard shorter than the halo it must provide")
+    if compute is None:
+        compute = _default_compute
+    x_local = x_local.contiguous()
+    out = torch.empty_like(x_local)
+    if spec.global_len < 3:
+        out.copy_(x_local)
+        return out
+    on_gpu = x_local.device.type == "cuda"
+    cur = torch.cuda.current_stream(x_local.device) if on_gpu else None
+
+    lo_halo = torch.empty((B, hl, D), dtype=x_local.dtype, device=x_local.device) if (prev_rank is not None and hl) else None
+    hi_halo = torch.empty((B, hr, D), dtype=x_local.dtype, device=x_local.device) if (next_rank is not None and hr) else None
+
+    def post_exchange():
+        ops = []
+        # my first hr rows are the next-shard halo of the previous rank; my last hl rows the lo halo of the next
+        if prev_rank is not None and hr:
+            ops.append(dist.P2POp(dist.isend, x_local[:, :hr].contiguous(), prev_rank, group))
+        if next_rank is not None and hl:
+            ops.append(dist.P2POp(dist.isend, x_local[:, Lloc - hl :].contiguous(), next_rank, group))
+        if lo_halo is not None:
+            ops.append(dist.P2POp(dist.irecv, lo_halo, prev_rank, group))
+        if hi_halo is not None:
+            ops.append(dist.P2POp(dist.irecv, hi_halo, next_rank, group))
+        return dist.batch_isend_irecv(ops) if ops else []
+
+    kw = dict(spec=spec, alpha=alpha, steps=steps, causal=causal, backward=backward)
+    if on_gpu:
+        comm = comm_stream if comm_stream is not None else torch.cuda.Stream(device=x_local.device)
+        comm.wait_stream(cur)
+        with torch.cuda.stream(comm):
+            works = post_exchange()
+            for w in works:
+                w.wait()
+        # interior rows need no halo: overlap them with the exchange
+        compute(_lib.SHARD_INTERIOR, x_local, out, lo_halo=None, hi_halo=None, **kw)
+        cur.wait_stream(comm)
+        for h in (lo_halo, hi_halo):
+            if h is not None:
+                h.record_stream(cur)
+    else:
+        works = post_exchange()
+        compute(_lib.SHARD_INTERIOR, x_local, out, lo_halo=None, hi_halo=None, **kw)
+        for w in works:
+            w.wait()
+    compute(_lib.SHARD_LO_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
+    compute(_lib.SHARD_HI_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
+    return out

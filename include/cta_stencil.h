@@ -1,0 +1,153 @@
+/*
+ * cta_stencil.h -- C ABI of the B200 (sm_100a) diffusion-stencil library
+ * (libcta_stencil.so).
+ *
+ * The library computes the multi-step diffusion refinement of Continuous-Time
+ * Attention,
+ *     x[i] <- x[i] + alpha * ((x[i+1] - 2 x[i]) + x[i-1])      (fp32 math)
+ * applied `steps` times along the sequence axis with the copy boundary (first
+ * and last row unchanged), its causal variant, attention-mask handling, packed
+ * variable-length sequences, and the adjoint (backward) with d(alpha).
+ *
+ * Conventions
+ *   - All tensors are device pointers owned by the caller; the library never
+ *     allocates device memory.  Strides are in ELEMENTS.
+ *   - dtype: CTA_F32 / CTA_BF16 / CTA_F16; the output dtype equals the input
+ *     dtype, arithmetic is fp32, results are rounded once at the end.
+ *   - Work is enqueued on `stream` (a cudaStream_t, NULL = legacy default);
+ *     no call synchronizes or reads device data on the host.
+ *   - Return value: CTA_OK, or an error code with a message available from
+ *     cta_last_error() (thread-local).  CTA_EINVAL corresponds to the
+ *     reference's ValueError, the others to RuntimeError.
+ *   - steps: 1..8 (every count has its own fused kernel).  Calls with
+ *     steps == 0 or a sequence shorter than 3 rows are the identity and are
+ *     handled by the caller (the Python layer mirrors the reference's
+ *     aliasing rules for them).
+ */
+#ifndef CTA_STENCIL_H_
+#define CTA_STENCIL_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CTA_ABI_VERSION 1
+
+enum { CTA_F32 = 0, CTA_BF16 = 1, CTA_F16 = 2 };
+enum { CTA_MASK_U8 = 0, CTA_MASK_I32 = 1, CTA_MASK_I64 = 2, CTA_MASK_F32 = 3, CTA_MASK_BF16 = 4, CTA_MASK_F16 = 5 };
+enum { CTA_OK = 0, CTA_EINVAL = 1, CTA_EUNSUPPORTED = 2, CTA_ECUDA = 3 };
+enum { CTA_SHARD_INTERIOR = 0, CTA_SHARD_LO_EDGE = 1, CTA_SHARD_HI_EDGE = 2 };
+
+/* ABI version of the loaded library (CTA_ABI_VERSION). */
+int cta_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* cta_last_error(void);
+
+/* Reads (and optionally clears) the device-side error word of every kernel
+ * family: 0 = ok, 1 = a bounded wait inside a kernel timed out.  This call
+ * synchronizes with the device. */
+int cta_device_error(int clear);
+
+/* Benchmark tuning hook: key 0 = target CTAs per SM used to size [B, L, D]
+ * tiles (default 6), key 1 = forced tile rows (0 = automatic).  Returns the
+ * previous value.  Process-wide, not thread-safe against concurrent launches. */
+int cta_set_tuning(int key, int value);
+
+/* ---------------------------------------------------------------------------
+ * [B, D, L] layout, L contiguous
+ * ------------------------------------------------------------------------- */
+
+/* y = A^steps x.  Replaces kernels/diffusion_triton.py:829-868
+ * (_diffusion_fused_triton_forward, steps in {1,2,4,8} there, 1..8 here)
+ * and :732-762 (_diffusion_step_triton_forward, steps = 1).
+ * x, y: [B, D, L] with row stride `row_stride` (>= L) for both. */
+int cta_diffusion_fwd_bdl(const void* x, void* y, int64_t B, int64_t D, int64_t L, int64_t row_stride, int dtype,
+                          int steps, float alpha, void* stream);
+
+/* grad_in = (A^T)^steps grad_out.  Replaces kernels/diffusion_triton.py:765-794
+ * (diffusion_step_triton_backward, steps = 1) and the host loop of
+ * _DiffusionFusedTriton.backward :880-888 (fused into one launch here). */
+int cta_diffusion_bwd_bdl(const void* grad_out, void* grad_in, int64_t B, int64_t D, int64_t L, int64_t row_stride,
+                          int dtype, int steps, float alpha, void* stream);
+
+/* General [B, D, L] form used by the `layout="bdl"` PDE layers
+ * (src/models/pde_layers.py:113-188): causal stencil, attention mask
+ * ([B, L], any listed dtype, non-zero = valid, strides mask_sB/mask_sL),
+ * one alpha per step given either as host floats (`alpha`, steps entries) or
+ * as device scalars (`alpha_dev[k]`, dtype alpha_dev_dtype; entry k used when
+ * non-NULL).  backward != 0 applies the adjoint instead. */
+int cta_diffusion_bdl_ex(const void* in, void* out, int64_t B, int64_t D, int64_t L, int64_t in_row_stride,
+                         int64_t out_row_stride, int dtype, int steps, int causal, int backward, const float* alpha,
+                         const void* const* alpha_dev, int alpha_dev_dtype, const void* mask, int mask_dtype,
+                         int64_t mask_sB, int64_t mask_sL, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * [B, L, D] layout, D contiguous (TMA-fed kernels)
+ * ------------------------------------------------------------------------- */
+
+/* Fused forward over `steps` steps.  Replaces, with one launch per call:
+ *   - src/cta/serving_vllm.py:29-46 (_diffusion_steps_bld) and the
+ *     transpose + Triton + transpose path of CtaPostAttnMixer.forward :234-266;
+ *   - a chain of `steps` DiffusionPDELayer(layout="bld") calls,
+ *     src/models/pde_layers.py:113-188 with :218-219 (causal, mask, per-layer
+ *     alpha), keeping fp32 between the steps. */
+int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t D, int64_t x_sB, int64_t x_sL,
+                          int64_t y_sB, int64_t y_sL, int dtype, int steps, int causal, const float* alpha,
+                          const void* const* alpha_dev, int alpha_dev_dtype, const void* mask, int mask_dtype,
+                          int64_t mask_sB, int64_t mask_sL, void* stream);
+
+/* Bytes of caller scratch needed by cta_diffusion_bwd_bld when dalpha != NULL
+ * (per-CTA partial sums and a completion counter).  The scratch must be
+ * zero-filled before its first use; the kernel leaves it reusable. */
+int64_t cta_diffusion_bwd_bld_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype, int steps, int causal);
+
+/* Fused backward: grad_in = A_1^T ... A_steps^T grad_out, and when dalpha is
+ * non-NULL also dalpha[k] = dLoss/dalpha_k (fp32, steps entries, deterministic)
+ * which needs x (the forward input) and `workspace`.  Replaces the autograd
+ * backward of the reference PDE layer chain (src/models/pde_layers.py:113-188,
+ * per-layer alpha :216-219) and kernels/diffusion_triton.py:765-794,880-888. */
+int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, float* dalpha, void* workspace,
+                          int64_t workspace_bytes, int64_t B, int64_t L, int64_t D, int64_t g_sB, int64_t g_sL,
+                          int64_t x_sB, int64_t x_sL, int64_t d_sB, int64_t d_sL, int dtype, int steps, int causal,
+                          const float* alpha, const void* const* alpha_dev, int alpha_dev_dtype, const void* mask,
+                          int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream);
+
+/* Packed variable-length prefill: x, y are [total_rows, D] (row strides
+ * x_sL / y_sL), cu_seqlens is a DEVICE int32 array of nseq+1 offsets.
+ *   pad_to_max = 0: every sequence has its own copy boundary and no stencil
+ *                   reads across sequences;
+ *   pad_to_max = 1: the reference rule of src/cta/serving_vllm.py:72-111,
+ *                   275-303 -- each sequence behaves as if zero-padded to
+ *                   max_len rows (boundary rows 0 and max_len-1), results
+ *                   identical to the reference's packed path.
+ * max_len must be >= the longest sequence.  The host never reads cu_seqlens. */
+int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t D, int64_t x_sL, int64_t y_sL,
+                             const int32_t* cu_seqlens, int64_t nseq, int64_t max_len, int pad_to_max, int dtype,
+                             int steps, float alpha, void* stream);
+
+/* One shard of an L-sharded sequence ([B, L_local, D], contiguous): rows
+ * [pos_offset, pos_offset + L_local) of a sequence of global_len rows.
+ * lo_halo: [B, lo_rows, D] contiguous copy of the lo_rows rows just before the
+ * shard, hi_halo: [B, hi_rows, D] the hi_rows rows just after it (NULL at a
+ * global end).  Rows needed: steps on each side for the non-causal stencil,
+ * 2*steps before the shard for the causal forward, 2*steps after it for the
+ * causal adjoint.  Edge parts need every halo that exists.
+ *   part = CTA_SHARD_INTERIOR : output rows that need no halo (launch while
+ *                               the halos are still in flight);
+ *   part = CTA_SHARD_LO_EDGE / CTA_SHARD_HI_EDGE : the rows next to the shard
+ *                               ends, reading the halos.
+ * backward != 0 applies the adjoint to a gradient instead.  No reference
+ * counterpart: the reference runs on one device only. */
+int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_local, int64_t D, int64_t pos_offset,
+                            int64_t global_len, const void* lo_halo, int64_t lo_rows, const void* hi_halo,
+                            int64_t hi_rows, int part, int dtype, int steps, int causal, int backward, float alpha,
+                            void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CTA_STENCIL_H_ */

@@ -1,0 +1,250 @@
+"""CPU oracle for the fused diffusion stencil -- TEST INFRASTRUCTURE ONLY.
+
+A restatement, in plain PyTorch on the CPU, of the reference's own algorithm
+for the hot path.  Only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it, and
+only as the checker or the timed CPU baseline; the product path
+(``cta_b200``) never calls it and has no CPU fallback.
+
+Pinning: ``tests/golden/make_golden.py`` runs the reference itself (imported
+from its source tree in the build container) on seeded inputs and commits the
+results under ``tests/golden/``; ``tests/test_oracle_golden.py`` checks that
+every function below reproduces them bit for bit (forward) or to 1e-6
+(gradients).
+
+Every function follows the reference op by op -- separately rounded fp32 ops
+in the reference's order -- so its fp32 results are the reference's results.
+Citations are to files of the reference project.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence, Union
+
+import torch
+
+Alpha = Union[float, torch.Tensor]
+
+
+# ---------------------------------------------------------------------------
+# core stencil along the last axis, fp32
+# ---------------------------------------------------------------------------
+def _lap_last(u: torch.Tensor) -> torch.Tensor:
+    # src/cta/ops/diffusion.py:48-52 : right - 2.0 * mid + left
+    return u[..., 2:] - 2.0 * u[..., 1:-1] + u[..., :-2]
+
+
+def step_bdl(x_bdl: torch.Tensor, *, alpha: float, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """One non-causal step on [B, D, L], copy boundary (src/cta/ops/diffusion.py:17-56)."""
+    if x_bdl.ndim != 3:
+        raise ValueError(f"expected x_bdl.ndim == 3, got {x_bdl.ndim}")
+    out_dtype = x_bdl.dtype if out_dtype is None else out_dtype
+    if x_bdl.shape[2] < 3:
+        return x_bdl.to(dtype=out_dtype)
+    u = x_bdl.to(dtype=torch.float32)
+    mid = u[:, :, 1:-1]
+    new_mid = mid + float(alpha) * _lap_last(u)
+    return torch.cat([u[:, :, :1], new_mid, u[:, :, -1:]], dim=2).to(dtype=out_dtype)
+
+
+def steps_bdl(x_bdl: torch.Tensor, *, alpha: float, steps: int, out_dtype: Optional[torch.dtype] = None):
+    """`steps` steps, fp32 in between, rounded once (src/cta/ops/diffusion.py:59-77)."""
+    if steps < 0:
+        raise ValueError(f"expected steps >= 0, got {steps}")
+    out_dtype = x_bdl.dtype if out_dtype is None else out_dtype
+    if steps == 0:
+        return x_bdl.to(dtype=out_dtype)
+    u = x_bdl
+    for _ in range(steps):
+        u = step_bdl(u, alpha=alpha, out_dtype=torch.float32)
+    return u.to(dtype=out_dtype)
+
+
+def steps_bld(x_bld: torch.Tensor, *, alpha: float, steps: int) -> torch.Tensor:
+    """[B, L, D] form, fp32 in between (src/cta/serving_vllm.py:29-46)."""
+    if steps <= 0:
+        return x_bld
+    if x_bld.ndim != 3:
+        raise ValueError(f"expected x_bld.ndim == 3, got {x_bld.ndim}")
+    if x_bld.shape[1] < 3:
+        return x_bld
+    u = x_bld.to(dtype=torch.float32)
+    for _ in range(steps):
+        lap = u[:, 2:, :] - 2.0 * u[:, 1:-1, :] + u[:, :-2, :]
+        u = torch.cat([u[:, :1, :], u[:, 1:-1, :] + float(alpha) * lap, u[:, -1:, :]], dim=1)
+    return u.to(dtype=x_bld.dtype)
+
+
+# ---------------------------------------------------------------------------
+# PDE layer (diffusion), src/models/pde_layers.py
+# ---------------------------------------------------------------------------
+def _alpha_f32(alpha: Alpha) -> Union[float, torch.Tensor]:
+    if isinstance(alpha, torch.Tensor):
+        return alpha.to(dtype=torch.float32)  # pde_layers.py:219
+    return float(alpha)
+
+
+def _valid3(mask: torch.Tensor, n_out: int) -> torch.Tensor:
+    # pde_layers.py:39-64 -- all three stencil rows valid, last n_out windows, as (B, 1, n_out)
+    full = mask[:, :-2] * mask[:, 1:-1] * mask[:, 2:]
+    return full[:, -n_out:].unsqueeze(1).bool()
+
+
+def layer_step(
+    x: torch.Tensor,
+    alpha: Alpha,
+    *,
+    layout: str = "bdl",
+    causal: bool = False,
+    attention_mask: Optional[torch.Tensor] = None,
+    keep_fp32: bool = False,
+) -> torch.Tensor:
+    """One DiffusionPDELayer step (src/models/pde_layers.py:113-188, :218-219).
+
+    keep_fp32=True returns the fp32 result instead of casting back to x.dtype
+    (the fused stack keeps fp32 between steps).
+    """
+    seq_dim = 2 if layout == "bdl" else 1
+    if x.size(seq_dim) < 3:
+        return x
+    u = x.to(dtype=torch.float32)
+    if layout == "bld":
+        u = u.transpose(1, 2)
+    lap = u[:, :, 2:] - 2.0 * u[:, :, 1:-1] + u[:, :, :-2]
+    a = _alpha_f32(alpha)
+    if causal:
+        interior = u[:, :, 2:]
+        upd = interior + a * lap
+        if attention_mask is not None:
+            upd = torch.where(_valid3(attention_mask, upd.size(2)), upd, interior)
+        y = torch.cat([u[:, :, :2], upd], dim=2)
+    else:
+        interior = u[:, :, 1:-1]
+        upd = interior + a * lap
+        if attention_mask is not None:
+            upd = torch.where(_valid3(attention_mask, upd.size(2)), upd, interior)
+        y = torch.cat([u[:, :, :1], upd, u[:, :, -1:]], dim=2)
+    if attention_mask is not None:
+        m = attention_mask.bool().to(dtype=y.dtype).unsqueeze(1)  # pde_layers.py:26-36
+        y = y * m + u * (1 - m)
+    if layout == "bld":
+        y = y.transpose(1, 2)
+    return y if keep_fp32 else y.to(dtype=x.dtype)
+
+
+def layer_chain(
+    x: torch.Tensor,
+    alphas: Sequence[Alpha],
+    *,
+    layout: str = "bdl",
+    causal: bool = False,
+    attention_mask: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Consecutive layers, each rounding to x.dtype (transformers.py:127-133 loop)."""
+    y = x
+    for a in alphas:
+        y = layer_step(y, a, layout=layout, causal=causal, attention_mask=attention_mask)
+    return y
+
+
+def fused_stack(
+    x: torch.Tensor,
+    alphas: Sequence[Alpha],
+    *,
+    layout: str = "bdl",
+    causal: bool = False,
+    attention_mask: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """The same layers with fp32 kept between them and one final rounding."""
+    seq_dim = 2 if layout == "bdl" else 1
+    if x.size(seq_dim) < 3 or len(alphas) == 0:
+        return x
+    y = x.to(torch.float32)
+    for a in alphas:
+        y = layer_step(y, a, layout=layout, causal=causal, attention_mask=attention_mask, keep_fp32=True)
+    return y.to(dtype=x.dtype)
+
+
+# ---------------------------------------------------------------------------
+# adjoint of one step (kernels/diffusion_triton.py:96-133)
+# ---------------------------------------------------------------------------
+def step_adjoint_bdl(g: torch.Tensor, *, alpha: float) -> torch.Tensor:
+    """dx for one non-causal step: interior (1-2a) dy + a (dy[i-1][i-1>=1] + dy[i+1][i+1<=L-2]),
+    ends dy[0] + a dy[1] and dy[L-1] + a dy[L-2]; L < 3 returns g."""
+    L = g.shape[-1]
+    if L < 3:
+        return g
+    dy = g.to(torch.float32)
+    a = float(alpha)
+    prev = torch.zeros_like(dy)
+    nxt = torch.zeros_like(dy)
+    prev[..., 2:] = dy[..., 1:-1]   # dy[i-1] where i-1 >= 1
+    nxt[..., :-2] = dy[..., 1:-1]   # dy[i+1] where i+1 <= L-2
+    dx = (1.0 - 2.0 * a) * dy + a * (prev + nxt)
+    dx[..., 0] = dy[..., 0] + a * dy[..., 1]
+    dx[..., -1] = dy[..., -1] + a * dy[..., -2]
+    return dx.to(g.dtype)
+
+
+def grads(fn, x: torch.Tensor, grad_out: torch.Tensor, params: Sequence[torch.Tensor] = ()):
+    """(dx, [dparam...]) of sum(fn(x) * grad_out) by autograd through the oracle."""
+    xr = x.detach().clone().requires_grad_(True)
+    ps = [p.detach().clone().requires_grad_(True) for p in params]
+    y = fn(xr, *ps)
+    (y.float() * grad_out.float()).sum().backward()
+    return xr.grad.detach(), [p.grad.detach() for p in ps]
+
+
+# ---------------------------------------------------------------------------
+# packed variable-length prefill
+# ---------------------------------------------------------------------------
+def mixer_packed(x_flat: torch.Tensor, qsl: Sequence[int], max_len: int, *, alpha: float, steps: int):
+    """Reference packed path: zero-pad every request to max_len, run the [B, L, D]
+    stencil, unpack (src/cta/serving_vllm.py:72-111, :292-303)."""
+    qsl = [int(v) for v in qsl]
+    if max_len < 3 or steps <= 0:
+        return x_flat.clone()
+    R = len(qsl) - 1
+    padded = torch.zeros((R, max_len, x_flat.shape[-1]), dtype=x_flat.dtype)
+    for i in range(R):
+        s, e = qsl[i], qsl[i + 1]
+        if e > s:
+            padded[i, : e - s] = x_flat[s:e]
+    y = steps_bld(padded, alpha=alpha, steps=steps)
+    out = torch.empty_like(x_flat)
+    for i in range(R):
+        s, e = qsl[i], qsl[i + 1]
+        if e > s:
+            out[s:e] = y[i, : e - s]
+    return out
+
+
+def varlen_per_sequence(x_flat: torch.Tensor, qsl: Sequence[int], *, alpha: float, steps: int):
+    """Every sequence refined on its own, with its own copy boundary."""
+    qsl = [int(v) for v in qsl]
+    out = x_flat.clone()
+    for i in range(len(qsl) - 1):
+        s, e = qsl[i], qsl[i + 1]
+        if e > s:
+            out[s:e] = steps_bld(x_flat[s:e].unsqueeze(0), alpha=alpha, steps=steps)[0]
+    return out
+
+
+# ---------------------------------------------------------------------------
+# L-sharded view: output rows [a, b) need input rows [a - h, b + h) only
+# ---------------------------------------------------------------------------
+def window_bld(
+    x_window: torch.Tensor, *, win_start: int, global_len: int, out_start: int, out_stop: int, alpha: float,
+    steps: int,
+) -> torch.Tensor:
+    """Rows [out_start, out_stop) of steps_bld over a global sequence, given only the rows
+    x_window = global rows [win_start, win_start + len) (which must cover the halo)."""
+    n = x_window.shape[1]
+    u = x_window.to(torch.float32)
+    pos = torch.arange(win_start, win_start + n)
+    fixed = ((pos <= 0) | (pos >= global_len - 1)).view(1, n, 1)
+    for _ in range(steps):
+        lap = u[:, 2:, :] - 2.0 * u[:, 1:-1, :] + u[:, :-2, :]
+        mid = u[:, 1:-1, :] + float(alpha) * lap
+        mid = torch.where(fixed[:, 1:-1, :], u[:, 1:-1, :], mid)
+        u = torch.cat([u[:, :1, :], mid, u[:, -1:, :]], dim=1)
+    return u[:, out_start - win_start : out_stop - win_start, :].to(x_window.dtype)

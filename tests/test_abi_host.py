@@ -1,0 +1,108 @@
+"""CPU-only checks: the C ABI library loads and exports every declared symbol,
+argument validation fails cleanly without touching a device, and the host-side
+logic of the Python surface (gating, step policies, errors) matches the reference."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def _declared_symbols():
+    text = (REPO / "include" / "cta_stencil.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(cta_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    from cta_b200 import _lib
+
+    lib = _lib.load()
+    names = _declared_symbols()
+    assert len(names) >= 12, names
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/cta_stencil.h but not exported"
+    assert set(names) == set(_lib._SIGNATURES), "ctypes signatures out of sync with the header"
+    assert lib.cta_abi_version() == 1
+
+
+def test_invalid_arguments_fail_before_launch():
+    from cta_b200 import _lib
+
+    lib = _lib.load()
+    one = _lib.float_array([0.1])
+    null = ctypes.c_void_p(0)
+    # bad dtype
+    rc = lib.cta_diffusion_fwd_bld(null, null, 1, 10, 8, 80, 8, 80, 8, 7, 1, 0, one, None, 0, null, 0, 0, 0, null)
+    assert rc == _lib.CTA_EINVAL and b"dtype" in lib.cta_last_error()
+    # steps out of range
+    rc = lib.cta_diffusion_fwd_bdl(null, null, 1, 1, 10, 10, 0, 9, ctypes.c_float(0.1), null)
+    assert rc == _lib.CTA_EINVAL and b"steps" in lib.cta_last_error()
+    # L < 3 is the caller's identity case
+    rc = lib.cta_diffusion_fwd_bdl(ctypes.c_void_p(16), ctypes.c_void_p(16), 1, 1, 2, 2, 0, 1, ctypes.c_float(0.1),
+                                   null)
+    assert rc == _lib.CTA_EINVAL
+    # alpha missing
+    rc = lib.cta_diffusion_fwd_bld(null, null, 1, 10, 8, 80, 8, 80, 8, 0, 1, 0, None, None, 0, null, 0, 0, 0, null)
+    assert rc == _lib.CTA_EINVAL and b"alpha" in lib.cta_last_error()
+    # empty tensors are a no-op
+    rc = lib.cta_diffusion_fwd_bld(null, null, 0, 10, 8, 80, 8, 80, 8, 0, 1, 0, one, None, 0, null, 0, 0, 0, null)
+    assert rc == _lib.CTA_OK
+    # bad shard part
+    rc = lib.cta_diffusion_shard_bld(ctypes.c_void_p(16), ctypes.c_void_p(16), 1, 100, 8, 0, 100, null, 0, null, 0,
+                                     7, 0, 2, 0, 0, ctypes.c_float(0.1), null)
+    assert rc == _lib.CTA_EINVAL
+    assert lib.cta_diffusion_bwd_bld_workspace_bytes(1, 16384, 512, 1, 4, 0) >= 256 + 4 * 4 * 512
+
+
+def test_python_errors_without_gpu():
+    from cta_b200 import diffusion as D
+    from cta_b200.pde_layers import DiffusionPDELayer, create_pde_layer
+
+    with pytest.raises(ValueError):
+        D.diffusion_triton_fused(torch.randn(1, 2, 10), steps=2)  # CPU tensor
+    with pytest.raises(ValueError):
+        D.diffusion_triton_fused(torch.randn(1, 2, 10), steps=-1)
+    x = torch.randn(1, 2, 10)
+    assert D.diffusion_triton_fused(x, steps=0) is x
+    with pytest.raises(ValueError):
+        DiffusionPDELayer(4, layout="lbd")
+    with pytest.raises(ValueError):
+        create_pde_layer("heat", 4)
+    with pytest.raises(NotImplementedError):
+        create_pde_layer("reaction-diffusion", 4)
+    layer = DiffusionPDELayer(4, layout="bdl")
+    short = torch.randn(1, 4, 2)
+    assert layer(short) is short  # pde_layers.py:130-131
+    with pytest.raises(ValueError):
+        layer(torch.randn(1, 4, 10))  # no CPU path
+
+
+def test_mixer_host_logic():
+    from cta_b200.serving_vllm import CtaConfig, CtaPostAttnMixer, _infer_prefill, _to_int
+
+    assert _infer_prefill(None) is True
+    assert _infer_prefill(SimpleNamespace(is_prefill=False)) is False
+    assert _infer_prefill(SimpleNamespace(num_prefill_tokens=0)) is False
+    assert _infer_prefill(SimpleNamespace(prefill_metadata=object())) is True
+    assert _to_int(torch.tensor([7])) == 7 and _to_int("7") is None
+    m = CtaPostAttnMixer(CtaConfig(steps_policy="linear", steps_scale=1024, max_steps=8))
+    assert [m._resolve_steps(n) for n in (10, 1024, 5000, 10**6)] == [1, 1, 4, 8]
+    m = CtaPostAttnMixer(CtaConfig(steps_policy="log2", max_steps=8, min_seq_len=16))
+    assert [m._resolve_steps(n) for n in (8, 16, 100, 10**6)] == [0, 4, 6, 8]
+    with pytest.raises(ValueError):
+        CtaPostAttnMixer(CtaConfig(layout="xyz"))
+    with pytest.raises(ValueError):
+        CtaPostAttnMixer(CtaConfig(varlen_mode="xyz"))
+    x = torch.randn(2, 10, 4)
+    assert CtaPostAttnMixer(CtaConfig(enabled=False))(x) is x
+    assert CtaPostAttnMixer(CtaConfig())(x, is_prefill=False) is x
+    flat = torch.randn(10, 4)
+    assert CtaPostAttnMixer(CtaConfig())(flat) is flat  # no metadata -> passthrough (:284-285)
+    md = SimpleNamespace(max_query_len=2, query_start_loc=[0, 2, 4])
+    assert CtaPostAttnMixer(CtaConfig())(flat, attn_metadata=md) is flat  # max_query_len < 3

@@ -1,0 +1,159 @@
+"""[B, L, D] kernels (layers, mixer, varlen) vs the oracle."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import assert_close
+from oracle import diffusion_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.float32, torch.bfloat16, torch.float16]
+# D multiple of 8 -> TMA path; odd / small D -> generic loader path
+SHAPES = [(1, 4096, 512), (2, 1000, 96), (2, 37, 6), (1, 3, 8), (3, 129, 264), (1, 77, 513), (2, 50, 1)]
+
+
+def _ops():
+    from cta_b200 import ops
+    return ops
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("steps", [1, 2, 3, 4, 5, 6, 7, 8])
+def test_forward_bitexact(dtype, steps):
+    torch.manual_seed(0)
+    x = torch.randn(2, 1024, 512, dtype=dtype)
+    y = _ops().bld_forward(x.cuda(), [0.1] * steps, steps)
+    ref = O.steps_bld(x, alpha=0.1, steps=steps)
+    assert torch.equal(y.cpu(), ref), (y.cpu().float() - ref.float()).abs().max()
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("steps", [1, 2, 4, 8])
+def test_forward_shapes(shape, steps):
+    torch.manual_seed(1)
+    for dtype in (torch.float32, torch.bfloat16):
+        x = torch.randn(*shape, dtype=dtype)
+        y = _ops().bld_forward(x.cuda(), [0.1] * steps, steps)
+        assert torch.equal(y.cpu(), O.steps_bld(x, alpha=0.1, steps=steps)), (shape, dtype)
+
+
+def test_forward_strided_rows():
+    torch.manual_seed(2)
+    base = torch.randn(2, 600, 512, device="cuda")
+    x = base[:, ::2, :]  # row stride 2*D (TMA with a non-dense row stride)
+    y = _ops().bld_forward(x, [0.1] * 4, 4)
+    assert torch.equal(y.cpu(), O.steps_bld(x.cpu(), alpha=0.1, steps=4))
+
+
+def _mask(B, L, device="cpu"):
+    m = torch.ones(B, L, dtype=torch.long)
+    if L > 10:
+        m[0, L - 7:] = 0
+        m[-1, 3] = 0
+        m[-1, L // 2 : L // 2 + 2] = 0
+    return m
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("use_mask", [False, True])
+@pytest.mark.parametrize("steps", [1, 2, 4, 8])
+@pytest.mark.parametrize("shape", [(2, 300, 512), (2, 23, 6), (3, 1500, 264)])
+def test_stack_forward_causal_mask(causal, use_mask, steps, shape):
+    torch.manual_seed(3)
+    B, L, D = shape
+    x = torch.randn(B, L, D)
+    alphas = [0.1, 0.03, 0.12, 0.05, 0.08, 0.02, 0.11, 0.07][:steps]
+    m = _mask(B, L) if use_mask else None
+    y = _ops().bld_forward(x.cuda(), alphas, steps, causal=causal, mask=None if m is None else m.cuda())
+    ref = O.fused_stack(x, alphas, layout="bld", causal=causal, attention_mask=m)
+    assert torch.equal(y.cpu(), ref)
+
+
+@pytest.mark.parametrize("mask_dtype", [torch.bool, torch.int32, torch.int64, torch.float32, torch.uint8])
+def test_mask_dtypes(mask_dtype):
+    torch.manual_seed(4)
+    x = torch.randn(2, 64, 16)
+    m = _mask(2, 64)
+    y = _ops().bld_forward(x.cuda(), [0.1, 0.05], 2, mask=m.to(mask_dtype).cuda())
+    assert torch.equal(y.cpu(), O.fused_stack(x, [0.1, 0.05], layout="bld", attention_mask=m))
+
+
+def test_device_alpha_scalars():
+    torch.manual_seed(5)
+    x = torch.randn(2, 200, 64)
+    al = [torch.tensor([0.1]), torch.tensor([0.05], dtype=torch.bfloat16), torch.tensor([0.2])]
+    y = _ops().bld_forward(x.cuda(), [a.cuda() for a in al], 3)
+    ref = O.fused_stack(x, [a.float() for a in al], layout="bld")
+    assert torch.equal(y.cpu(), ref)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("use_mask", [False, True])
+@pytest.mark.parametrize("steps", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("shape", [(2, 300, 512), (2, 23, 6), (1, 700, 264)])
+def test_backward_dx_dalpha(causal, use_mask, steps, shape):
+    torch.manual_seed(6)
+    B, L, D = shape
+    x = torch.randn(B, L, D)
+    g = torch.randn(B, L, D)
+    alphas = [0.1, 0.03, 0.12, 0.05, 0.08, 0.02, 0.11, 0.07][:steps]
+    m = _mask(B, L) if use_mask else None
+    kw = dict(layout="bld", causal=causal, attention_mask=m)
+    dx_ref, da_ref = O.grads(lambda t, *al: O.fused_stack(t, list(al), **kw), x, g,
+                             [torch.tensor([a]) for a in alphas])
+    ops = _ops()
+    mc = None if m is None else m.cuda()
+    dx, da = ops.bld_backward(g.cuda(), alphas, steps, x=x.cuda(), causal=causal, mask=mc, need_dalpha=True)
+    assert_close(dx, dx_ref)
+    da_ref = torch.cat(da_ref)
+    scale = max(1.0, da_ref.abs().max().item())
+    assert (da.cpu() - da_ref).abs().max().item() <= 1e-4 * scale, (da.cpu(), da_ref)
+    dx2, none = ops.bld_backward(g.cuda(), alphas, steps, causal=causal, mask=mc)
+    assert none is None
+    assert torch.equal(dx2, dx)
+
+
+def test_backward_dalpha_repeatable():
+    torch.manual_seed(7)
+    x = torch.randn(1, 4096, 512, device="cuda")
+    g = torch.randn(1, 4096, 512, device="cuda")
+    ops = _ops()
+    r1 = ops.bld_backward(g, [0.1] * 4, 4, x=x, need_dalpha=True)[1].clone()
+    r2 = ops.bld_backward(g, [0.1] * 4, 4, x=x, need_dalpha=True)[1].clone()
+    assert torch.equal(r1, r2)  # deterministic reduction, workspace reusable
+
+
+@pytest.mark.parametrize("steps", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_varlen_reference_rule(steps, dtype):
+    torch.manual_seed(8)
+    lens = [5, 9, 3, 1, 2, 7, 40, 300, 33]
+    qsl = [0]
+    for n in lens:
+        qsl.append(qsl[-1] + n)
+    x = torch.randn(qsl[-1], 64).to(dtype)
+    cu = torch.tensor(qsl, dtype=torch.int32, device="cuda")
+    y = _ops().varlen_forward(x.cuda(), cu, max(lens), 0.1, steps, pad_to_max=True)
+    assert torch.equal(y.cpu(), O.mixer_packed(x, qsl, max(lens), alpha=0.1, steps=steps))
+
+
+@pytest.mark.parametrize("steps", [1, 2, 4, 8])
+def test_varlen_sequence_rule(steps):
+    torch.manual_seed(9)
+    lens = [5, 9, 3, 1, 2, 7, 40, 300, 33, 0, 17]
+    qsl = [0]
+    for n in lens:
+        qsl.append(qsl[-1] + n)
+    x = torch.randn(qsl[-1], 264)
+    cu = torch.tensor(qsl, dtype=torch.int32, device="cuda")
+    y = _ops().varlen_forward(x.cuda(), cu, max(lens), 0.1, steps, pad_to_max=False)
+    assert torch.equal(y.cpu(), O.varlen_per_sequence(x, qsl, alpha=0.1, steps=steps))
+
+
+def test_varlen_golden(golden):
+    for c in golden["mixer_packed"]:
+        cu = torch.tensor(c["qsl"], dtype=torch.int32, device="cuda")
+        y = _ops().varlen_forward(c["x"].cuda(), cu, c["max_len"], c["alpha"], c["steps"], pad_to_max=True)
+        assert torch.equal(y.cpu(), c["y"])
