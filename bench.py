@@ -221,6 +221,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    if args.mode == "kernel":
+        # bare launches for profilers: no sampler, e2e, sweep or CPU baseline
+        t = _time_launches(step, args.steps, stream)
+        if rank == 0:
+            print(json.dumps({"mode": "kernel", "launches": args.steps, "us_per_call": t / args.steps * 1e6,
+                              "config": _config(args)}), flush=True)
+        return
     if world > 1:
         dist.barrier()
     sampler = ClockSampler(local_rank) if rank == 0 else None
@@ -321,6 +328,8 @@ def main() -> None:
     ap.add_argument("--stencil-steps", type=int, default=4)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--mode", choices=["full", "kernel"], default="full",
+                    help="kernel: only warmup + timed launches of the fused kernel (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -115,6 +115,8 @@ __global__ void __launch_bounds__(kBldThreads) bld_bwd_kernel(const __grid_const
     float2 al[S];
 #pragma unroll
     for (int k = 0; k < S; ++k) al[k] = f2(alf[k]);
+    // rounded products as fma with a run-time -0 addend: exactly the forward's rounding
+    const float2 zn2 = f2(a.neg_zero);
 
     // adjoint state per level m (step k = S - m)
     float2 A1[S], A2[S], G1[S], G2[S];
@@ -170,7 +172,7 @@ __global__ void __launch_bounds__(kBldThreads) bld_bwd_kernel(const __grid_const
                 for (int q = 0; q < S; ++q) {
                   const float2 lp = lap3(F2[q], F1[q], xc);  // lap_c(u_q)[jx]
                   lapv[q] = lp;
-                  float2 un = __fadd2_rn(xc, __fmul2_rn(al[q], lp));
+                  float2 un = add2(xc, fma2(al[q], lp, zn2));
                   if (SLOW) un = sel2(fx, xc, un);
                   F2[q] = F1[q];
                   F1[q] = xc;
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(kBldThreads) bld_bwd_kernel(const __grid_const
                 for (int q = 0; q < S; ++q) {
                   const float2 lp = lap3(F2[q], F1[q], xc);  // lap(u_q)[jx - q - 1]
                   lapv[q] = lp;
-                  float2 un = __fadd2_rn(F1[q], __fmul2_rn(al[q], lp));
+                  float2 un = add2(F1[q], fma2(al[q], lp, zn2));
                   if (SLOW) un = sel2((fw >> (S - 1 - q)) & 1u, F1[q], un);
                   F2[q] = F1[q];
                   F1[q] = xc;
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(kBldThreads) bld_bwd_kernel(const __grid_const
             if (SLOW) {
               if (rb.zero(jg)) cur_g = f2(0.f);
             }
-            float2 cur_a = __fmul2_rn(al[S - 1], cur_g);
+            float2 cur_a = mul2(al[S - 1], cur_g);
             if (SLOW) cur_a = sel2(rb.fixed(jg), f2(0.f), cur_a);
             uint32_t fwg = 0u;
             if (SLOW && !CAUSAL) fwg = rb.window8_fixed(jg - S);
@@ -226,24 +228,24 @@ __global__ void __launch_bounds__(kBldThreads) bld_bwd_kernel(const __grid_const
                 const int rel = t - G::pair_off(k);  // paired row - l0
                 bool take = rel >= 0 && rel < nout;
                 if (SLOW) take = take && !rb.fixed(l0 + rel);
-                if (take) acc[k - 1] = __ffma2_rn(gk, lk, acc[k - 1]);
+                if (take) acc[k - 1] = fma2(gk, lk, acc[k - 1]);
               }
               float2 gn;
               if (CAUSAL) {
-                gn = __fadd2_rn(G2[m], lap3(cur_a, A1[m], A2[m]));
+                gn = add2(G2[m], lap3(cur_a, A1[m], A2[m]));
                 A2[m] = A1[m];
                 A1[m] = cur_a;
                 G2[m] = G1[m];
                 G1[m] = cur_g;
               } else {
-                gn = __fadd2_rn(G1[m], lap3(A2[m], A1[m], cur_a));
+                gn = add2(G1[m], lap3(A2[m], A1[m], cur_a));
                 A2[m] = A1[m];
                 A1[m] = cur_a;
                 G1[m] = cur_g;
               }
               cur_g = gn;
               if (m < S - 1) {
-                cur_a = __fmul2_rn(al[S - 2 - m], gn);
+                cur_a = mul2(al[S - 2 - m], gn);
                 if (SLOW) {
                   const bool fx = CAUSAL ? rb.fixed(jg - 2 * m - 2) : ((fwg >> (S - 1 - m)) & 1u);
                   cur_a = sel2(fx, f2(0.f), cur_a);
@@ -336,7 +338,7 @@ template <typename T, int S, bool CAUSAL, bool DA>
 cudaError_t launch_bwd_t(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap, dim3 grid, size_t smem,
                          cudaStream_t st) {
   auto kern = bld_bwd_kernel<T, S, CAUSAL, DA>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kBldThreads, smem, st>>>(*gmap, *xmap, a);
   return cudaGetLastError();

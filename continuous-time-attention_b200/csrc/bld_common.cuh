@@ -1,6 +1,7 @@
 // Device helpers shared by the [B, L, D] forward and backward kernels.
 #pragma once
 
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -25,7 +26,8 @@ __device__ __forceinline__ Seg resolve_seg(const BldArgs& a, int z) {
     const int64_t b1 = a.cu_seqlens[z + 1];
     s.row0 = b0;
     s.bcoord = 0;
-    s.n = b1 > b0 ? b1 - b0 : 0;
+    // offsets outside the packed tensor (malformed input) leave the sequence untouched
+    s.n = (b1 > b0 && b0 >= 0 && b1 <= a.L) ? b1 - b0 : 0;
     s.gdom = a.pad_to_max ? a.max_len : s.n;
     s.pos = 0;
   } else {
@@ -155,6 +157,38 @@ __device__ __forceinline__ void load_alphas(const BldArgs& a, float* out, int st
   for (int k = 0; k < kMaxSteps; ++k) {
     if (k < steps) out[k] = a.alpha_dev[k] != nullptr ? load_scalar(a.alpha_dev[k], a.alpha_dev_dtype) : a.alpha[k];
   }
+}
+
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device); the
+// attribute lives in the device context, so it is tracked per device.
+inline cudaError_t ensure_smem_attr(const void* kern, size_t smem) {
+  struct Entry {
+    const void* kern;
+    unsigned long long devmask;
+    size_t smem;
+  };
+  static Entry table[512];
+  static int n = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+  for (int i = 0; i < n; ++i) {
+    if (table[i].kern == kern) {
+      if (bit && (table[i].devmask & bit) && table[i].smem >= smem) return cudaSuccess;
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e == cudaSuccess) {
+        table[i].devmask |= bit;
+        if (smem > table[i].smem) table[i].smem = smem;
+      }
+      return e;
+    }
+  }
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess && n < 512) table[n++] = Entry{kern, bit, smem};
+  return e;
 }
 
 }  // namespace

@@ -1,6 +1,5 @@
 // Fused multi-step diffusion stencil on [B, L, D] hidden states (feature axis
-// contiguous) -- forward, backward (A^T applied `steps` times) and backward
-// with the per-step d(alpha) reduction, all in one launch per call.
+// contiguous) -- forward, all `steps` steps in one launch.
 //
 // Reference semantics followed here:
 //   * one step, copy boundary:      src/cta/ops/diffusion.py:17-56
@@ -8,20 +7,20 @@
 //                                   src/cta/serving_vllm.py:29-46 ([B,L,D])
 //   * causal stencil, attention mask, per-layer alpha:
 //                                   src/models/pde_layers.py:39-64,113-188,218-219
-//   * adjoint of one step:          kernels/diffusion_triton.py:96-133
 //   * zero-padded packed prefill:   src/cta/serving_vllm.py:72-111,275-303
 //
-// Work decomposition.  A CTA owns an output tile of TL rows x 256 columns.
-// Its 128 threads each own two adjacent columns (one float2) and *march* down
-// the rows of the tile plus a halo: every arriving input row advances all
-// `steps` time levels by one row (a wavefront, level k lags k rows, or 0 rows
-// for the causal stencil), so each thread keeps only two rows of state per
-// level in registers and every intermediate level stays on chip.  Input rows
-// arrive in shared memory through a ring of TMA tile loads (16 rows x 256
-// columns per chunk, 4 chunks in flight, one mbarrier per slot); the output is
-// written once, straight from registers.  HBM traffic is therefore one read of
-// the input (the halo rows are re-read from L2 by the neighbouring tile) and
-// one write of the output.
+// Work decomposition.  A CTA owns an output tile of TL rows x 512 columns.
+// Its 128 threads each own four adjacent columns (two packed fp32 pairs) and
+// *march* down the rows of the tile plus a halo: every arriving input row
+// advances all `steps` time levels by one row (a wavefront: level k lags k
+// rows, or 0 rows for the causal stencil), so a thread keeps two rows of state
+// per level in registers and every intermediate level stays on chip.  Input
+// rows arrive in shared memory through a ring of TMA tile loads (8 rows x 512
+// columns per chunk as two 256-column boxes, 4 chunks in flight, one mbarrier
+// per slot); the output is written once, straight from registers, as one
+// 8/16-byte vector per thread and row.  HBM traffic is one read of the input
+// (halo rows are re-read from L2 by the neighbouring tile) and one write of
+// the output.
 //
 // Rows that must not change -- the copy boundary, rows whose 3-row stencil
 // touches a masked position, per-sequence boundaries of packed prefill -- are
@@ -33,21 +32,46 @@ namespace cta {
 
 __device__ int g_bld_fwd_error;
 
-// ===========================================================================
-// forward
-// ===========================================================================
+namespace {
+
+// Plain-load fill of one forward chunk (two [RC][256] column blocks), for
+// tensors TMA cannot address and for shard edges that read neighbour halos.
+template <typename T>
+__device__ void fill_fwd_chunk(const BldArgs& a, const Seg& s, int64_t jrow0, int d0, T* dst) {
+  const T zero = Elem<T>::from_f(0.f);
+  for (int idx = threadIdx.x; idx < kFwdRC * kFwdDT; idx += kFwdThreads) {
+    const int i = idx / kFwdDT;
+    const int cc = idx - i * kFwdDT;
+    const int box = cc / kBoxCols, cb = cc - box * kBoxCols;
+    const int64_t tr = s.row0 + jrow0 + i;
+    const int col = d0 + cc;
+    const T* rowp = nullptr;
+    if (tr >= 0 && tr < a.L) {
+      rowp = static_cast<const T*>(a.x) + static_cast<int64_t>(s.bcoord) * a.xsB + tr * a.xsL;
+    } else if (tr < 0 && a.lo_ext != nullptr && tr >= -a.hext_lo) {
+      rowp = static_cast<const T*>(a.lo_ext) + (static_cast<int64_t>(s.bcoord) * a.hext_lo + (a.hext_lo + tr)) * a.D;
+    } else if (tr >= a.L && a.hi_ext != nullptr && tr - a.L < a.hext_hi) {
+      rowp = static_cast<const T*>(a.hi_ext) + (static_cast<int64_t>(s.bcoord) * a.hext_hi + (tr - a.L)) * a.D;
+    }
+    dst[box * kFwdRC * kBoxCols + i * kBoxCols + cb] = (rowp != nullptr && col < a.D) ? rowp[col] : zero;
+  }
+}
+
+}  // namespace
+
 template <typename T, int S, bool CAUSAL>
-__global__ void __launch_bounds__(kBldThreads) bld_fwd_kernel(const __grid_constant__ CUtensorMap xmap,
+__global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_constant__ CUtensorMap xmap,
                                                               const BldArgs a) {
-  using E = Elem<T>;
-  using P = typename E::Pair;
+  using Q = Quad<T>;
+  using V = typename Q::V;
   constexpr int HL = CAUSAL ? 2 * S : S;  // halo rows above the tile
   constexpr int LAG = 2 * S;              // march rows before the first output row
-  constexpr int PAIRS = kBldDT / 2;
+  constexpr int CHUNK = kFwdRC * kFwdDT;  // elements per pipeline slot
+  constexpr int BOXE = kFwdRC * kBoxCols;  // elements per TMA box
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   T* ring = reinterpret_cast<T*>(smem_raw);
-  __shared__ __align__(8) uint64_t full_bar[kBldStages];
+  __shared__ __align__(8) uint64_t full_bar[kFwdStages];
   __shared__ uint32_t fbits[kBldMaxWords + 2];
   __shared__ uint32_t zbits[kBldMaxWords + 2];
 
@@ -55,130 +79,177 @@ __global__ void __launch_bounds__(kBldThreads) bld_fwd_kernel(const __grid_const
   const int64_t l0 = a.out_begin + static_cast<int64_t>(blockIdx.x) * a.TL;
   const int64_t oend = a.out_end < sg.n ? a.out_end : sg.n;
   if (l0 >= oend) return;
-  const int d0 = blockIdx.y * kBldDT;
+  const int d0 = blockIdx.y * kFwdDT;
   const int64_t jb = l0 - HL;
   const int nout = static_cast<int>(oend - l0 < a.TL ? oend - l0 : a.TL);
   const int nrows = nout + LAG;
-  const int nch = (nrows + kBldRC - 1) / kBldRC;
+  const int nch = (nrows + kFwdRC - 1) / kFwdRC;
   const int tid = threadIdx.x;
   const bool use_tma = a.use_tma != 0;
+  const int nbox = (d0 + kBoxCols < a.D) ? 2 : 1;
 
   if (tid == 0) {
     if (use_tma) prefetch_tmap(&xmap);
 #pragma unroll
-    for (int s = 0; s < kBldStages; ++s) mbar_init(&full_bar[s], 1);
+    for (int s = 0; s < kFwdStages; ++s) mbar_init(&full_bar[s], 1);
     fence_mbar_init();
   }
   RowBits rb{fbits, zbits, jb};
-  const bool slow = build_row_bits<CAUSAL>(a, sg, rb, (nch * kBldRC + 31) / 32);
+  const bool slow = build_row_bits<CAUSAL>(a, sg, rb, (nch * kFwdRC + 31) / 32);
 
   auto issue = [&](int c) {
-    const int slot = c % kBldStages;
-    mbar_arrive_expect_tx(&full_bar[slot], kBldRC * kBldDT * sizeof(T));
-    tma_load_3d(ring + slot * kBldRC * kBldDT, &xmap, &full_bar[slot], d0,
-                static_cast<int>(sg.row0 + jb + c * kBldRC), sg.bcoord);
+    const int slot = c % kFwdStages;
+    mbar_arrive_expect_tx(&full_bar[slot], nbox * BOXE * sizeof(T));
+    const int row = static_cast<int>(sg.row0 + jb + c * kFwdRC);
+    for (int b = 0; b < nbox; ++b)
+      tma_load_3d(ring + slot * CHUNK + b * BOXE, &xmap, &full_bar[slot], d0 + b * kBoxCols, row, sg.bcoord);
   };
   if (use_tma && tid == 0) {
-    for (int c = 0; c < nch && c < kBldStages; ++c) issue(c);
+    for (int c = 0; c < nch && c < kFwdStages; ++c) issue(c);
   }
 
   float alf[kMaxSteps];
   load_alphas(a, alf, S);
-  float2 al[S];
+  pf2 al[S];
 #pragma unroll
-  for (int k = 0; k < S; ++k) al[k] = f2(alf[k]);
+  for (int k = 0; k < S; ++k) al[k] = pbc(alf[k]);
+  const pf2 m2 = pbc(-2.f);
+  const pf2 zn = pbc(a.neg_zero);
 
-  float2 P1[S], P2[S];
+  // per-level state: rows (lag+2, lag+1) behind the newest, for both pairs
+  pf2 P1a[S], P2a[S], P1b[S], P2b[S];
 #pragma unroll
-  for (int k = 0; k < S; ++k) P1[k] = P2[k] = f2(0.f);
+  for (int k = 0; k < S; ++k) P1a[k] = P2a[k] = P1b[k] = P2b[k] = 0ull;
 
-  const int col = d0 + 2 * tid;
+  // column quad of this thread: box (tid / 64), 4 columns at (tid % 64) * 4
+  const int box = tid >> 6;
+  const int cb = (tid & 63) * 4;
+  const int col = d0 + box * kBoxCols + cb;
   const bool col_ok = col < a.D;
-  const bool pair_ok = a.y != nullptr && (col + 1 < a.D) && ((a.ysB | a.ysL) % 2 == 0) &&
-                       (reinterpret_cast<uintptr_t>(a.y) % sizeof(P) == 0);
-  T* ybase = static_cast<T*>(a.y) + static_cast<int64_t>(sg.bcoord) * a.ysB;
+  const bool quad_ok = a.y_quad_ok != 0 && col + 3 < a.D;
+  T* const ybase = static_cast<T*>(a.y) + static_cast<int64_t>(sg.bcoord) * a.ysB + sg.row0 * a.ysL + col;
+  const int soff = box * BOXE + cb;  // element offset of this thread in a slot
+
+  auto store_row = [&](int64_t orow, pf2 pa, pf2 pb) {
+    T* yp = ybase + orow * a.ysL;
+    if (quad_ok) {
+      *reinterpret_cast<V*>(yp) = Q::join(pa, pb);
+    } else if (col_ok) {
+      float v[4];
+      upk(pa, v[0], v[1]);
+      upk(pb, v[2], v[3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (col + j < a.D) yp[j] = Elem<T>::from_f(v[j]);
+    }
+  };
+
+  // one march row: input (xa, xb) of march row t; returns level-S values
+  auto step_row = [&](auto slow_tag, int64_t j, pf2& xa, pf2& xb) {
+    constexpr bool SLOW = decltype(slow_tag)::value;
+    if (SLOW) {
+      if (rb.zero(j)) xa = xb = 0ull;
+    }
+    if (CAUSAL) {
+      const bool fx = SLOW && rb.fixed(j);
+#pragma unroll
+      for (int k = 0; k < S; ++k) {
+        pf2 na = pst_c(P2a[k], P1a[k], xa, al[k], m2, zn);
+        pf2 nb = pst_c(P2b[k], P1b[k], xb, al[k], m2, zn);
+        if (SLOW) {
+          na = psel(fx, xa, na);
+          nb = psel(fx, xb, nb);
+        }
+        P2a[k] = P1a[k];
+        P1a[k] = xa;
+        xa = na;
+        P2b[k] = P1b[k];
+        P1b[k] = xb;
+        xb = nb;
+      }
+    } else {
+      // level k updates row j-1-k: bit (S-1-k) of the window of rows j-S .. j-1
+      const uint32_t fw = SLOW ? rb.window8_fixed(j - S) : 0u;
+#pragma unroll
+      for (int k = 0; k < S; ++k) {
+        pf2 na = pst_nc(P2a[k], P1a[k], xa, al[k], m2, zn);
+        pf2 nb = pst_nc(P2b[k], P1b[k], xb, al[k], m2, zn);
+        if (SLOW) {
+          const bool fx = (fw >> (S - 1 - k)) & 1u;
+          na = psel(fx, P1a[k], na);
+          nb = psel(fx, P1b[k], nb);
+        }
+        P2a[k] = P1a[k];
+        P1a[k] = xa;
+        xa = na;
+        P2b[k] = P1b[k];
+        P1b[k] = xb;
+        xb = nb;
+      }
+    }
+  };
+
+  auto march_chunk = [&](auto slow_tag, int c, const T* buf) {
+    const int t0 = c * kFwdRC;
+    // chunks whose every row is an output row store without per-row checks
+    const bool all_store = t0 >= LAG && t0 + kFwdRC <= LAG + nout;
+    V in[kFwdRC];
+#pragma unroll
+    for (int i = 0; i < kFwdRC; ++i) in[i] = *reinterpret_cast<const V*>(buf + soff + i * kBoxCols);
+#pragma unroll
+    for (int i = 0; i < kFwdRC; ++i) {
+      pf2 xa, xb;
+      Q::split(in[i], xa, xb);
+      step_row(slow_tag, jb + t0 + i, xa, xb);
+      const int t = t0 + i;
+      if (all_store || (t >= LAG && t < LAG + nout)) store_row(l0 + t - LAG, xa, xb);
+    }
+  };
 
   int err = 0;
   for (int c = 0; c < nch; ++c) {
-    const int slot = c % kBldStages;
-    T* buf = ring + slot * kBldRC * kBldDT;
+    const int slot = c % kFwdStages;
+    T* buf = ring + slot * CHUNK;
     if (use_tma) {
-      if (!mbar_wait_bounded(&full_bar[slot], (c / kBldStages) & 1)) err = 1;
+      if (!mbar_wait_bounded(&full_bar[slot], (c / kFwdStages) & 1)) err = 1;
     } else {
-      fill_chunk_generic<T>(a, a.x, a.xsB, a.xsL, sg, jb + c * kBldRC, d0, buf);
+      fill_fwd_chunk<T>(a, sg, jb + c * kFwdRC, d0, buf);
       __syncthreads();
     }
     if (!err) {
-      const P* rp = reinterpret_cast<const P*>(buf) + tid;
-      auto march = [&](auto slow_tag) {
-        constexpr bool SLOW = decltype(slow_tag)::value;
-#pragma unroll
-        for (int i = 0; i < kBldRC; ++i) {
-          const int t = c * kBldRC + i;
-          const int64_t j = jb + t;
-          float2 cur = E::unpack(rp[i * PAIRS]);
-          if (SLOW) {
-            if (rb.zero(j)) cur = f2(0.f);
-          }
-          if (CAUSAL) {
-            const bool fx = SLOW && rb.fixed(j);
-#pragma unroll
-            for (int k = 0; k < S; ++k) {
-              float2 nx = stencil_c(P2[k], P1[k], cur, al[k]);
-              if (SLOW) nx = sel2(fx, cur, nx);
-              P2[k] = P1[k];
-              P1[k] = cur;
-              cur = nx;
-            }
-          } else {
-            // level k updates row j-1-k; bit (S-1-k) of the window of rows j-S .. j-1
-            const uint32_t fw = SLOW ? rb.window8_fixed(j - S) : 0u;
-#pragma unroll
-            for (int k = 0; k < S; ++k) {
-              float2 nx = stencil_nc(P2[k], P1[k], cur, al[k]);
-              if (SLOW) nx = sel2((fw >> (S - 1 - k)) & 1u, P1[k], nx);
-              P2[k] = P1[k];
-              P1[k] = cur;
-              cur = nx;
-            }
-          }
-          const int64_t orow = l0 + t - LAG;
-          if (t >= LAG && orow < oend && col_ok) {
-            const int64_t tr = sg.row0 + orow;
-            if (tr >= 0 && tr < a.L) store_pair<T>(ybase + tr * a.ysL, col, a, cur, pair_ok);
-          }
-        }
-      };
-      if (slow) march(std::true_type{});
-      else march(std::false_type{});
+      if (slow) march_chunk(std::true_type{}, c, buf);
+      else march_chunk(std::false_type{}, c, buf);
     }
     if (__syncthreads_or(err)) {
       if (tid == 0) {
         atomicExch(&g_bld_fwd_error, kDevTimeout);
         // drain (bounded) every load still in flight before the CTA exits
         if (use_tma)
-          for (int cc = c; cc < nch && cc < c + kBldStages; ++cc)
-            mbar_wait_bounded(&full_bar[cc % kBldStages], (cc / kBldStages) & 1);
+          for (int cc = c; cc < nch && cc < c + kFwdStages; ++cc)
+            mbar_wait_bounded(&full_bar[cc % kFwdStages], (cc / kFwdStages) & 1);
       }
       __syncthreads();
       return;
     }
-    if (use_tma && tid == 0 && c + kBldStages < nch) issue(c + kBldStages);
+    if (use_tma && tid == 0 && c + kFwdStages < nch) issue(c + kFwdStages);
   }
 }
 
+size_t fwd_smem_bytes(int dtype) {
+  const size_t es = dtype == kF32 ? 4 : 2;
+  return static_cast<size_t>(kFwdStages) * kFwdRC * kFwdDT * es;
+}
 
 namespace {
 
 template <typename T, int S, bool CAUSAL>
 cudaError_t launch_fwd_t(const BldArgs& a, const CUtensorMap* xmap, dim3 grid, size_t smem, cudaStream_t st) {
   auto kern = bld_fwd_kernel<T, S, CAUSAL>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kBldThreads, smem, st>>>(*xmap, a);
+  kern<<<grid, kFwdThreads, smem, st>>>(*xmap, a);
   return cudaGetLastError();
 }
-
 
 template <typename T, bool CAUSAL>
 cudaError_t fwd_steps(const BldArgs& a, const CUtensorMap* m, int steps, dim3 g, size_t sm, cudaStream_t st) {
@@ -195,13 +266,11 @@ cudaError_t fwd_steps(const BldArgs& a, const CUtensorMap* m, int steps, dim3 g,
   }
 }
 
-
 template <typename T>
 cudaError_t fwd_dtype(const BldArgs& a, const CUtensorMap* m, int steps, int causal, dim3 g, size_t sm,
                       cudaStream_t st) {
   return causal ? fwd_steps<T, true>(a, m, steps, g, sm, st) : fwd_steps<T, false>(a, m, steps, g, sm, st);
 }
-
 
 }  // namespace
 
@@ -214,7 +283,6 @@ cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, int dtype,
     default: return cudaErrorInvalidValue;
   }
 }
-
 
 int read_device_error_bld_fwd(int clear) {
   int v = 0;

@@ -73,9 +73,50 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 3-D map over a [nb, rows, D] tensor with element strides (sB, sL, 1); box is
-// kBldRC rows x kBldDT columns.  Returns false when TMA cannot address it.
+// box_rows rows x kBoxCols columns.  Returns false when TMA cannot address it.
+bool encode_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t rows, int64_t D, int64_t sB,
+                int64_t sL, int box_rows);
+
+// Encoded maps are pure host data; the last few are kept per thread so that
+// repeated calls on the same buffers skip the encode.
 bool make_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t rows, int64_t D, int64_t sB,
-              int64_t sL) {
+              int64_t sL, int box_rows) {
+  struct Slot {
+    const void* base;
+    int dtype;
+    int box_rows;
+    int64_t nb, rows, D, sB, sL;
+    bool ok;
+    CUtensorMap map;
+  };
+  constexpr int kSlots = 16;
+  thread_local Slot cache[kSlots];
+  thread_local int next = 0;
+  for (int i = 0; i < kSlots; ++i) {
+    const Slot& c = cache[i];
+    if (c.base == base && base != nullptr && c.dtype == dtype && c.box_rows == box_rows && c.nb == nb &&
+        c.rows == rows && c.D == D && c.sB == sB && c.sL == sL) {
+      if (c.ok) *m = c.map;
+      return c.ok;
+    }
+  }
+  Slot& c = cache[next];
+  next = (next + 1) % kSlots;
+  c.ok = encode_map(&c.map, base, dtype, nb, rows, D, sB, sL, box_rows);
+  c.base = base;
+  c.dtype = dtype;
+  c.box_rows = box_rows;
+  c.nb = nb;
+  c.rows = rows;
+  c.D = D;
+  c.sB = sB;
+  c.sL = sL;
+  if (c.ok) *m = c.map;
+  return c.ok;
+}
+
+bool encode_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t rows, int64_t D, int64_t sB,
+                int64_t sL, int box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr || base == nullptr) return false;
   const int64_t es = static_cast<int64_t>(dtype_size(dtype));
@@ -88,7 +129,7 @@ bool make_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t r
   if (sL * es >= (1LL << 40) || bstride >= (1LL << 40)) return false;
   cuuint64_t gdim[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(nb)};
   cuuint64_t gstride[2] = {static_cast<cuuint64_t>(sL * es), static_cast<cuuint64_t>(bstride)};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBldDT), static_cast<cuuint32_t>(kBldRC), 1u};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBoxCols), static_cast<cuuint32_t>(box_rows), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUtensorMapDataType dt = dtype == CTA_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : dtype == CTA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -149,19 +190,25 @@ int check_common(int dtype, int steps) {
 BldArgs blank_bld() {
   BldArgs a;
   std::memset(&a, 0, sizeof(a));
+  a.neg_zero = -0.0f;
   return a;
+}
+
+bool quad_ok(const void* y, int dtype, int64_t nb, int64_t D, int64_t sB, int64_t sL) {
+  const int64_t es = static_cast<int64_t>(dtype_size(dtype));
+  return reinterpret_cast<uintptr_t>(y) % (4 * es) == 0 && D % 4 == 0 && sL % 4 == 0 && (nb == 1 || sB % 4 == 0);
 }
 
 int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int64_t tile_rows, cudaStream_t st,
                const CUtensorMap& xmap) {
   const int64_t ntl = (tile_rows + a.TL - 1) / a.TL;
-  const int64_t ndt = (a.D + kBldDT - 1) / kBldDT;
+  const int64_t ndt = (a.D + kFwdDT - 1) / kFwdDT;
   if (ntl <= 0 || nbatch <= 0) return ok();
   if (ntl > 0x7fffffffLL || ndt > 65535 || nbatch > 65535)
     return fail(CTA_EUNSUPPORTED, "grid too large (tiles %lld, D tiles %lld, batch %lld)", (long long)ntl,
                 (long long)ndt, (long long)nbatch);
   dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(nbatch));
-  const cudaError_t e = launch_bld_fwd(a, &xmap, dtype, steps, causal, grid, bld_smem_bytes(dtype, 0), st);
+  const cudaError_t e = launch_bld_fwd(a, &xmap, dtype, steps, causal, grid, fwd_smem_bytes(dtype), st);
   if (e != cudaSuccess) return cuda_fail(e, "bld forward launch");
   return ok();
 }
@@ -221,6 +268,7 @@ int cta_diffusion_bdl_ex(const void* in, void* out, int64_t B, int64_t D, int64_
   if (L < 3) return fail(CTA_EINVAL, "L < 3 is the identity; handled by the caller");
   BdlArgs a;
   std::memset(&a, 0, sizeof(a));
+  a.neg_zero = -0.0f;
   a.in = in;
   a.out = out;
   a.rows = B * D;
@@ -296,13 +344,14 @@ int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t 
   a.msB = mask_sB;
   a.msL = mask_sL;
   fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
-  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
+  const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
   a.TL = pick_tl(L, ndt * B, steps);
   a.out_begin = 0;
   a.out_end = L;
+  a.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
   CUtensorMap xmap;
   std::memset(&xmap, 0, sizeof(xmap));
-  a.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL) ? 1 : 0;
+  a.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC) ? 1 : 0;
   return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), xmap);
 }
 
@@ -373,8 +422,8 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
   CUtensorMap gmap, xmap;
   std::memset(&gmap, 0, sizeof(gmap));
   std::memset(&xmap, 0, sizeof(xmap));
-  bool tma = make_map(&gmap, grad_out, dtype, B, L, D, g_sB, g_sL);
-  if (da) tma = tma && make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL);
+  bool tma = make_map(&gmap, grad_out, dtype, B, L, D, g_sB, g_sL, kBldRC);
+  if (da) tma = tma && make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kBldRC);
   else xmap = gmap;
   a.use_tma = tma ? 1 : 0;
   if (da) {
@@ -413,15 +462,16 @@ int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t
   a.pad_to_max = pad_to_max ? 1 : 0;
   a.max_len = max_len;
   for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
-  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
+  const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
   // tiles are cut per sequence: size them from the average sequence length
   const int64_t avg = std::max<int64_t>(1, total_rows / nseq);
   a.TL = pick_tl(avg, ndt * nseq, steps);
   a.out_begin = 0;
   a.out_end = max_len;
+  a.y_quad_ok = quad_ok(y, dtype, 1, D, 0, y_sL) ? 1 : 0;
   CUtensorMap xmap;
   std::memset(&xmap, 0, sizeof(xmap));
-  a.use_tma = make_map(&xmap, x, dtype, 1, total_rows, D, 0, x_sL) ? 1 : 0;
+  a.use_tma = make_map(&xmap, x, dtype, 1, total_rows, D, 0, x_sL, kFwdRC) ? 1 : 0;
   return launch_fwd(a, dtype, steps, 0, nseq, max_len, static_cast<cudaStream_t>(stream), xmap);
 }
 
@@ -484,14 +534,16 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
     a.hext_hi = a.hi_ext ? static_cast<int>(hi_rows) : 0;
   }
   for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
-  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
+  const int64_t ndt = (D + (backward ? kBldDT : kFwdDT) - 1) / (backward ? kBldDT : kFwdDT);
   a.TL = edge ? static_cast<int>(std::min<int64_t>(kBldMaxTL, ((oe - ob + kBldRC - 1) / kBldRC) * kBldRC))
               : pick_tl(oe - ob, ndt * B, steps);
   a.out_begin = ob;
   a.out_end = oe;
+  a.y_quad_ok = quad_ok(out, dtype, B, D, L_local * D, D) ? 1 : 0;
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
-  a.use_tma = (!edge && make_map(&map, in, dtype, B, L_local, D, L_local * D, D)) ? 1 : 0;
+  a.use_tma =
+      (!edge && make_map(&map, in, dtype, B, L_local, D, L_local * D, D, backward ? kBldRC : kFwdRC)) ? 1 : 0;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (!backward) return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, oe - ob, st, map);
   const int64_t ntl = (oe - ob + a.TL - 1) / a.TL;

@@ -5,12 +5,12 @@
 // src/models/pde_layers.py:141,147/162,219):
 //     lap = (right - 2*mid) + left ;  y = mid + alpha * lap
 // `2*mid` is exact, so `right - 2*mid` rounded once equals fma(mid, -2, right).
-// Every other op is issued as its own round-to-nearest instruction
-// (__fadd2_rn / __fmul2_rn), never contracted, so the fp32 forward result is
-// bit-identical to the reference's CPU result.
+// Every other op is issued as its own round-to-nearest instruction (add2 /
+// mul2 below), never contracted, so the fp32 forward result is bit-identical
+// to the reference's CPU result.
 //
 // Two adjacent feature columns are processed together as one float2 with the
-// Blackwell packed-fp32 instructions (FADD2/FMUL2/FFMA2); each lane of a
+// Blackwell packed-fp32 instructions (add/mul/fma .f32x2); each half of a
 // packed op rounds exactly like the scalar op.
 #pragma once
 
@@ -65,36 +65,164 @@ template <> struct Elem<__half> {
 };
 
 // ---------------------------------------------------------------------------
-// packed fp32 stencil arithmetic
+// packed fp32 arithmetic.  Issued as PTX with an explicit .rn rounding
+// modifier: ptxas never contracts such instructions into a fused multiply-add,
+// which the reference's separately rounded ops require for bit-identical fp32.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// a * b + c with a single rounding
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // Non-causal update of the centre row c from rows l (i-1) and r (i+1).
 __device__ __forceinline__ float2 stencil_nc(float2 l, float2 c, float2 r, float2 al) {
-  float2 t = __ffma2_rn(c, f2(-2.f), r);  // r - 2c, one rounding (2c is exact)
-  t = __fadd2_rn(t, l);
-  t = __fmul2_rn(al, t);
-  return __fadd2_rn(c, t);
+  float2 t = fma2(c, f2(-2.f), r);  // r - 2c, one rounding (2c is exact)
+  t = add2(t, l);
+  t = mul2(al, t);
+  return add2(c, t);
 }
 
 // Causal update of row i (value c) from rows i-1 (p1) and i-2 (p2):
 // lap = (x[i] - 2 x[i-1]) + x[i-2] (src/models/pde_layers.py:141,145-147).
 __device__ __forceinline__ float2 stencil_c(float2 p2, float2 p1, float2 c, float2 al) {
-  float2 t = __ffma2_rn(p1, f2(-2.f), c);
-  t = __fadd2_rn(t, p2);
-  t = __fmul2_rn(al, t);
-  return __fadd2_rn(c, t);
+  float2 t = fma2(p1, f2(-2.f), c);
+  t = add2(t, p2);
+  t = mul2(al, t);
+  return add2(c, t);
 }
 
 // Laplacian only, same rounding sequence as above.
 __device__ __forceinline__ float2 lap3(float2 lo, float2 mid, float2 hi) {
-  float2 t = __ffma2_rn(mid, f2(-2.f), hi);
-  return __fadd2_rn(t, lo);
+  float2 t = fma2(mid, f2(-2.f), hi);
+  return add2(t, lo);
 }
 
 __device__ __forceinline__ float2 sel2(bool p, float2 a, float2 b) {
   return make_float2(p ? a.x : b.x, p ? a.y : b.y);
 }
+
+// ---------------------------------------------------------------------------
+// the same arithmetic on a pair held in ONE 64-bit register (pf2), so the
+// packed instructions never need pair-forming moves.
+// ---------------------------------------------------------------------------
+typedef unsigned long long pf2;
+
+__device__ __forceinline__ pf2 pk(float lo, float hi) {
+  pf2 d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void upk(pf2 v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ pf2 pbc(float a) { return pk(a, a); }
+__device__ __forceinline__ pf2 padd(pf2 a, pf2 b) {
+  pf2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ pf2 pmul(pf2 a, pf2 b) {
+  pf2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ pf2 pfma(pf2 a, pf2 b, pf2 c) {
+  pf2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// Rounded product a*b computed as fma(a, b, zn) with zn = -0.0 supplied at
+// run time.  -0 is the exact additive identity, so the result is round(a*b)
+// for every sign; because ptxas cannot see that zn is zero it can neither turn
+// this into a plain multiply nor contract it with the add that consumes it.
+// (ptxas fuses packed mul.rn.f32x2 -> add.rn.f32x2 pairs into one fma even
+// with -fmad=false; measured on B200, 148461 of 1M stencils differed.)
+__device__ __forceinline__ pf2 pmul_sep(pf2 a, pf2 b, pf2 zn) { return pfma(a, b, zn); }
+
+// non-causal update of centre c from l (row i-1) and r (row i+1); m2 = {-2,-2}
+__device__ __forceinline__ pf2 pst_nc(pf2 l, pf2 c, pf2 r, pf2 al, pf2 m2, pf2 zn) {
+  pf2 t = pfma(c, m2, r);  // r - 2c, one rounding (2c is exact)
+  t = padd(t, l);
+  t = pmul_sep(al, t, zn);
+  return padd(c, t);
+}
+// causal update of c (row i) from p1 (row i-1) and p2 (row i-2)
+__device__ __forceinline__ pf2 pst_c(pf2 p2, pf2 p1, pf2 c, pf2 al, pf2 m2, pf2 zn) {
+  pf2 t = pfma(p1, m2, c);
+  t = padd(t, p2);
+  t = pmul_sep(al, t, zn);
+  return padd(c, t);
+}
+// (hi - 2 mid) + lo
+__device__ __forceinline__ pf2 plap(pf2 lo, pf2 mid, pf2 hi, pf2 m2) { return padd(pfma(mid, m2, hi), lo); }
+__device__ __forceinline__ pf2 psel(bool p, pf2 a, pf2 b) { return p ? a : b; }
+
+// four consecutive columns <-> two pairs
+template <typename T> struct Quad;
+template <> struct Quad<__nv_bfloat16> {
+  using V = uint2;
+  __device__ __forceinline__ static pf2 w2p(uint32_t w) {
+    return pk(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
+  __device__ __forceinline__ static uint32_t p2w(pf2 p) {
+    float lo, hi;
+    upk(p, lo, hi);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static void split(V v, pf2& a, pf2& b) { a = w2p(v.x); b = w2p(v.y); }
+  __device__ __forceinline__ static V join(pf2 a, pf2 b) { return make_uint2(p2w(a), p2w(b)); }
+};
+template <> struct Quad<__half> {
+  using V = uint2;
+  __device__ __forceinline__ static pf2 w2p(uint32_t w) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    return pk(f.x, f.y);
+  }
+  __device__ __forceinline__ static uint32_t p2w(pf2 p) {
+    float lo, hi;
+    upk(p, lo, hi);
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static void split(V v, pf2& a, pf2& b) { a = w2p(v.x); b = w2p(v.y); }
+  __device__ __forceinline__ static V join(pf2 a, pf2 b) { return make_uint2(p2w(a), p2w(b)); }
+};
+template <> struct Quad<float> {
+  using V = float4;
+  __device__ __forceinline__ static void split(V v, pf2& a, pf2& b) { a = pk(v.x, v.y); b = pk(v.z, v.w); }
+  __device__ __forceinline__ static V join(pf2 a, pf2 b) {
+    float4 r;
+    upk(a, r.x, r.y);
+    upk(b, r.z, r.w);
+    return r;
+  }
+};
 
 // ---------------------------------------------------------------------------
 // shared-memory / mbarrier / TMA PTX wrappers

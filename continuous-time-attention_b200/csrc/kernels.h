@@ -20,6 +20,13 @@ constexpr int kBldDT = kBldThreads * kBldVec;  // 256 columns per CTA (TMA box i
 constexpr int kBldRC = 16;                    // rows per pipeline chunk
 constexpr int kBldStages = 4;                 // chunks in flight per CTA
 constexpr int kBldMaxTL = 2048;               // max output rows per CTA tile
+// forward kernel: 4 columns per thread (two packed pairs), 512-column tiles
+// fed by two 256-column TMA boxes per 8-row chunk
+constexpr int kFwdThreads = 128;
+constexpr int kFwdDT = 512;
+constexpr int kFwdRC = 8;
+constexpr int kFwdStages = 4;
+constexpr int kBoxCols = 256;                 // TMA box inner extent (max 256)
 constexpr int kBldMaxWords = (kBldMaxTL + 2 * 2 * kMaxSteps + kBldRC + 31) / 32 + 1;
 
 struct BldArgs {
@@ -49,6 +56,8 @@ struct BldArgs {
   int TL;
   int64_t out_begin, out_end;
   int use_tma;
+  int y_quad_ok;  // output rows allow aligned 4-column vector stores
+  float neg_zero;  // -0.0f: run-time additive identity (see pmul_sep)
   // per-step coefficients: host values, or device scalars when alpha_dev[k] != nullptr
   float alpha[kMaxSteps];
   const void* alpha_dev[kMaxSteps];
@@ -75,6 +84,7 @@ struct BdlArgs {
   int64_t L;
   int64_t in_rs, out_rs;  // row strides (elements)
   int vec_ok;             // 16-byte vector access is legal for every row
+  float neg_zero;         // -0.0f: run-time additive identity (see pmul_sep)
   const void* mask;
   int mask_dtype;
   int64_t msB, msL;
@@ -91,6 +101,7 @@ cudaError_t launch_bld_bwd(const BldArgs& a, const CUtensorMap* gmap, const CUte
 cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st);
 
 size_t bld_smem_bytes(int dtype, int with_x_stream);
+size_t fwd_smem_bytes(int dtype);
 int read_device_error_bld_fwd(int clear);
 int read_device_error_bld_bwd(int clear);
 int read_device_error_bdl(int clear);

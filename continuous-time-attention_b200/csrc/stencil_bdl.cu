@@ -106,16 +106,15 @@ __device__ __forceinline__ uint32_t fixed_bits(const BdlArgs& a, int64_t row, in
   return bits;
 }
 
-__device__ __forceinline__ float2 shfl_up2(float2 v, int d) {
-  return make_float2(__shfl_up_sync(0xffffffffu, v.x, d), __shfl_up_sync(0xffffffffu, v.y, d));
-}
-__device__ __forceinline__ float2 shfl_down2(float2 v, int d) {
-  return make_float2(__shfl_down_sync(0xffffffffu, v.x, d), __shfl_down_sync(0xffffffffu, v.y, d));
-}
+__device__ __forceinline__ pf2 shfl_up_p(pf2 v, int d) { return __shfl_up_sync(0xffffffffu, v, d); }
+__device__ __forceinline__ pf2 shfl_down_p(pf2 v, int d) { return __shfl_down_sync(0xffffffffu, v, d); }
 
 // select per packed half: keep `keep` where the fixed bit of that window is set
-__device__ __forceinline__ float2 sel_fixed(uint32_t fa, uint32_t fb, int i, float2 keep, float2 upd) {
-  return make_float2(((fa >> i) & 1u) ? keep.x : upd.x, ((fb >> i) & 1u) ? keep.y : upd.y);
+__device__ __forceinline__ pf2 sel_fixed(uint32_t fa, uint32_t fb, int i, pf2 keep, pf2 upd) {
+  float k0, k1, u0, u1;
+  upk(keep, k0, k1);
+  upk(upd, u0, u1);
+  return pk(((fa >> i) & 1u) ? k0 : u0, ((fb >> i) & 1u) ? k1 : u1);
 }
 
 }  // namespace
@@ -125,6 +124,7 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
   // halo lanes: the one-sided causal stencil reaches 2*S <= 16 positions to
   // the left (forward) or right (adjoint); the centred one S <= 8 each side.
   constexpr int HLN = CAUSAL ? (BWD ? 0 : 2) : 1;
+  constexpr int HRN = CAUSAL ? (BWD ? 2 : 0) : 1;
   const int lane = threadIdx.x & 31;
   const int64_t nwin = (a.L + kBdlOut - 1) / kBdlOut;
   const int64_t total = a.rows * nwin;
@@ -143,9 +143,10 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
 #pragma unroll
     for (int i = 0; i < E8; ++i) vbv[i] = 0.f;
   }
-  float2 e[E8];
+  // window A in the low half, window B in the high half of every pair
+  pf2 e[E8];
 #pragma unroll
-  for (int i = 0; i < E8; ++i) e[i] = make_float2(va[i], vbv[i]);
+  for (int i = 0; i < E8; ++i) e[i] = pk(va[i], vbv[i]);
 
   const uint32_t fa = fixed_bits<CAUSAL>(a, ra, pa, true);
   const uint32_t fb = fixed_bits<CAUSAL>(a, rbw, pb, vb);
@@ -155,58 +156,60 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
 #pragma unroll
   for (int k = 0; k < kMaxSteps; ++k)
     if (k < S) al[k] = a.alpha_dev[k] != nullptr ? load_scalar(a.alpha_dev[k], a.alpha_dev_dtype) : a.alpha[k];
+  const pf2 m2 = pbc(-2.f);
+  const pf2 zn = pbc(a.neg_zero);
 
   auto run = [&](auto slow_tag) {
     constexpr bool SLOW = decltype(slow_tag)::value;
 #pragma unroll
     for (int s = 0; s < S; ++s) {
       if (!BWD) {
-        const float2 alv = f2(al[s]);
-        float2 n[E8];
+        const pf2 alv = pbc(al[s]);
+        pf2 n[E8];
         if (CAUSAL) {
-          const float2 m2 = shfl_up2(e[E8 - 2], 1), m1 = shfl_up2(e[E8 - 1], 1);
+          const pf2 m2n = shfl_up_p(e[E8 - 2], 1), m1n = shfl_up_p(e[E8 - 1], 1);
 #pragma unroll
           for (int i = 0; i < E8; ++i) {
-            const float2 p2 = i >= 2 ? e[i - 2] : (i == 1 ? m1 : m2);
-            const float2 p1 = i >= 1 ? e[i - 1] : m1;
-            n[i] = stencil_c(p2, p1, e[i], alv);
+            const pf2 p2 = i >= 2 ? e[i - 2] : (i == 1 ? m1n : m2n);
+            const pf2 p1 = i >= 1 ? e[i - 1] : m1n;
+            n[i] = pst_c(p2, p1, e[i], alv, m2, zn);
           }
         } else {
-          const float2 lft = shfl_up2(e[E8 - 1], 1), rgt = shfl_down2(e[0], 1);
+          const pf2 lft = shfl_up_p(e[E8 - 1], 1), rgt = shfl_down_p(e[0], 1);
 #pragma unroll
           for (int i = 0; i < E8; ++i) {
-            const float2 l = i > 0 ? e[i - 1] : lft;
-            const float2 r = i < E8 - 1 ? e[i + 1] : rgt;
-            n[i] = stencil_nc(l, e[i], r, alv);
+            const pf2 l = i > 0 ? e[i - 1] : lft;
+            const pf2 r = i < E8 - 1 ? e[i + 1] : rgt;
+            n[i] = pst_nc(l, e[i], r, alv, m2, zn);
           }
         }
 #pragma unroll
         for (int i = 0; i < E8; ++i) e[i] = SLOW ? sel_fixed(fa, fb, i, e[i], n[i]) : n[i];
       } else {
-        // adjoint of forward step S-1-s
-        const float2 alv = f2(al[S - 1 - s]);
-        float2 av[E8];
+        // adjoint of forward step S-1-s: a = alpha * g on updated positions
+        const pf2 alv = pbc(al[S - 1 - s]);
+        pf2 av[E8];
 #pragma unroll
         for (int i = 0; i < E8; ++i) {
-          av[i] = __fmul2_rn(alv, e[i]);
-          if (SLOW) av[i] = sel_fixed(fa, fb, i, f2(0.f), av[i]);
+          av[i] = pmul(alv, e[i]);
+          if (SLOW) av[i] = sel_fixed(fa, fb, i, 0ull, av[i]);
         }
         if (CAUSAL) {
-          const float2 q1 = shfl_down2(av[0], 1), q2 = shfl_down2(av[1], 1);
+          const pf2 q1 = shfl_down_p(av[0], 1), q2 = shfl_down_p(av[1], 1);
 #pragma unroll
           for (int i = 0; i < E8; ++i) {
-            const float2 a1 = i + 1 < E8 ? av[i + 1] : (i + 1 == E8 ? q1 : q2);
-            const float2 a2 = i + 2 < E8 ? av[i + 2] : (i + 2 == E8 ? q1 : q2);
-            e[i] = __fadd2_rn(e[i], lap3(a2, a1, av[i]));  // (a[i] - 2a[i+1]) + a[i+2]
+            const pf2 a1 = i + 1 < E8 ? av[i + 1] : (i + 1 == E8 ? q1 : q2);
+            const pf2 a2 = i + 2 < E8 ? av[i + 2] : (i + 2 == E8 ? q1 : q2);
+            e[i] = padd(e[i], plap(a2, a1, av[i], m2));  // (a[i] - 2a[i+1]) + a[i+2]
           }
         } else {
-          const float2 lft = shfl_up2(av[E8 - 1], 1), rgt = shfl_down2(av[0], 1);
-          float2 n[E8];
+          const pf2 lft = shfl_up_p(av[E8 - 1], 1), rgt = shfl_down_p(av[0], 1);
+          pf2 n[E8];
 #pragma unroll
           for (int i = 0; i < E8; ++i) {
-            const float2 l = i > 0 ? av[i - 1] : lft;
-            const float2 r = i < E8 - 1 ? av[i + 1] : rgt;
-            n[i] = __fadd2_rn(e[i], lap3(l, av[i], r));
+            const pf2 l = i > 0 ? av[i - 1] : lft;
+            const pf2 r = i < E8 - 1 ? av[i + 1] : rgt;
+            n[i] = padd(e[i], plap(l, av[i], r, m2));
           }
 #pragma unroll
           for (int i = 0; i < E8; ++i) e[i] = n[i];
@@ -217,13 +220,9 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
   if (slow) run(std::true_type{});
   else run(std::false_type{});
 
-  const int hrn = CAUSAL ? (BWD ? 2 : 0) : 1;
-  if (lane >= HLN && lane < 32 - hrn) {
+  if (lane >= HLN && lane < 32 - HRN) {
 #pragma unroll
-    for (int i = 0; i < E8; ++i) {
-      va[i] = e[i].x;
-      vbv[i] = e[i].y;
-    }
+    for (int i = 0; i < E8; ++i) upk(e[i], va[i], vbv[i]);
     store_window<T>(a, ra, pa, va);
     if (vb) store_window<T>(a, rbw, pb, vbv);
   }

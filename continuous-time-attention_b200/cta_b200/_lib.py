@@ -113,19 +113,56 @@ def mask_code(dt: torch.dtype) -> int:
         raise ValueError(f"unsupported attention_mask dtype {dt}") from None
 
 
-def stream_ptr(t: torch.Tensor) -> c_void_p:
-    return c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
-def ptr(t: torch.Tensor | None) -> c_void_p:
-    return c_void_p(t.data_ptr() if t is not None else 0)
+def stream_ptr(t: torch.Tensor) -> int:
+    """The caller's current CUDA stream on t's device, as a raw cudaStream_t."""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index)
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int:
+    return t.data_ptr() if t is not None else 0
+
+
+_float_arrays: dict = {}
 
 
 def float_array(vals) -> ctypes.Array:
-    arr = (c_float * MAX_STEPS)()
-    for i, v in enumerate(vals):
-        arr[i] = float(v)
+    """ctypes float[8] of the given host coefficients (cached, treat as read-only)."""
+    key = tuple(float(v) for v in vals)
+    arr = _float_arrays.get(key)
+    if arr is None:
+        arr = (c_float * MAX_STEPS)()
+        for i, v in enumerate(key):
+            arr[i] = v
+        if len(_float_arrays) < 4096:
+            _float_arrays[key] = arr
     return arr
+
+
+class on_device:
+    """Make t's device current for the call (no-op when it already is)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, t: torch.Tensor):
+        self.idx = t.device.index
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
 
 
 def ptr_array(tensors) -> ctypes.Array:

@@ -33,6 +33,8 @@ CFLAGS = [
     "-lineinfo",
     "-std=c++17",
     "--expt-relaxed-constexpr",
+    # no contraction: every fused multiply-add in the kernels is written explicitly
+    "-fmad=false",
     "-Xcompiler",
     "-fPIC",
     "-Xcompiler",

@@ -86,7 +86,7 @@ def bdl(
     fa, pa, pcode, keep = _alpha_args(alphas, steps, x.device)
     m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
     lib = _lib.load()
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         rc = lib.cta_diffusion_bdl_ex(
             _lib.ptr(x), _lib.ptr(y), B, D, L, x.stride(1), y.stride(1), _lib.dtype_code(x.dtype), steps,
             int(causal), int(backward), fa, pa, pcode, _lib.ptr(m), mcode, msb, msl, _lib.stream_ptr(x),
@@ -105,7 +105,7 @@ def bdl_simple(x: torch.Tensor, alpha: float, steps: int, backward: bool = False
     y = torch.empty_like(x)
     lib = _lib.load()
     fn = lib.cta_diffusion_bwd_bdl if backward else lib.cta_diffusion_fwd_bdl
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         rc = fn(_lib.ptr(x), _lib.ptr(y), B, D, L, L, _lib.dtype_code(x.dtype), steps, float(alpha),
                 _lib.stream_ptr(x))
     _lib.check(rc)
@@ -140,7 +140,7 @@ def bld_forward(
     fa, pa, pcode, keep = _alpha_args(alphas, steps, x.device)
     m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
     lib = _lib.load()
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         rc = lib.cta_diffusion_fwd_bld(
             _lib.ptr(x), _lib.ptr(y), B, L, D, x.stride(0), x.stride(1), y.stride(0), y.stride(1),
             _lib.dtype_code(x.dtype), steps, int(causal), fa, pa, pcode, _lib.ptr(m), mcode, msb, msl,
@@ -200,7 +200,7 @@ def bld_backward(
         ws_bytes = int(lib.cta_diffusion_bwd_bld_workspace_bytes(B, L, D, _lib.dtype_code(g.dtype), steps,
                                                                  int(causal)))
         ws = _workspace(g.device, ws_bytes)
-    with torch.cuda.device(g.device):
+    with _lib.on_device(g):
         rc = lib.cta_diffusion_bwd_bld(
             _lib.ptr(g), _lib.ptr(dx), _lib.ptr(xs), _lib.ptr(dalpha), _lib.ptr(ws), ws_bytes, B, L, D,
             g.stride(0), g.stride(1), xs.stride(0) if xs is not None else 0, xs.stride(1) if xs is not None else 0,
@@ -238,7 +238,7 @@ def varlen_forward(
     y = torch.empty((T, D), dtype=x.dtype, device=x.device) if out is None else out
     nseq = cu_seqlens.numel() - 1
     lib = _lib.load()
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         rc = lib.cta_diffusion_fwd_varlen(
             _lib.ptr(x), _lib.ptr(y), T, D, x.stride(0), y.stride(0), _lib.ptr(cu_seqlens), nseq, int(max_len),
             int(pad_to_max), _lib.dtype_code(x.dtype), steps, float(alpha), _lib.stream_ptr(x),
@@ -271,10 +271,10 @@ def shard_part(
     hi_rows = hi_halo.shape[1] if hi_halo is not None else 0
     st = stream if stream is not None else torch.cuda.current_stream(x_local.device)
     lib = _lib.load()
-    with torch.cuda.device(x_local.device):
+    with _lib.on_device(x_local):
         rc = lib.cta_diffusion_shard_bld(
             _lib.ptr(x_local), _lib.ptr(out), B, Lloc, D, int(pos_offset), int(global_len), _lib.ptr(lo_halo),
             lo_rows, _lib.ptr(hi_halo), hi_rows, int(part), _lib.dtype_code(x_local.dtype), steps, int(causal),
-            int(backward), float(alpha), _lib.c_void_p(st.cuda_stream),
+            int(backward), float(alpha), st.cuda_stream,
         )
     _lib.check(rc)

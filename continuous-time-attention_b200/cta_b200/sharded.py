@@ -56,6 +56,22 @@ def halo_rows(steps: int, causal: bool, backward: bool) -> tuple[int, int]:
     return steps, steps
 
 
+def partition(spec: ShardSpec, steps: int, causal: bool, backward: bool) -> dict[int, tuple[int, int]]:
+    """Local output rows of each launch part, {part: (begin, end)}.
+
+    Interior rows are those whose stencil reach stays inside the shard (or
+    runs off a global end); the edge parts are the rest.  The same rule is
+    applied by cta_diffusion_shard_bld in the C ABI.
+    """
+    hl, hr = halo_rows(steps, causal, backward)
+    L = spec.local_len
+    has_lo = spec.pos_offset > 0
+    has_hi = spec.pos_offset + L < spec.global_len
+    ib = min(hl, L) if has_lo else 0
+    ie = max(L - hr, ib) if has_hi else L
+    return {_lib.SHARD_INTERIOR: (ib, ie), _lib.SHARD_LO_EDGE: (0, ib), _lib.SHARD_HI_EDGE: (ie, L)}
+
+
 def _default_compute(part, x_local, out, *, lo_halo, hi_halo, spec, alpha, steps, causal, backward):
     from . import ops
 

@@ -30,7 +30,10 @@ def test_layer_chain_matches_reference_golden(golden):
         (y.float() * c["g"].cuda().float()).sum().backward()
         assert_close(x.grad, c["dx"])
         da = torch.cat([l.alpha.grad for l in layers]).cpu()
-        assert (da - c["dalpha"]).abs().max().item() <= 1e-4 * max(1.0, c["dalpha"].abs().max().item())
+        # d(alpha) is a reduction: relative bar; in bf16 every layer's input gradient is
+        # rounded to bf16 (as in the reference), so earlier layers inherit 1-ulp differences
+        rel = 1e-4 if c["x"].dtype == torch.float32 else 2e-2
+        assert (da - c["dalpha"]).abs().max().item() <= rel * max(1.0, c["dalpha"].abs().max().item())
 
 
 @pytest.mark.parametrize("layout", ["bld", "bdl"])
