@@ -61,16 +61,23 @@ __device__ void fill_fwd_chunk(const BldArgs& a, const Seg& s, int64_t jrow0, in
 
 template <typename T, int S, bool CAUSAL>
 __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                              const __grid_constant__ CUtensorMap ymap,
                                                               const BldArgs a) {
   using Q = Quad<T>;
   using V = typename Q::V;
   constexpr int HL = CAUSAL ? 2 * S : S;  // halo rows above the tile
-  constexpr int LAG = 2 * S;              // march rows before the first output row
-  constexpr int CHUNK = kFwdRC * kFwdDT;  // elements per pipeline slot
+  constexpr int LAG = 2 * S;              // wavefront depth: march rows before the first finished row
+  // extra leading rows so that output rows start on a chunk boundary
+  constexpr int PAD = (kFwdRC - LAG % kFwdRC) % kFwdRC;
+  constexpr int PRO = PAD + LAG;  // prologue rows (no output), a multiple of kFwdRC
+  constexpr int NPRO = PRO / kFwdRC;
+  constexpr int CHUNK = kFwdRC * kFwdDT;   // elements per pipeline slot
   constexpr int BOXE = kFwdRC * kBoxCols;  // elements per TMA box
+  static_assert(NPRO >= 1 && NPRO <= 2, "prologue spans one or two chunks");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   T* ring = reinterpret_cast<T*>(smem_raw);
+  T* stage = ring + kFwdStages * CHUNK;  // output staging for the TMA stores
   __shared__ __align__(8) uint64_t full_bar[kFwdStages];
   __shared__ uint32_t fbits[kBldMaxWords + 2];
   __shared__ uint32_t zbits[kBldMaxWords + 2];
@@ -80,16 +87,18 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
   const int64_t oend = a.out_end < sg.n ? a.out_end : sg.n;
   if (l0 >= oend) return;
   const int d0 = blockIdx.y * kFwdDT;
-  const int64_t jb = l0 - HL;
+  const int64_t jb = l0 - HL - PAD;  // first march row
   const int nout = static_cast<int>(oend - l0 < a.TL ? oend - l0 : a.TL);
-  const int nrows = nout + LAG;
+  const int nrows = PRO + nout;
   const int nch = (nrows + kFwdRC - 1) / kFwdRC;
   const int tid = threadIdx.x;
   const bool use_tma = a.use_tma != 0;
+  const bool tstore = a.use_tma_store != 0;
   const int nbox = (d0 + kBoxCols < a.D) ? 2 : 1;
 
   if (tid == 0) {
     if (use_tma) prefetch_tmap(&xmap);
+    if (tstore) prefetch_tmap(&ymap);
 #pragma unroll
     for (int s = 0; s < kFwdStages; ++s) mbar_init(&full_bar[s], 1);
     fence_mbar_init();
@@ -116,7 +125,7 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
   const pf2 m2 = pbc(-2.f);
   const pf2 zn = pbc(a.neg_zero);
 
-  // per-level state: rows (lag+2, lag+1) behind the newest, for both pairs
+  // per-level state: the level's input on the two previous march rows, for both pairs
   pf2 P1a[S], P2a[S], P1b[S], P2b[S];
 #pragma unroll
   for (int k = 0; k < S; ++k) P1a[k] = P2a[k] = P1b[k] = P2b[k] = 0ull;
@@ -144,9 +153,12 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
     }
   };
 
-  // one march row: input (xa, xb) of march row t; returns level-S values
-  auto step_row = [&](auto slow_tag, int64_t j, pf2& xa, pf2& xb) {
+  // One march row.  TCT >= 0 is the compile-time march row of a prologue row:
+  // level k there is only computed once its inputs are valid (TCT >= 2k + 2),
+  // so the start-up triangle of the wavefront costs nothing.
+  auto step_row = [&](auto slow_tag, auto tct_tag, int64_t j, pf2& xa, pf2& xb) {
     constexpr bool SLOW = decltype(slow_tag)::value;
+    constexpr int TCT = decltype(tct_tag)::value;
     if (SLOW) {
       if (rb.zero(j)) xa = xb = 0ull;
     }
@@ -154,11 +166,14 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
       const bool fx = SLOW && rb.fixed(j);
 #pragma unroll
       for (int k = 0; k < S; ++k) {
-        pf2 na = pst_c(P2a[k], P1a[k], xa, al[k], m2, zn);
-        pf2 nb = pst_c(P2b[k], P1b[k], xb, al[k], m2, zn);
-        if (SLOW) {
-          na = psel(fx, xa, na);
-          nb = psel(fx, xb, nb);
+        pf2 na = xa, nb = xb;
+        if (TCT < 0 || TCT >= 2 * k + 2) {
+          na = pst_c(P2a[k], P1a[k], xa, al[k], m2, zn);
+          nb = pst_c(P2b[k], P1b[k], xb, al[k], m2, zn);
+          if (SLOW) {
+            na = psel(fx, xa, na);
+            nb = psel(fx, xb, nb);
+          }
         }
         P2a[k] = P1a[k];
         P1a[k] = xa;
@@ -172,12 +187,15 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
       const uint32_t fw = SLOW ? rb.window8_fixed(j - S) : 0u;
 #pragma unroll
       for (int k = 0; k < S; ++k) {
-        pf2 na = pst_nc(P2a[k], P1a[k], xa, al[k], m2, zn);
-        pf2 nb = pst_nc(P2b[k], P1b[k], xb, al[k], m2, zn);
-        if (SLOW) {
-          const bool fx = (fw >> (S - 1 - k)) & 1u;
-          na = psel(fx, P1a[k], na);
-          nb = psel(fx, P1b[k], nb);
+        pf2 na = xa, nb = xb;
+        if (TCT < 0 || TCT >= 2 * k + 2) {
+          na = pst_nc(P2a[k], P1a[k], xa, al[k], m2, zn);
+          nb = pst_nc(P2b[k], P1b[k], xb, al[k], m2, zn);
+          if (SLOW) {
+            const bool fx = (fw >> (S - 1 - k)) & 1u;
+            na = psel(fx, P1a[k], na);
+            nb = psel(fx, P1b[k], nb);
+          }
         }
         P2a[k] = P1a[k];
         P1a[k] = xa;
@@ -189,97 +207,131 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
     }
   };
 
-  auto march_chunk = [&](auto slow_tag, int c, const T* buf) {
+  // kind: 0..NPRO-1 = prologue chunk, NPRO = full output chunk, NPRO+1 = partial last chunk
+  auto march_chunk = [&](auto slow_tag, auto kind_tag, int c, const T* buf) {
+    constexpr int KIND = decltype(kind_tag)::value;
     const int t0 = c * kFwdRC;
-    // chunks whose every row is an output row store without per-row checks
-    const bool all_store = t0 >= LAG && t0 + kFwdRC <= LAG + nout;
     V in[kFwdRC];
 #pragma unroll
     for (int i = 0; i < kFwdRC; ++i) in[i] = *reinterpret_cast<const V*>(buf + soff + i * kBoxCols);
-#pragma unroll
-    for (int i = 0; i < kFwdRC; ++i) {
+    T* st = stage + ((c - NPRO) & 1) * CHUNK + soff;
+    static_for<kFwdRC>([&](auto I) {
+      constexpr int i = decltype(I)::value;
       pf2 xa, xb;
       Q::split(in[i], xa, xb);
-      step_row(slow_tag, jb + t0 + i, xa, xb);
-      const int t = t0 + i;
-      if (all_store || (t >= LAG && t < LAG + nout)) store_row(l0 + t - LAG, xa, xb);
-    }
+      if constexpr (KIND < NPRO) {
+        step_row(slow_tag, std::integral_constant<int, KIND * kFwdRC + i>{}, jb + t0 + i, xa, xb);
+      } else {
+        step_row(slow_tag, std::integral_constant<int, -1>{}, jb + t0 + i, xa, xb);
+        const int64_t orow = l0 + t0 + i - PRO;
+        if constexpr (KIND == NPRO) {
+          if (tstore) *reinterpret_cast<V*>(st + i * kBoxCols) = Q::join(xa, xb);
+          else store_row(orow, xa, xb);
+        } else {
+          if (t0 + i < nrows) store_row(orow, xa, xb);
+        }
+      }
+    });
   };
 
   int err = 0;
   for (int c = 0; c < nch; ++c) {
     const int slot = c % kFwdStages;
-    T* buf = ring + slot * CHUNK;
+    const T* buf = ring + slot * CHUNK;
     if (use_tma) {
       if (!mbar_wait_bounded(&full_bar[slot], (c / kFwdStages) & 1)) err = 1;
     } else {
-      fill_fwd_chunk<T>(a, sg, jb + c * kFwdRC, d0, buf);
+      fill_fwd_chunk<T>(a, sg, jb + c * kFwdRC, d0, ring + slot * CHUNK);
       __syncthreads();
     }
+    const bool full = c >= NPRO && (c + 1) * kFwdRC <= nrows;
     if (!err) {
-      if (slow) march_chunk(std::true_type{}, c, buf);
-      else march_chunk(std::false_type{}, c, buf);
+      auto dispatch = [&](auto slow_tag) {
+        if (c == 0) march_chunk(slow_tag, std::integral_constant<int, 0>{}, c, buf);
+        else if (NPRO > 1 && c == 1) march_chunk(slow_tag, std::integral_constant<int, (NPRO > 1 ? 1 : 0)>{}, c, buf);
+        else if (full) march_chunk(slow_tag, std::integral_constant<int, NPRO>{}, c, buf);
+        else march_chunk(slow_tag, std::integral_constant<int, NPRO + 1>{}, c, buf);
+      };
+      if (slow) dispatch(std::true_type{});
+      else dispatch(std::false_type{});
     }
+    const bool tma_out = tstore && full;
+    if (tma_out) fence_proxy_async_smem();
+    // the store issued after the previous chunk must have finished reading the
+    // staging slot that the next chunk will overwrite
+    if (tstore && tid == 0) bulk_wait_read_all();
     if (__syncthreads_or(err)) {
       if (tid == 0) {
         atomicExch(&g_bld_fwd_error, kDevTimeout);
-        // drain (bounded) every load still in flight before the CTA exits
+        // drain (bounded) every load still in flight, and the stores, before the CTA exits
         if (use_tma)
           for (int cc = c; cc < nch && cc < c + kFwdStages; ++cc)
             mbar_wait_bounded(&full_bar[cc % kFwdStages], (cc / kFwdStages) & 1);
+        if (tstore) bulk_wait_all();
       }
       __syncthreads();
       return;
     }
-    if (use_tma && tid == 0 && c + kFwdStages < nch) issue(c + kFwdStages);
+    if (tid == 0) {
+      if (tma_out) {
+        const int orow0 = static_cast<int>(sg.row0 + l0 + c * kFwdRC - PRO);
+        const T* src = stage + ((c - NPRO) & 1) * CHUNK;
+        for (int b = 0; b < nbox; ++b) tma_store_3d(&ymap, src + b * BOXE, d0 + b * kBoxCols, orow0, sg.bcoord);
+        bulk_commit();
+      }
+      if (use_tma && c + kFwdStages < nch) issue(c + kFwdStages);
+    }
   }
+  if (tstore && tid == 0) bulk_wait_all();
 }
 
 size_t fwd_smem_bytes(int dtype) {
   const size_t es = dtype == kF32 ? 4 : 2;
-  return static_cast<size_t>(kFwdStages) * kFwdRC * kFwdDT * es;
+  return static_cast<size_t>(kFwdStages + kFwdOutSlots) * kFwdRC * kFwdDT * es;
 }
 
 namespace {
 
 template <typename T, int S, bool CAUSAL>
-cudaError_t launch_fwd_t(const BldArgs& a, const CUtensorMap* xmap, dim3 grid, size_t smem, cudaStream_t st) {
+cudaError_t launch_fwd_t(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, dim3 grid, size_t smem,
+                         cudaStream_t st) {
   auto kern = bld_fwd_kernel<T, S, CAUSAL>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, kFwdThreads, smem, st>>>(*xmap, a);
+  kern<<<grid, kFwdThreads, smem, st>>>(*xmap, *ymap, a);
   return cudaGetLastError();
 }
 
 template <typename T, bool CAUSAL>
-cudaError_t fwd_steps(const BldArgs& a, const CUtensorMap* m, int steps, dim3 g, size_t sm, cudaStream_t st) {
+cudaError_t fwd_steps(const BldArgs& a, const CUtensorMap* m, const CUtensorMap* ym, int steps, dim3 g, size_t sm,
+                      cudaStream_t st) {
   switch (steps) {
-    case 1: return launch_fwd_t<T, 1, CAUSAL>(a, m, g, sm, st);
-    case 2: return launch_fwd_t<T, 2, CAUSAL>(a, m, g, sm, st);
-    case 3: return launch_fwd_t<T, 3, CAUSAL>(a, m, g, sm, st);
-    case 4: return launch_fwd_t<T, 4, CAUSAL>(a, m, g, sm, st);
-    case 5: return launch_fwd_t<T, 5, CAUSAL>(a, m, g, sm, st);
-    case 6: return launch_fwd_t<T, 6, CAUSAL>(a, m, g, sm, st);
-    case 7: return launch_fwd_t<T, 7, CAUSAL>(a, m, g, sm, st);
-    case 8: return launch_fwd_t<T, 8, CAUSAL>(a, m, g, sm, st);
+    case 1: return launch_fwd_t<T, 1, CAUSAL>(a, m, ym, g, sm, st);
+    case 2: return launch_fwd_t<T, 2, CAUSAL>(a, m, ym, g, sm, st);
+    case 3: return launch_fwd_t<T, 3, CAUSAL>(a, m, ym, g, sm, st);
+    case 4: return launch_fwd_t<T, 4, CAUSAL>(a, m, ym, g, sm, st);
+    case 5: return launch_fwd_t<T, 5, CAUSAL>(a, m, ym, g, sm, st);
+    case 6: return launch_fwd_t<T, 6, CAUSAL>(a, m, ym, g, sm, st);
+    case 7: return launch_fwd_t<T, 7, CAUSAL>(a, m, ym, g, sm, st);
+    case 8: return launch_fwd_t<T, 8, CAUSAL>(a, m, ym, g, sm, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <typename T>
-cudaError_t fwd_dtype(const BldArgs& a, const CUtensorMap* m, int steps, int causal, dim3 g, size_t sm,
-                      cudaStream_t st) {
-  return causal ? fwd_steps<T, true>(a, m, steps, g, sm, st) : fwd_steps<T, false>(a, m, steps, g, sm, st);
+cudaError_t fwd_dtype(const BldArgs& a, const CUtensorMap* m, const CUtensorMap* ym, int steps, int causal, dim3 g,
+                      size_t sm, cudaStream_t st) {
+  return causal ? fwd_steps<T, true>(a, m, ym, steps, g, sm, st) : fwd_steps<T, false>(a, m, ym, steps, g, sm, st);
 }
 
 }  // namespace
 
-cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, int dtype, int steps, int causal, dim3 grid,
-                           size_t smem, cudaStream_t st) {
+cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, int dtype, int steps,
+                           int causal, dim3 grid, size_t smem, cudaStream_t st) {
   switch (dtype) {
-    case kF32: return fwd_dtype<float>(a, xmap, steps, causal, grid, smem, st);
-    case kBF16: return fwd_dtype<__nv_bfloat16>(a, xmap, steps, causal, grid, smem, st);
-    case kF16: return fwd_dtype<__half>(a, xmap, steps, causal, grid, smem, st);
+    case kF32: return fwd_dtype<float>(a, xmap, ymap, steps, causal, grid, smem, st);
+    case kBF16: return fwd_dtype<__nv_bfloat16>(a, xmap, ymap, steps, causal, grid, smem, st);
+    case kF16: return fwd_dtype<__half>(a, xmap, ymap, steps, causal, grid, smem, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -200,7 +200,7 @@ bool quad_ok(const void* y, int dtype, int64_t nb, int64_t D, int64_t sB, int64_
 }
 
 int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int64_t tile_rows, cudaStream_t st,
-               const CUtensorMap& xmap) {
+               const CUtensorMap& xmap, const CUtensorMap& ymap) {
   const int64_t ntl = (tile_rows + a.TL - 1) / a.TL;
   const int64_t ndt = (a.D + kFwdDT - 1) / kFwdDT;
   if (ntl <= 0 || nbatch <= 0) return ok();
@@ -208,7 +208,7 @@ int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int
     return fail(CTA_EUNSUPPORTED, "grid too large (tiles %lld, D tiles %lld, batch %lld)", (long long)ntl,
                 (long long)ndt, (long long)nbatch);
   dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(nbatch));
-  const cudaError_t e = launch_bld_fwd(a, &xmap, dtype, steps, causal, grid, fwd_smem_bytes(dtype), st);
+  const cudaError_t e = launch_bld_fwd(a, &xmap, &ymap, dtype, steps, causal, grid, fwd_smem_bytes(dtype), st);
   if (e != cudaSuccess) return cuda_fail(e, "bld forward launch");
   return ok();
 }
@@ -349,10 +349,12 @@ int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t 
   a.out_begin = 0;
   a.out_end = L;
   a.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
-  CUtensorMap xmap;
+  CUtensorMap xmap, ymap;
   std::memset(&xmap, 0, sizeof(xmap));
+  std::memset(&ymap, 0, sizeof(ymap));
   a.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC) ? 1 : 0;
-  return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), xmap);
+  a.use_tma_store = make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC) ? 1 : 0;
+  return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), xmap, ymap);
 }
 
 int64_t cta_diffusion_bwd_bld_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype, int steps, int causal) {
@@ -469,10 +471,12 @@ int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t
   a.out_begin = 0;
   a.out_end = max_len;
   a.y_quad_ok = quad_ok(y, dtype, 1, D, 0, y_sL) ? 1 : 0;
-  CUtensorMap xmap;
+  CUtensorMap xmap, ymap;
   std::memset(&xmap, 0, sizeof(xmap));
+  std::memset(&ymap, 0, sizeof(ymap));
   a.use_tma = make_map(&xmap, x, dtype, 1, total_rows, D, 0, x_sL, kFwdRC) ? 1 : 0;
-  return launch_fwd(a, dtype, steps, 0, nseq, max_len, static_cast<cudaStream_t>(stream), xmap);
+  a.use_tma_store = make_map(&ymap, y, dtype, 1, total_rows, D, 0, y_sL, kFwdRC) ? 1 : 0;
+  return launch_fwd(a, dtype, steps, 0, nseq, max_len, static_cast<cudaStream_t>(stream), xmap, ymap);
 }
 
 int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_local, int64_t D, int64_t pos_offset,
@@ -540,12 +544,16 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
   a.out_begin = ob;
   a.out_end = oe;
   a.y_quad_ok = quad_ok(out, dtype, B, D, L_local * D, D) ? 1 : 0;
-  CUtensorMap map;
+  CUtensorMap map, omap;
   std::memset(&map, 0, sizeof(map));
+  std::memset(&omap, 0, sizeof(omap));
   a.use_tma =
       (!edge && make_map(&map, in, dtype, B, L_local, D, L_local * D, D, backward ? kBldRC : kFwdRC)) ? 1 : 0;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (!backward) return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, oe - ob, st, map);
+  if (!backward) {
+    a.use_tma_store = make_map(&omap, out, dtype, B, L_local, D, L_local * D, D, kFwdRC) ? 1 : 0;
+    return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, oe - ob, st, map, omap);
+  }
   const int64_t ntl = (oe - ob + a.TL - 1) / a.TL;
   if (ntl > 0x7fffffffLL || ndt > 65535 || B > 65535) return fail(CTA_EUNSUPPORTED, "grid too large");
   dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(B));

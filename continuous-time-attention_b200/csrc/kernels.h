@@ -25,7 +25,8 @@ constexpr int kBldMaxTL = 2048;               // max output rows per CTA tile
 constexpr int kFwdThreads = 128;
 constexpr int kFwdDT = 512;
 constexpr int kFwdRC = 8;
-constexpr int kFwdStages = 4;
+constexpr int kFwdStages = 3;    // input chunks in flight
+constexpr int kFwdOutSlots = 2;  // output staging chunks for the TMA stores
 constexpr int kBoxCols = 256;                 // TMA box inner extent (max 256)
 constexpr int kBldMaxWords = (kBldMaxTL + 2 * 2 * kMaxSteps + kBldRC + 31) / 32 + 1;
 
@@ -57,6 +58,7 @@ struct BldArgs {
   int64_t out_begin, out_end;
   int use_tma;
   int y_quad_ok;  // output rows allow aligned 4-column vector stores
+  int use_tma_store;  // the output tensor map is valid: full chunks leave through TMA stores
   float neg_zero;  // -0.0f: run-time additive identity (see pmul_sep)
   // per-step coefficients: host values, or device scalars when alpha_dev[k] != nullptr
   float alpha[kMaxSteps];
@@ -94,8 +96,8 @@ struct BdlArgs {
 };
 
 // launchers (return cudaError_t of the launch)
-cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, int dtype, int steps, int causal,
-                           dim3 grid, size_t smem, cudaStream_t st);
+cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, int dtype,
+                           int steps, int causal, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bld_bwd(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap, int dtype,
                            int steps, int causal, int with_dalpha, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st);
