@@ -116,7 +116,7 @@ struct RowBits {
   }
 };
 
-template <bool CAUSAL>
+template <bool CAUSAL, int NWARPS = kBldThreads / 32>
 __device__ __forceinline__ bool build_row_bits(const BldArgs& a, const Seg& sg, RowBits rb, int nwords) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t any = 0;
@@ -124,7 +124,7 @@ __device__ __forceinline__ bool build_row_bits(const BldArgs& a, const Seg& sg, 
     rb.fbits[0] = 0xffffffffu;
     rb.zbits[0] = 0u;
   }
-  for (int w = warp; w < nwords; w += kBldThreads / 32) {
+  for (int w = warp; w < nwords; w += NWARPS) {
     const int64_t j = rb.jbits + w * 32 + lane;
     const uint32_t fm = __ballot_sync(0xffffffffu, row_fixed<CAUSAL>(a, sg, j));
     const uint32_t zm = __ballot_sync(0xffffffffu, row_zero(a, sg, j));
@@ -137,6 +137,10 @@ __device__ __forceinline__ bool build_row_bits(const BldArgs& a, const Seg& sg, 
   if (threadIdx.x == 0) {
     rb.fbits[nwords + 1] = 0xffffffffu;
     rb.zbits[nwords + 1] = 0u;
+  }
+  if (NWARPS == 1) {
+    __syncwarp();
+    return any != 0u;  // ballots made `any` warp-uniform
   }
   return __syncthreads_or(any != 0u) != 0;
 }

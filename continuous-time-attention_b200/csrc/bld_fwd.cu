@@ -9,18 +9,18 @@
 //                                   src/models/pde_layers.py:39-64,113-188,218-219
 //   * zero-padded packed prefill:   src/cta/serving_vllm.py:72-111,275-303
 //
-// Work decomposition.  A CTA owns an output tile of TL rows x 512 columns.
-// Its 128 threads each own four adjacent columns (two packed fp32 pairs) and
-// *march* down the rows of the tile plus a halo: every arriving input row
-// advances all `steps` time levels by one row (a wavefront: level k lags k
-// rows, or 0 rows for the causal stencil), so a thread keeps two rows of state
-// per level in registers and every intermediate level stays on chip.  Input
-// rows arrive in shared memory through a ring of TMA tile loads (8 rows x 512
-// columns per chunk as two 256-column boxes, 4 chunks in flight, one mbarrier
-// per slot); the output is written once, straight from registers, as one
-// 8/16-byte vector per thread and row.  HBM traffic is one read of the input
-// (halo rows are re-read from L2 by the neighbouring tile) and one write of
-// the output.
+// Work decomposition.  A CTA is ONE warp with its own pipeline, owning an
+// output tile of TL rows x 128 columns; no CTA-wide barrier exists.  Each
+// lane owns four adjacent columns (two packed fp32 pairs) and *marches* down
+// the rows of the tile plus a halo: every arriving input row advances all
+// `steps` time levels by one row (a wavefront: level k lags k rows, or 0 rows
+// for the causal stencil), so a lane keeps two rows of state per level in
+// registers and every intermediate level stays on chip.  Input rows arrive in
+// shared memory through a ring of TMA tile loads (8 rows x 128 columns per
+// chunk, 4 chunks in flight, one mbarrier per slot); finished rows are staged
+// in shared memory and leave through TMA tile stores, 8 rows at a time.  HBM
+// traffic is one read of the input (halo rows are re-read from L2 by the
+// neighbouring tile) and one write of the output.
 //
 // Rows that must not change -- the copy boundary, rows whose 3-row stencil
 // touches a masked position, per-sequence boundaries of packed prefill -- are
@@ -34,15 +34,14 @@ __device__ int g_bld_fwd_error;
 
 namespace {
 
-// Plain-load fill of one forward chunk (two [RC][256] column blocks), for
-// tensors TMA cannot address and for shard edges that read neighbour halos.
+// Plain-load fill of one forward chunk ([RC][128]), for tensors TMA cannot
+// address and for shard edges that read neighbour halos.
 template <typename T>
 __device__ void fill_fwd_chunk(const BldArgs& a, const Seg& s, int64_t jrow0, int d0, T* dst) {
   const T zero = Elem<T>::from_f(0.f);
   for (int idx = threadIdx.x; idx < kFwdRC * kFwdDT; idx += kFwdThreads) {
     const int i = idx / kFwdDT;
     const int cc = idx - i * kFwdDT;
-    const int box = cc / kBoxCols, cb = cc - box * kBoxCols;
     const int64_t tr = s.row0 + jrow0 + i;
     const int col = d0 + cc;
     const T* rowp = nullptr;
@@ -53,14 +52,14 @@ __device__ void fill_fwd_chunk(const BldArgs& a, const Seg& s, int64_t jrow0, in
     } else if (tr >= a.L && a.hi_ext != nullptr && tr - a.L < a.hext_hi) {
       rowp = static_cast<const T*>(a.hi_ext) + (static_cast<int64_t>(s.bcoord) * a.hext_hi + (tr - a.L)) * a.D;
     }
-    dst[box * kFwdRC * kBoxCols + i * kBoxCols + cb] = (rowp != nullptr && col < a.D) ? rowp[col] : zero;
+    dst[i * kFwdDT + cc] = (rowp != nullptr && col < a.D) ? rowp[col] : zero;
   }
 }
 
 }  // namespace
 
 template <typename T, int S, bool CAUSAL>
-__global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_constant__ CUtensorMap xmap,
+__global__ void __launch_bounds__(kFwdThreads, (S >= 6 ? kFwdMinCtasDeep : kFwdMinCtas)) bld_fwd_kernel(const __grid_constant__ CUtensorMap xmap,
                                                               const __grid_constant__ CUtensorMap ymap,
                                                               const BldArgs a) {
   using Q = Quad<T>;
@@ -71,8 +70,7 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
   constexpr int PAD = (kFwdRC - LAG % kFwdRC) % kFwdRC;
   constexpr int PRO = PAD + LAG;  // prologue rows (no output), a multiple of kFwdRC
   constexpr int NPRO = PRO / kFwdRC;
-  constexpr int CHUNK = kFwdRC * kFwdDT;   // elements per pipeline slot
-  constexpr int BOXE = kFwdRC * kBoxCols;  // elements per TMA box
+  constexpr int CHUNK = kFwdRC * kFwdDT;  // elements per pipeline slot (one TMA box)
   static_assert(NPRO >= 1 && NPRO <= 2, "prologue spans one or two chunks");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -94,7 +92,6 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
   const int tid = threadIdx.x;
   const bool use_tma = a.use_tma != 0;
   const bool tstore = a.use_tma_store != 0;
-  const int nbox = (d0 + kBoxCols < a.D) ? 2 : 1;
 
   if (tid == 0) {
     if (use_tma) prefetch_tmap(&xmap);
@@ -103,19 +100,18 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
     for (int s = 0; s < kFwdStages; ++s) mbar_init(&full_bar[s], 1);
     fence_mbar_init();
   }
-  RowBits rb{fbits, zbits, jb};
-  const bool slow = build_row_bits<CAUSAL>(a, sg, rb, (nch * kFwdRC + 31) / 32);
-
   auto issue = [&](int c) {
     const int slot = c % kFwdStages;
-    mbar_arrive_expect_tx(&full_bar[slot], nbox * BOXE * sizeof(T));
-    const int row = static_cast<int>(sg.row0 + jb + c * kFwdRC);
-    for (int b = 0; b < nbox; ++b)
-      tma_load_3d(ring + slot * CHUNK + b * BOXE, &xmap, &full_bar[slot], d0 + b * kBoxCols, row, sg.bcoord);
+    mbar_arrive_expect_tx(&full_bar[slot], CHUNK * sizeof(T));
+    tma_load_3d(ring + slot * CHUNK, &xmap, &full_bar[slot], d0, static_cast<int>(sg.row0 + jb + c * kFwdRC),
+                sg.bcoord);
   };
+  // the first loads fly while the fixed-row bitmap is built
   if (use_tma && tid == 0) {
     for (int c = 0; c < nch && c < kFwdStages; ++c) issue(c);
   }
+  RowBits rb{fbits, zbits, jb};
+  const bool slow = build_row_bits<CAUSAL, 1>(a, sg, rb, (nch * kFwdRC + 31) / 32);
 
   float alf[kMaxSteps];
   load_alphas(a, alf, S);
@@ -130,14 +126,13 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
 #pragma unroll
   for (int k = 0; k < S; ++k) P1a[k] = P2a[k] = P1b[k] = P2b[k] = 0ull;
 
-  // column quad of this thread: box (tid / 64), 4 columns at (tid % 64) * 4
-  const int box = tid >> 6;
-  const int cb = (tid & 63) * 4;
-  const int col = d0 + box * kBoxCols + cb;
+  // column quad of this lane
+  const int cb = tid * 4;
+  const int col = d0 + cb;
   const bool col_ok = col < a.D;
   const bool quad_ok = a.y_quad_ok != 0 && col + 3 < a.D;
   T* const ybase = static_cast<T*>(a.y) + static_cast<int64_t>(sg.bcoord) * a.ysB + sg.row0 * a.ysL + col;
-  const int soff = box * BOXE + cb;  // element offset of this thread in a slot
+  const int soff = cb;  // element offset of this lane in a slot row
 
   auto store_row = [&](int64_t orow, pf2 pa, pf2 pb) {
     T* yp = ybase + orow * a.ysL;
@@ -213,7 +208,7 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
     const int t0 = c * kFwdRC;
     V in[kFwdRC];
 #pragma unroll
-    for (int i = 0; i < kFwdRC; ++i) in[i] = *reinterpret_cast<const V*>(buf + soff + i * kBoxCols);
+    for (int i = 0; i < kFwdRC; ++i) in[i] = *reinterpret_cast<const V*>(buf + soff + i * kFwdDT);
     T* st = stage + ((c - NPRO) & 1) * CHUNK + soff;
     static_for<kFwdRC>([&](auto I) {
       constexpr int i = decltype(I)::value;
@@ -225,7 +220,7 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
         step_row(slow_tag, std::integral_constant<int, -1>{}, jb + t0 + i, xa, xb);
         const int64_t orow = l0 + t0 + i - PRO;
         if constexpr (KIND == NPRO) {
-          if (tstore) *reinterpret_cast<V*>(st + i * kBoxCols) = Q::join(xa, xb);
+          if (tstore) *reinterpret_cast<V*>(st + i * kFwdDT) = Q::join(xa, xb);
           else store_row(orow, xa, xb);
         } else {
           if (t0 + i < nrows) store_row(orow, xa, xb);
@@ -234,33 +229,27 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
     });
   };
 
-  int err = 0;
-  for (int c = 0; c < nch; ++c) {
+  // One pipeline step: wait for chunk c, march it, hand full output chunks to
+  // the TMA store, refill the slot.  Returns false after a timed-out wait.
+  auto do_chunk = [&](auto slow_tag, auto kind_tag, int c) -> bool {
+    constexpr int KIND = decltype(kind_tag)::value;
+    constexpr bool FULL = KIND == NPRO;
     const int slot = c % kFwdStages;
     const T* buf = ring + slot * CHUNK;
+    int err = 0;
     if (use_tma) {
       if (!mbar_wait_bounded(&full_bar[slot], (c / kFwdStages) & 1)) err = 1;
     } else {
       fill_fwd_chunk<T>(a, sg, jb + c * kFwdRC, d0, ring + slot * CHUNK);
-      __syncthreads();
+      __syncwarp();
     }
-    const bool full = c >= NPRO && (c + 1) * kFwdRC <= nrows;
-    if (!err) {
-      auto dispatch = [&](auto slow_tag) {
-        if (c == 0) march_chunk(slow_tag, std::integral_constant<int, 0>{}, c, buf);
-        else if (NPRO > 1 && c == 1) march_chunk(slow_tag, std::integral_constant<int, (NPRO > 1 ? 1 : 0)>{}, c, buf);
-        else if (full) march_chunk(slow_tag, std::integral_constant<int, NPRO>{}, c, buf);
-        else march_chunk(slow_tag, std::integral_constant<int, NPRO + 1>{}, c, buf);
-      };
-      if (slow) dispatch(std::true_type{});
-      else dispatch(std::false_type{});
-    }
-    const bool tma_out = tstore && full;
-    if (tma_out) fence_proxy_async_smem();
+    if (!err) march_chunk(slow_tag, kind_tag, c, buf);
+    if (FULL && tstore) fence_proxy_async_smem();
     // the store issued after the previous chunk must have finished reading the
-    // staging slot that the next chunk will overwrite
+    // staging slot that the next chunk overwrites
     if (tstore && tid == 0) bulk_wait_read_all();
-    if (__syncthreads_or(err)) {
+    __syncwarp();
+    if (__any_sync(0xffffffffu, err)) {
       if (tid == 0) {
         atomicExch(&g_bld_fwd_error, kDevTimeout);
         // drain (bounded) every load still in flight, and the stores, before the CTA exits
@@ -269,20 +258,36 @@ __global__ void __launch_bounds__(kFwdThreads) bld_fwd_kernel(const __grid_const
             mbar_wait_bounded(&full_bar[cc % kFwdStages], (cc / kFwdStages) & 1);
         if (tstore) bulk_wait_all();
       }
-      __syncthreads();
-      return;
+      __syncwarp();
+      return false;
     }
     if (tid == 0) {
-      if (tma_out) {
+      if (FULL && tstore) {
         const int orow0 = static_cast<int>(sg.row0 + l0 + c * kFwdRC - PRO);
-        const T* src = stage + ((c - NPRO) & 1) * CHUNK;
-        for (int b = 0; b < nbox; ++b) tma_store_3d(&ymap, src + b * BOXE, d0 + b * kBoxCols, orow0, sg.bcoord);
+        tma_store_3d(&ymap, stage + ((c - NPRO) & 1) * CHUNK, d0, orow0, sg.bcoord);
         bulk_commit();
       }
       if (use_tma && c + kFwdStages < nch) issue(c + kFwdStages);
     }
-  }
-  if (tstore && tid == 0) bulk_wait_all();
+    return true;
+  };
+
+  // prologue chunks, then a single-body loop over full chunks, then the
+  // partial last chunk; the fast/slow choice is made once per tile
+  const int nfull_end = nrows / kFwdRC;  // chunks [NPRO, nfull_end) are full
+  auto run = [&](auto slow_tag) -> bool {
+    if (!do_chunk(slow_tag, std::integral_constant<int, 0>{}, 0)) return false;
+    if constexpr (NPRO > 1) {
+      if (!do_chunk(slow_tag, std::integral_constant<int, 1>{}, 1)) return false;
+    }
+    for (int c = NPRO; c < nfull_end; ++c)
+      if (!do_chunk(slow_tag, std::integral_constant<int, NPRO>{}, c)) return false;
+    if (nfull_end < nch)
+      if (!do_chunk(slow_tag, std::integral_constant<int, NPRO + 1>{}, nfull_end)) return false;
+    return true;
+  };
+  const bool ok = slow ? run(std::true_type{}) : run(std::false_type{});
+  if (ok && tstore && tid == 0) bulk_wait_all();
 }
 
 size_t fwd_smem_bytes(int dtype) {

@@ -73,18 +73,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 3-D map over a [nb, rows, D] tensor with element strides (sB, sL, 1); box is
-// box_rows rows x kBoxCols columns.  Returns false when TMA cannot address it.
+// box_rows rows x box_cols columns.  Returns false when TMA cannot address it.
 bool encode_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t rows, int64_t D, int64_t sB,
-                int64_t sL, int box_rows);
+                int64_t sL, int box_rows, int box_cols);
 
 // Encoded maps are pure host data; the last few are kept per thread so that
 // repeated calls on the same buffers skip the encode.
 bool make_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t rows, int64_t D, int64_t sB,
-              int64_t sL, int box_rows) {
+              int64_t sL, int box_rows, int box_cols) {
   struct Slot {
     const void* base;
     int dtype;
-    int box_rows;
+    int box_rows, box_cols;
     int64_t nb, rows, D, sB, sL;
     bool ok;
     CUtensorMap map;
@@ -94,7 +94,8 @@ bool make_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t r
   thread_local int next = 0;
   for (int i = 0; i < kSlots; ++i) {
     const Slot& c = cache[i];
-    if (c.base == base && base != nullptr && c.dtype == dtype && c.box_rows == box_rows && c.nb == nb &&
+    if (c.base == base && base != nullptr && c.dtype == dtype && c.box_rows == box_rows && c.box_cols == box_cols &&
+        c.nb == nb &&
         c.rows == rows && c.D == D && c.sB == sB && c.sL == sL) {
       if (c.ok) *m = c.map;
       return c.ok;
@@ -102,10 +103,11 @@ bool make_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t r
   }
   Slot& c = cache[next];
   next = (next + 1) % kSlots;
-  c.ok = encode_map(&c.map, base, dtype, nb, rows, D, sB, sL, box_rows);
+  c.ok = encode_map(&c.map, base, dtype, nb, rows, D, sB, sL, box_rows, box_cols);
   c.base = base;
   c.dtype = dtype;
   c.box_rows = box_rows;
+  c.box_cols = box_cols;
   c.nb = nb;
   c.rows = rows;
   c.D = D;
@@ -116,7 +118,7 @@ bool make_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t r
 }
 
 bool encode_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t rows, int64_t D, int64_t sB,
-                int64_t sL, int box_rows) {
+                int64_t sL, int box_rows, int box_cols) {
   auto fn = encode_fn();
   if (fn == nullptr || base == nullptr) return false;
   const int64_t es = static_cast<int64_t>(dtype_size(dtype));
@@ -129,7 +131,7 @@ bool encode_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t
   if (sL * es >= (1LL << 40) || bstride >= (1LL << 40)) return false;
   cuuint64_t gdim[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(nb)};
   cuuint64_t gstride[2] = {static_cast<cuuint64_t>(sL * es), static_cast<cuuint64_t>(bstride)};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(kBoxCols), static_cast<cuuint32_t>(box_rows), 1u};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUtensorMapDataType dt = dtype == CTA_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : dtype == CTA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -145,14 +147,15 @@ bool encode_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t
 // that the 2*steps halo rows stay a small overhead
 // ---------------------------------------------------------------------------
 struct Tuning {
-  int ctas_per_sm = 6;
+  int ctas_per_sm = 6;       // backward kernels (128-thread CTAs)
   int tl_override = 0;
+  int fwd_ctas_per_sm = 16;  // forward kernels (one-warp CTAs): one full wave
 };
 Tuning g_tuning;
 
-int pick_tl(int64_t rows, int64_t parallel_ctas, int steps) {
+int pick_tl(int64_t rows, int64_t parallel_ctas, int steps, int per_sm) {
   if (g_tuning.tl_override > 0) return std::min(kBldMaxTL, ((g_tuning.tl_override + kBldRC - 1) / kBldRC) * kBldRC);
-  const int64_t target = static_cast<int64_t>(num_sms()) * g_tuning.ctas_per_sm;
+  const int64_t target = static_cast<int64_t>(num_sms()) * per_sm;
   int64_t tl = (rows * std::max<int64_t>(parallel_ctas, 1) + target - 1) / target;
   tl = ((tl + kBldRC - 1) / kBldRC) * kBldRC;
   const int64_t min_tl = steps >= 6 ? 64 : 32;
@@ -245,6 +248,9 @@ int cta_set_tuning(int key, int value) {
   } else if (key == 1) {
     prev = g_tuning.tl_override;
     g_tuning.tl_override = value > 0 ? value : 0;
+  } else if (key == 2) {
+    prev = g_tuning.fwd_ctas_per_sm;
+    g_tuning.fwd_ctas_per_sm = value > 0 ? value : 16;
   }
   return prev;
 }
@@ -345,15 +351,15 @@ int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t 
   a.msL = mask_sL;
   fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-  a.TL = pick_tl(L, ndt * B, steps);
+  a.TL = pick_tl(L, ndt * B, steps, g_tuning.fwd_ctas_per_sm);
   a.out_begin = 0;
   a.out_end = L;
   a.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
   CUtensorMap xmap, ymap;
   std::memset(&xmap, 0, sizeof(xmap));
   std::memset(&ymap, 0, sizeof(ymap));
-  a.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC) ? 1 : 0;
-  a.use_tma_store = make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC) ? 1 : 0;
+  a.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
+  a.use_tma_store = make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
   return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), xmap, ymap);
 }
 
@@ -415,7 +421,7 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
   a.msL = mask_sL;
   fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
   const int64_t ndt = (D + kBldDT - 1) / kBldDT;
-  a.TL = std::max(pick_tl(L, ndt * B, steps), 32);
+  a.TL = std::max(pick_tl(L, ndt * B, steps, g_tuning.ctas_per_sm), 32);
   a.out_begin = 0;
   a.out_end = L;
   const int64_t ntl = (L + a.TL - 1) / a.TL;
@@ -424,8 +430,8 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
   CUtensorMap gmap, xmap;
   std::memset(&gmap, 0, sizeof(gmap));
   std::memset(&xmap, 0, sizeof(xmap));
-  bool tma = make_map(&gmap, grad_out, dtype, B, L, D, g_sB, g_sL, kBldRC);
-  if (da) tma = tma && make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kBldRC);
+  bool tma = make_map(&gmap, grad_out, dtype, B, L, D, g_sB, g_sL, kBldRC, kBoxCols);
+  if (da) tma = tma && make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kBldRC, kBoxCols);
   else xmap = gmap;
   a.use_tma = tma ? 1 : 0;
   if (da) {
@@ -467,15 +473,15 @@ int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
   // tiles are cut per sequence: size them from the average sequence length
   const int64_t avg = std::max<int64_t>(1, total_rows / nseq);
-  a.TL = pick_tl(avg, ndt * nseq, steps);
+  a.TL = pick_tl(avg, ndt * nseq, steps, g_tuning.fwd_ctas_per_sm);
   a.out_begin = 0;
   a.out_end = max_len;
   a.y_quad_ok = quad_ok(y, dtype, 1, D, 0, y_sL) ? 1 : 0;
   CUtensorMap xmap, ymap;
   std::memset(&xmap, 0, sizeof(xmap));
   std::memset(&ymap, 0, sizeof(ymap));
-  a.use_tma = make_map(&xmap, x, dtype, 1, total_rows, D, 0, x_sL, kFwdRC) ? 1 : 0;
-  a.use_tma_store = make_map(&ymap, y, dtype, 1, total_rows, D, 0, y_sL, kFwdRC) ? 1 : 0;
+  a.use_tma = make_map(&xmap, x, dtype, 1, total_rows, D, 0, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
+  a.use_tma_store = make_map(&ymap, y, dtype, 1, total_rows, D, 0, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
   return launch_fwd(a, dtype, steps, 0, nseq, max_len, static_cast<cudaStream_t>(stream), xmap, ymap);
 }
 
@@ -540,7 +546,7 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
   for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
   const int64_t ndt = (D + (backward ? kBldDT : kFwdDT) - 1) / (backward ? kBldDT : kFwdDT);
   a.TL = edge ? static_cast<int>(std::min<int64_t>(kBldMaxTL, ((oe - ob + kBldRC - 1) / kBldRC) * kBldRC))
-              : pick_tl(oe - ob, ndt * B, steps);
+              : pick_tl(oe - ob, ndt * B, steps, backward ? g_tuning.ctas_per_sm : g_tuning.fwd_ctas_per_sm);
   a.out_begin = ob;
   a.out_end = oe;
   a.y_quad_ok = quad_ok(out, dtype, B, D, L_local * D, D) ? 1 : 0;
@@ -548,10 +554,11 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
   std::memset(&map, 0, sizeof(map));
   std::memset(&omap, 0, sizeof(omap));
   a.use_tma =
-      (!edge && make_map(&map, in, dtype, B, L_local, D, L_local * D, D, backward ? kBldRC : kFwdRC)) ? 1 : 0;
+      (!edge && make_map(&map, in, dtype, B, L_local, D, L_local * D, D, backward ? kBldRC : kFwdRC,
+                           backward ? kBoxCols : kFwdDT)) ? 1 : 0;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (!backward) {
-    a.use_tma_store = make_map(&omap, out, dtype, B, L_local, D, L_local * D, D, kFwdRC) ? 1 : 0;
+    a.use_tma_store = make_map(&omap, out, dtype, B, L_local, D, L_local * D, D, kFwdRC, kFwdDT) ? 1 : 0;
     return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, oe - ob, st, map, omap);
   }
   const int64_t ntl = (oe - ob + a.TL - 1) / a.TL;

@@ -20,14 +20,16 @@ constexpr int kBldDT = kBldThreads * kBldVec;  // 256 columns per CTA (TMA box i
 constexpr int kBldRC = 16;                    // rows per pipeline chunk
 constexpr int kBldStages = 4;                 // chunks in flight per CTA
 constexpr int kBldMaxTL = 2048;               // max output rows per CTA tile
-// forward kernel: 4 columns per thread (two packed pairs), 512-column tiles
-// fed by two 256-column TMA boxes per 8-row chunk
-constexpr int kFwdThreads = 128;
-constexpr int kFwdDT = 512;
+// forward kernel: one warp per CTA running its own pipeline; 4 columns per
+// lane (two packed pairs) -> 128-column tiles, one TMA box per 8-row chunk
+constexpr int kFwdThreads = 32;
+constexpr int kFwdDT = 128;
 constexpr int kFwdRC = 8;
-constexpr int kFwdStages = 3;    // input chunks in flight
+constexpr int kFwdStages = 4;    // input chunks in flight
+constexpr int kFwdMinCtas = 20;      // register budget: one-warp CTAs per SM for steps <= 5
+constexpr int kFwdMinCtasDeep = 12;  // ... and for steps >= 6 (more state per lane)
 constexpr int kFwdOutSlots = 2;  // output staging chunks for the TMA stores
-constexpr int kBoxCols = 256;                 // TMA box inner extent (max 256)
+constexpr int kBoxCols = 256;    // TMA box inner extent of the backward maps (max 256)
 constexpr int kBldMaxWords = (kBldMaxTL + 2 * 2 * kMaxSteps + kBldRC + 31) / 32 + 1;
 
 struct BldArgs {

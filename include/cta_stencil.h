@@ -51,8 +51,9 @@ const char* cta_last_error(void);
  * synchronizes with the device. */
 int cta_device_error(int clear);
 
-/* Benchmark tuning hook: key 0 = target CTAs per SM used to size [B, L, D]
- * tiles (default 6), key 1 = forced tile rows (0 = automatic).  Returns the
+/* Benchmark tuning hook: key 0 = target CTAs per SM used to size the [B, L, D]
+ * backward tiles (default 6), key 1 = forced tile rows (0 = automatic), key 2 =
+ * target CTAs per SM of the [B, L, D] forward (default 16).  Returns the
  * previous value.  Process-wide, not thread-safe against concurrent launches. */
 int cta_set_tuning(int key, int value);
 
