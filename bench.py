@@ -13,8 +13,9 @@ N > 1 (torchrun, one rank per GPU): every rank runs the same per-GPU workload
 on its own GPU (independent replicas, weak scaling; the stencil of one
 sequence shards only with the L-sharded workload, `--workload sharded`).
 
-Reported: `value` tokens/s with inputs resident in HBM (device-timed, max over
-ranks); `e2e` the same through the public API with pinned host buffers
+Reported: `value` tokens/s with inputs resident in HBM (device-timed with CUDA
+events over CUDA-graph replays of the calls, max over ranks); `e2e` the same
+through the public API, called eagerly, with pinned host buffers
 (H2D + kernel + D2H each step); `roofline` of the fused kernel against the
 measured HBM copy bandwidth; `cpu_baseline` the CPU oracle (the reference's
 algorithm in PyTorch) on the host cores; `clocks` sampled during timing.
@@ -58,7 +59,8 @@ def _ncu_traffic(key: str):
     if not p.exists():
         return None
     try:
-        return json.loads(p.read_text()).get(key)
+        entry = json.loads(p.read_text()).get(key)
+        return None if entry is None else entry.get("per_launch_bytes")
     except Exception:  # noqa: BLE001
         return None
 
@@ -119,7 +121,7 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU side: the oracle (the reference's algorithm) on the host cores
 # ---------------------------------------------------------------------------
-def cpu_reference_rate(L: int, D: int, steps: int, seconds: float = 12.0, max_calls: int = 64):
+def cpu_reference_rate(L: int, D: int, steps: int, seconds: float = 12.0, max_calls: int = 100000):
     """Tokens/s of the CPU oracle on row windows of the [1, L, D] bf16 workload."""
     from oracle import diffusion_oracle as O
 
@@ -186,6 +188,7 @@ def _config(args):
 # GPU side
 # ---------------------------------------------------------------------------
 def _time_launches(fn, n: int, stream) -> float:
+    """Seconds for n eager calls, CUDA events on the launching stream."""
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -195,6 +198,38 @@ def _time_launches(fn, n: int, stream) -> float:
     end.record(stream)
     torch.cuda.synchronize()
     return start.elapsed_time(end) / 1e3
+
+
+class GraphLoop:
+    """`per_graph` consecutive calls captured once as a CUDA graph; timing replays
+    it, so the device runs the launches back to back without host gaps."""
+
+    def __init__(self, fn, per_graph: int):
+        self.per_graph = per_graph
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(per_graph):  # warm every buffer / attribute outside capture
+                fn(i)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            for i in range(per_graph):
+                fn(i)
+        torch.cuda.synchronize()
+
+    def time(self, n_calls: int, stream) -> tuple[float, int]:
+        reps = max(1, (n_calls + self.per_graph - 1) // self.per_graph)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(reps):
+            self.graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / 1e3, reps * self.per_graph
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
@@ -221,6 +256,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    loop = None if args.mode == "kernel" else GraphLoop(step, nbuf * max(1, 64 // nbuf))
     if args.mode == "kernel":
         # bare launches for profilers: no sampler, e2e, sweep or CPU baseline
         t = _time_launches(step, args.steps, stream)
@@ -233,9 +269,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     sampler = ClockSampler(local_rank) if rank == 0 else None
     if sampler:
         sampler.__enter__()
-    elapsed = _time_launches(step, args.steps, stream)
+    elapsed, n_calls = loop.time(args.steps, stream)
     if sampler:
         sampler.__exit__(None, None, None)
+    args.steps = n_calls  # whole graphs only: the count actually timed
     if world > 1:
         t = torch.tensor([elapsed], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -281,10 +318,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             by = [torch.empty_like(bx[0]) for _ in range(nb)]
             for Ss in (2, 4, 8):
                 fn = (lambda i, bx=bx, by=by, Ss=Ss, nb=nb: ops.bld_forward(bx[i % nb], [0.1] * Ss, Ss, out=by[i % nb]))
-                for i in range(5):
-                    fn(i)
-                n = 200
-                t = _time_launches(fn, n, stream) / n
+                gl = GraphLoop(fn, nb * max(1, 64 // nb))
+                t, n = gl.time(1000, stream)
+                t /= n
                 gbs = 2 * Ls * D * esize / t / 1e9
                 sweep.append({"L": Ls, "steps": Ss, "us_per_call": round(t * 1e6, 2), "GB/s": round(gbs, 1),
                               "frac": round(gbs / peak, 3), "tokens/s": round(Ls / t)})
@@ -320,8 +356,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--L", type=int, default=65536)
     ap.add_argument("--D", type=int, default=512)
