@@ -224,6 +224,15 @@ int64_t dalpha_max_ctas(int64_t B, int64_t L, int64_t D) {
 
 }  // namespace
 
+void cta::set_last_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+}
+
 extern "C" {
 
 int cta_abi_version(void) { return CTA_ABI_VERSION; }

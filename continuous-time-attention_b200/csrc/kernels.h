@@ -104,6 +104,9 @@ cudaError_t launch_bld_bwd(const BldArgs& a, const CUtensorMap* gmap, const CUte
                            int steps, int causal, int with_dalpha, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st);
 
+// sets the thread-local message returned by cta_last_error()
+void set_last_error(const char* fmt, ...) __attribute__((format(printf, 1, 2)));
+
 size_t bld_smem_bytes(int dtype, int with_x_stream);
 size_t fwd_smem_bytes(int dtype);
 int read_device_error_bld_fwd(int clear);

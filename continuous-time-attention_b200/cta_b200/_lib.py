@@ -58,6 +58,10 @@ _SIGNATURES = {
                                       c_int64, c_void_p]),
     "cta_diffusion_fwd_varlen": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64,
                                          c_int64, c_int, c_int, c_int, c_float, c_void_p]),
+    "cta_diffusion_bwd_bld_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                              c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+                                              c_int, POINTER(c_float), POINTER(c_void_p), c_int, c_void_p, c_int,
+                                              c_int64, c_int64, c_void_p]),
     "cta_diffusion_shard_bld": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p,
                                         c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_float,
                                         c_void_p]),

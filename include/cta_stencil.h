@@ -116,6 +116,26 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
                           const float* alpha, const void* const* alpha_dev, int alpha_dev_dtype, const void* mask,
                           int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream);
 
+/* Allocation-free form of cta_diffusion_bwd_bld (no counterpart in the
+ * reference).  For callers that cannot provide fresh device memory -- an engine
+ * that has reserved almost the whole GPU for its own pool, or a latency-critical
+ * path that must not pay cudaMalloc's implicit synchronisation -- the d(alpha)
+ * scratch comes from a fixed array inside the library (262400 bytes per device,
+ * held until the process exits).  Same arguments as cta_diffusion_bwd_bld minus
+ * the workspace.  Shapes whose reduction needs more scratch than that (more than
+ * 65536 CTA x step partial sums) are rejected with CTA_EINVAL.  The first call on
+ * a device looks up the array's device address; make that first call before
+ * any stream capture.  The array is shared by every call on a device and keeps
+ * the previous call's contents (the completion counter is cleared at the start
+ * of each call), so calls whose work overlaps on the GPU race and must be
+ * serialised by the caller.  Calls no cudaMalloc, cudaFree or allocating
+ * library routine. */
+int cta_diffusion_bwd_bld_noalloc(const void* grad_out, void* grad_in, const void* x, float* dalpha, int64_t B,
+                                  int64_t L, int64_t D, int64_t g_sB, int64_t g_sL, int64_t x_sB, int64_t x_sL,
+                                  int64_t d_sB, int64_t d_sL, int dtype, int steps, int causal, const float* alpha,
+                                  const void* const* alpha_dev, int alpha_dev_dtype, const void* mask,
+                                  int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream);
+
 /* Packed variable-length prefill: x, y are [total_rows, D] (row strides
  * x_sL / y_sL), cu_seqlens is a DEVICE int32 array of nseq+1 offsets.
  *   pad_to_max = 0: every sequence has its own copy boundary and no stencil
