@@ -353,6 +353,140 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+
+# ---------------------------------------------------------------------------
+# other configurations of the stencil (selected with --workload)
+# ---------------------------------------------------------------------------
+def _max_over_ranks(t: float, dev, world: int) -> float:
+    if world == 1:
+        return t
+    import torch.distributed as dist
+
+    v = torch.tensor([t], device=dev, dtype=torch.float64)
+    dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    return float(v.item())
+
+
+def _emit(rank, line):
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_varlen(args, rank, world, local_rank):
+    """Packed prefill through the mixer: 64 sequences, lengths U[512, 8192], D=4096 bf16,
+    steps 4, one varlen launch per call (each rank a replica)."""
+    from types import SimpleNamespace
+
+    from cta_b200.serving_vllm import CtaConfig, CtaPostAttnMixer
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator().manual_seed(0)
+    lens = torch.randint(512, 8193, (64,), generator=gen)
+    qsl = torch.zeros(65, dtype=torch.int32)
+    qsl[1:] = torch.cumsum(lens, 0)
+    T, D = int(qsl[-1]), args.D if args.D != 512 else 4096
+    nb = 2
+    xs = [torch.randn(T, D, device=dev, dtype=torch.bfloat16) for _ in range(nb)]
+    md = SimpleNamespace(max_query_len=int(lens.max()), query_start_loc=qsl.to(dev), is_prefill=True)
+    mixer = CtaPostAttnMixer(CtaConfig(steps=args.stencil_steps, alpha=0.1, trace=False))
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        mixer(xs[i % nb], attn_metadata=md)
+
+    for i in range(args.warmup):
+        step(i)
+    k = min(args.steps, 200)
+    t = _max_over_ranks(_time_launches(step, k, stream), dev, world)
+    peak, _ = _peaks()
+    per = t / k
+    gbs = 2 * T * D * 2 / per / 1e9
+    _emit(rank, {"metric": METRIC, "value": T * world / per, "unit": "tokens/s", "n_gpus": world, "steps": k,
+                 "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
+                 "dtype": "bf16", "data": "synthetic",
+                 "config": {"workload": "varlen_mixer", "nseq": 64, "tokens": T, "D": D,
+                            "steps": args.stencil_steps, "rule": "reference zero-pad to max_query_len"},
+                 "hbm_gbs": gbs, "hbm_frac": gbs / peak, "gpu_launches": k})
+
+
+def run_block(args, rank, world, local_rank):
+    """PDE-Transformer LM (causal stencil) fwd+bwd: D=512, 8 heads, FFN 2048, 6 layers, pde_steps 4,
+    bf16, B=1; the same model with pde_steps=0 is timed for the refinement's share."""
+    from cta_b200.transformers import PDETransformerLM
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L = args.L
+    torch.manual_seed(0)
+    ids = torch.randint(0, 32000, (1, L), device=dev)
+    tgt = torch.randint(0, 32000, (1, L), device=dev)
+    mask = torch.ones(1, L, dtype=torch.long, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+    for pde in (args.stencil_steps, 0):
+        net = PDETransformerLM(vocab_size=32000, embed_dim=512, num_heads=8, hidden_dim=2048, num_layers=6,
+                               pde_steps=pde, max_length=L, dropout=0.0).to(dev, torch.bfloat16)
+
+        def step(_i):
+            out = net(ids, mask)
+            loss = torch.nn.functional.cross_entropy(out.view(-1, out.shape[-1]).float(), tgt.view(-1))
+            loss.backward()
+
+        for i in range(max(3, min(args.warmup, 5))):
+            step(i)
+        k = max(3, min(args.steps, 10))
+        res[pde] = _max_over_ranks(_time_launches(step, k, stream), dev, world) / k
+        del net
+        torch.cuda.empty_cache()
+    per = res[args.stencil_steps]
+    _emit(rank, {"metric": METRIC, "value": L * world / per, "unit": "tokens/s", "n_gpus": world, "steps": 10,
+                 "warmup": 3, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
+                 "dtype": "bf16", "data": "synthetic",
+                 "config": {"workload": "pde_transformer_lm_fwd_bwd", "B": 1, "L": L, "D": 512, "layers": 6,
+                            "heads": 8, "ffn": 2048, "pde_steps": args.stencil_steps, "causal": True},
+                 "ms_without_pde": res[0] * 1e3, "pde_share": (per - res[0]) / per})
+
+
+def run_sharded(args, rank, world, local_rank):
+    """Long-context stencil: bf16 x[1, L, 4096] split evenly over the ranks, steps 8,
+    forward + adjoint, steps-row halos exchanged with NCCL send/recv per call."""
+    from cta_b200.sharded import even_shards, sharded_diffusion
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L, D, S = args.L if args.L != 65536 else 1 << 20, 4096, args.stencil_steps if args.stencil_steps != 4 else 8
+    spec = even_shards(L, world, rank)
+    torch.manual_seed(1000 + rank)
+    x = torch.randn(1, spec.local_len, D, device=dev, dtype=torch.bfloat16)
+    g = torch.randn_like(x)
+    comm = torch.cuda.Stream(device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(_i):
+        sharded_diffusion(x, spec, alpha=0.1, steps=S, comm_stream=comm)
+        sharded_diffusion(g, spec, alpha=0.1, steps=S, backward=True, comm_stream=comm)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    k = max(3, min(args.steps, 20))
+    t = _max_over_ranks(_time_launches(step, k, stream), dev, world)
+    per = t / k
+    peak, _ = _peaks()
+    bytes_rank = 4 * spec.local_len * D * 2  # fwd read+write, adjoint read+write
+    _emit(rank, {"metric": METRIC, "value": L / per, "unit": "tokens/s", "n_gpus": world, "steps": k,
+                 "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "strong",
+                 "dtype": "bf16", "data": "synthetic",
+                 "config": {"workload": "sharded_fwd_bwd", "B": 1, "L": L, "D": D, "steps": S,
+                            "parallelism": f"L-sharded x{world}", "halo_rows": S},
+                 "hbm_gbs_per_gpu": bytes_rank / per / 1e9, "hbm_frac": bytes_rank / per / 1e9 / peak})
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -364,6 +498,9 @@ def main() -> None:
     ap.add_argument("--stencil-steps", type=int, default=4)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", choices=["fused_fwd", "varlen", "block", "sharded"], default="fused_fwd",
+                    help="fused_fwd: headline single-GPU forward; varlen: 64-sequence packed mixer, D=4096; "
+                         "block: PDE-Transformer LM fwd+bwd; sharded: L=1M x 4096 split over the ranks")
     ap.add_argument("--mode", choices=["full", "kernel"], default="full",
                     help="kernel: only warmup + timed launches of the fused kernel (for ncu)")
     args = ap.parse_args()
@@ -385,7 +522,8 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        {"fused_fwd": run_ours, "varlen": run_varlen, "block": run_block, "sharded": run_sharded}[args.workload](
+            args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
