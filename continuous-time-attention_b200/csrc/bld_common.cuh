@@ -106,6 +106,13 @@ struct RowBits {
     const uint64_t v = static_cast<uint64_t>(fbits[w]) | (static_cast<uint64_t>(fbits[w + 1]) << 32);
     return static_cast<uint32_t>(v >> sh) & 0xffu;
   }
+  __device__ __forceinline__ uint32_t window16_fixed(int64_t row_lo) const {
+    // bits for rows row_lo .. row_lo+15 (bit m = row_lo + m)
+    const int64_t p = row_lo - jbits + 32;
+    const int w = static_cast<int>(p >> 5), sh = static_cast<int>(p & 31);
+    const uint64_t v = static_cast<uint64_t>(fbits[w]) | (static_cast<uint64_t>(fbits[w + 1]) << 32);
+    return static_cast<uint32_t>(v >> sh) & 0xffffu;
+  }
   __device__ __forceinline__ bool fixed(int64_t row) const {
     const int64_t p = row - jbits + 32;
     return (fbits[p >> 5] >> (p & 31)) & 1u;

@@ -58,13 +58,28 @@ __device__ void fill_fwd_chunk(const BldArgs& a, const Seg& s, int64_t jrow0, in
 
 }  // namespace
 
-template <typename T, int S, bool CAUSAL>
-__global__ void __launch_bounds__(kFwdThreads, (S >= 6 ? kFwdMinCtasDeep : kFwdMinCtas)) bld_fwd_kernel(const __grid_constant__ CUtensorMap xmap,
-                                                              const __grid_constant__ CUtensorMap ymap,
-                                                              const BldArgs a) {
+// ADJ = false: forward, x -> y.  ADJ = true: the adjoint of the same `steps`
+// steps applied to a gradient, g -> dx (without d(alpha)); it shares the whole
+// pipeline, only the per-row update and the halo side differ.
+// Register budget: variants with little per-level state are held to the
+// budget of kFwdMinCtas resident CTAs per SM; the deep ones (more steps, the
+// adjoint's larger state, fp32 chunks) are left uncapped so they never spill.
+template <typename T, int S, bool CAUSAL, bool ADJ>
+constexpr int march_min_ctas() {
+  return ((!ADJ && S <= (sizeof(T) == 4 ? 4 : 5)) || (ADJ && !CAUSAL && S <= 3) || (ADJ && CAUSAL && S <= 2))
+             ? kFwdMinCtas
+             : 1;
+}
+
+template <typename T, int S, bool CAUSAL, bool ADJ>
+__global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ>()))
+    bld_march_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
+                     const BldArgs a) {
   using Q = Quad<T>;
   using V = typename Q::V;
-  constexpr int HL = CAUSAL ? 2 * S : S;  // halo rows above the tile
+  // halo rows above the tile: the causal forward reads 2S rows back, its
+  // adjoint (anti-causal) only reads forward
+  constexpr int HL = ADJ ? (CAUSAL ? 0 : S) : (CAUSAL ? 2 * S : S);
   constexpr int LAG = 2 * S;              // wavefront depth: march rows before the first finished row
   // extra leading rows so that output rows start on a chunk boundary
   constexpr int PAD = (kFwdRC - LAG % kFwdRC) % kFwdRC;
@@ -121,10 +136,12 @@ __global__ void __launch_bounds__(kFwdThreads, (S >= 6 ? kFwdMinCtasDeep : kFwdM
   const pf2 m2 = pbc(-2.f);
   const pf2 zn = pbc(a.neg_zero);
 
-  // per-level state: the level's input on the two previous march rows, for both pairs
-  pf2 P1a[S], P2a[S], P1b[S], P2b[S];
+  // per-level state, for both pairs.  Forward: the level's input on the two
+  // previous march rows (P1, P2).  Adjoint: a = alpha*g on the two previous
+  // rows (P1, P2) and g on the one (non-causal) or two (causal) previous rows (G1, G2).
+  pf2 P1a[S], P2a[S], P1b[S], P2b[S], G1a[S], G1b[S], G2a[S], G2b[S];
 #pragma unroll
-  for (int k = 0; k < S; ++k) P1a[k] = P2a[k] = P1b[k] = P2b[k] = 0ull;
+  for (int k = 0; k < S; ++k) P1a[k] = P2a[k] = P1b[k] = P2b[k] = G1a[k] = G1b[k] = G2a[k] = G2b[k] = 0ull;
 
   // column quad of this lane
   const int cb = tid * 4;
@@ -157,7 +174,49 @@ __global__ void __launch_bounds__(kFwdThreads, (S >= 6 ? kFwdMinCtasDeep : kFwdM
     if (SLOW) {
       if (rb.zero(j)) xa = xb = 0ull;
     }
-    if (CAUSAL) {
+    if constexpr (ADJ) {
+      // g enters as level S; level m applies the adjoint of forward step S-m:
+      //   non-causal  g_new[i] = g[i] + (a[i+1] - 2 a[i]) + a[i-1],  i = j-1-m
+      //   causal      g_new[i] = g[i] + (a[i] - 2 a[i+1]) + a[i+2],  i = j-2-2m
+      // with a = alpha * g on updated rows and 0 on fixed rows.
+      const bool f0 = SLOW && rb.fixed(j);
+      const uint32_t fw = SLOW ? (CAUSAL ? rb.window16_fixed(j - 2 * S) : rb.window8_fixed(j - S)) : 0u;
+      pf2 ca = pmul_sep(al[S - 1], xa, zn), cb = pmul_sep(al[S - 1], xb, zn);
+      if (SLOW && f0) ca = cb = 0ull;
+#pragma unroll
+      for (int m = 0; m < S; ++m) {
+        pf2 na = xa, nb = xb;
+        if (TCT < 0 || TCT >= 2 * m + 2) {
+          if (CAUSAL) {
+            na = padd(G2a[m], plap(ca, P1a[m], P2a[m], m2));
+            nb = padd(G2b[m], plap(cb, P1b[m], P2b[m], m2));
+          } else {
+            na = padd(G1a[m], plap(P2a[m], P1a[m], ca, m2));
+            nb = padd(G1b[m], plap(P2b[m], P1b[m], cb, m2));
+          }
+        }
+        P2a[m] = P1a[m];
+        P1a[m] = ca;
+        P2b[m] = P1b[m];
+        P1b[m] = cb;
+        if (CAUSAL) {
+          G2a[m] = G1a[m];
+          G2b[m] = G1b[m];
+        }
+        G1a[m] = xa;
+        G1b[m] = xb;
+        xa = na;
+        xb = nb;
+        if (m < S - 1) {
+          ca = pmul_sep(al[S - 2 - m], xa, zn);
+          cb = pmul_sep(al[S - 2 - m], xb, zn);
+          if (SLOW) {
+            const bool f = CAUSAL ? ((fw >> (2 * S - 2 * m - 2)) & 1u) : ((fw >> (S - 1 - m)) & 1u);
+            if (f) ca = cb = 0ull;
+          }
+        }
+      }
+    } else if (CAUSAL) {
       const bool fx = SLOW && rb.fixed(j);
 #pragma unroll
       for (int k = 0; k < S; ++k) {
@@ -297,46 +356,50 @@ size_t fwd_smem_bytes(int dtype) {
 
 namespace {
 
-template <typename T, int S, bool CAUSAL>
+template <typename T, int S, bool CAUSAL, bool ADJ>
 cudaError_t launch_fwd_t(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, dim3 grid, size_t smem,
                          cudaStream_t st) {
-  auto kern = bld_fwd_kernel<T, S, CAUSAL>;
+  auto kern = bld_march_kernel<T, S, CAUSAL, ADJ>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kFwdThreads, smem, st>>>(*xmap, *ymap, a);
   return cudaGetLastError();
 }
 
-template <typename T, bool CAUSAL>
+template <typename T, bool CAUSAL, bool ADJ>
 cudaError_t fwd_steps(const BldArgs& a, const CUtensorMap* m, const CUtensorMap* ym, int steps, dim3 g, size_t sm,
                       cudaStream_t st) {
   switch (steps) {
-    case 1: return launch_fwd_t<T, 1, CAUSAL>(a, m, ym, g, sm, st);
-    case 2: return launch_fwd_t<T, 2, CAUSAL>(a, m, ym, g, sm, st);
-    case 3: return launch_fwd_t<T, 3, CAUSAL>(a, m, ym, g, sm, st);
-    case 4: return launch_fwd_t<T, 4, CAUSAL>(a, m, ym, g, sm, st);
-    case 5: return launch_fwd_t<T, 5, CAUSAL>(a, m, ym, g, sm, st);
-    case 6: return launch_fwd_t<T, 6, CAUSAL>(a, m, ym, g, sm, st);
-    case 7: return launch_fwd_t<T, 7, CAUSAL>(a, m, ym, g, sm, st);
-    case 8: return launch_fwd_t<T, 8, CAUSAL>(a, m, ym, g, sm, st);
+    case 1: return launch_fwd_t<T, 1, CAUSAL, ADJ>(a, m, ym, g, sm, st);
+    case 2: return launch_fwd_t<T, 2, CAUSAL, ADJ>(a, m, ym, g, sm, st);
+    case 3: return launch_fwd_t<T, 3, CAUSAL, ADJ>(a, m, ym, g, sm, st);
+    case 4: return launch_fwd_t<T, 4, CAUSAL, ADJ>(a, m, ym, g, sm, st);
+    case 5: return launch_fwd_t<T, 5, CAUSAL, ADJ>(a, m, ym, g, sm, st);
+    case 6: return launch_fwd_t<T, 6, CAUSAL, ADJ>(a, m, ym, g, sm, st);
+    case 7: return launch_fwd_t<T, 7, CAUSAL, ADJ>(a, m, ym, g, sm, st);
+    case 8: return launch_fwd_t<T, 8, CAUSAL, ADJ>(a, m, ym, g, sm, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <typename T>
-cudaError_t fwd_dtype(const BldArgs& a, const CUtensorMap* m, const CUtensorMap* ym, int steps, int causal, dim3 g,
-                      size_t sm, cudaStream_t st) {
-  return causal ? fwd_steps<T, true>(a, m, ym, steps, g, sm, st) : fwd_steps<T, false>(a, m, ym, steps, g, sm, st);
+cudaError_t fwd_dtype(const BldArgs& a, const CUtensorMap* m, const CUtensorMap* ym, int steps, int causal, int adj,
+                      dim3 g, size_t sm, cudaStream_t st) {
+  if (adj)
+    return causal ? fwd_steps<T, true, true>(a, m, ym, steps, g, sm, st)
+                  : fwd_steps<T, false, true>(a, m, ym, steps, g, sm, st);
+  return causal ? fwd_steps<T, true, false>(a, m, ym, steps, g, sm, st)
+                : fwd_steps<T, false, false>(a, m, ym, steps, g, sm, st);
 }
 
 }  // namespace
 
 cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, int dtype, int steps,
-                           int causal, dim3 grid, size_t smem, cudaStream_t st) {
+                           int causal, int adjoint, dim3 grid, size_t smem, cudaStream_t st) {
   switch (dtype) {
-    case kF32: return fwd_dtype<float>(a, xmap, ymap, steps, causal, grid, smem, st);
-    case kBF16: return fwd_dtype<__nv_bfloat16>(a, xmap, ymap, steps, causal, grid, smem, st);
-    case kF16: return fwd_dtype<__half>(a, xmap, ymap, steps, causal, grid, smem, st);
+    case kF32: return fwd_dtype<float>(a, xmap, ymap, steps, causal, adjoint, grid, smem, st);
+    case kBF16: return fwd_dtype<__nv_bfloat16>(a, xmap, ymap, steps, causal, adjoint, grid, smem, st);
+    case kF16: return fwd_dtype<__half>(a, xmap, ymap, steps, causal, adjoint, grid, smem, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -203,7 +203,7 @@ bool quad_ok(const void* y, int dtype, int64_t nb, int64_t D, int64_t sB, int64_
 }
 
 int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int64_t tile_rows, cudaStream_t st,
-               const CUtensorMap& xmap, const CUtensorMap& ymap) {
+               const CUtensorMap& xmap, const CUtensorMap& ymap, int adjoint = 0) {
   const int64_t ntl = (tile_rows + a.TL - 1) / a.TL;
   const int64_t ndt = (a.D + kFwdDT - 1) / kFwdDT;
   if (ntl <= 0 || nbatch <= 0) return ok();
@@ -211,7 +211,8 @@ int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int
     return fail(CTA_EUNSUPPORTED, "grid too large (tiles %lld, D tiles %lld, batch %lld)", (long long)ntl,
                 (long long)ndt, (long long)nbatch);
   dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(nbatch));
-  const cudaError_t e = launch_bld_fwd(a, &xmap, &ymap, dtype, steps, causal, grid, fwd_smem_bytes(dtype), st);
+  const cudaError_t e =
+      launch_bld_fwd(a, &xmap, &ymap, dtype, steps, causal, adjoint, grid, fwd_smem_bytes(dtype), st);
   if (e != cudaSuccess) return cuda_fail(e, "bld forward launch");
   return ok();
 }
@@ -410,6 +411,36 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
     }
     return ok();
   }
+  if (!da) {
+    // adjoint only: the one-warp TMA march kernel (same pipeline as the forward)
+    BldArgs m = blank_bld();
+    m.x = grad_out;
+    m.y = grad_in;
+    m.xsB = g_sB;
+    m.xsL = g_sL;
+    m.ysB = d_sB;
+    m.ysL = d_sL;
+    m.L = L;
+    m.D = static_cast<int>(D);
+    m.nbatch = static_cast<int>(B);
+    m.global_len = L;
+    m.mask = mask;
+    m.mask_dtype = mask_dtype;
+    m.msB = mask_sB;
+    m.msL = mask_sL;
+    fill_alpha(m, steps, alpha, alpha_dev, alpha_dev_dtype);
+    const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
+    m.TL = pick_tl(L, ndt * B, steps, g_tuning.fwd_ctas_per_sm);
+    m.out_begin = 0;
+    m.out_end = L;
+    m.y_quad_ok = quad_ok(grad_in, dtype, B, D, d_sB, d_sL) ? 1 : 0;
+    CUtensorMap gm, dm;
+    std::memset(&gm, 0, sizeof(gm));
+    std::memset(&dm, 0, sizeof(dm));
+    m.use_tma = make_map(&gm, grad_out, dtype, B, L, D, g_sB, g_sL, kFwdRC, kFwdDT) ? 1 : 0;
+    m.use_tma_store = make_map(&dm, grad_in, dtype, B, L, D, d_sB, d_sL, kFwdRC, kFwdDT) ? 1 : 0;
+    return launch_fwd(m, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), gm, dm, 1);
+  }
   BldArgs a = blank_bld();
   a.g = grad_out;
   a.x = x;
@@ -480,9 +511,12 @@ int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t
   a.max_len = max_len;
   for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-  // tiles are cut per sequence: size them from the average sequence length
+  // tiles are cut per sequence: about eight tiles per average sequence keeps
+  // the waves balanced across unequal lengths (halo overhead 2*steps/TL)
   const int64_t avg = std::max<int64_t>(1, total_rows / nseq);
-  a.TL = pick_tl(avg, ndt * nseq, steps, g_tuning.fwd_ctas_per_sm);
+  a.TL = g_tuning.tl_override > 0
+             ? pick_tl(avg, ndt * nseq, steps, g_tuning.fwd_ctas_per_sm)
+             : static_cast<int>(std::min<int64_t>(512, std::max<int64_t>(64, ((avg / 8 + 15) / 16) * 16)));
   a.out_begin = 0;
   a.out_end = max_len;
   a.y_quad_ok = quad_ok(y, dtype, 1, D, 0, y_sL) ? 1 : 0;
@@ -536,8 +570,7 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
       return fail(CTA_EINVAL, "bad halo row counts");
   }
   BldArgs a = blank_bld();
-  if (backward) a.g = in;
-  else a.x = in;
+  a.x = in;  // the march kernel's input stream (x forward, the gradient for the adjoint)
   a.y = out;
   a.xsB = a.gsB = a.ysB = L_local * D;
   a.xsL = a.gsL = a.ysL = D;
@@ -553,29 +586,19 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
     a.hext_hi = a.hi_ext ? static_cast<int>(hi_rows) : 0;
   }
   for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
-  const int64_t ndt = (D + (backward ? kBldDT : kFwdDT) - 1) / (backward ? kBldDT : kFwdDT);
+  const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
   a.TL = edge ? static_cast<int>(std::min<int64_t>(kBldMaxTL, ((oe - ob + kBldRC - 1) / kBldRC) * kBldRC))
-              : pick_tl(oe - ob, ndt * B, steps, backward ? g_tuning.ctas_per_sm : g_tuning.fwd_ctas_per_sm);
+              : pick_tl(oe - ob, ndt * B, steps, g_tuning.fwd_ctas_per_sm);
   a.out_begin = ob;
   a.out_end = oe;
   a.y_quad_ok = quad_ok(out, dtype, B, D, L_local * D, D) ? 1 : 0;
   CUtensorMap map, omap;
   std::memset(&map, 0, sizeof(map));
   std::memset(&omap, 0, sizeof(omap));
-  a.use_tma =
-      (!edge && make_map(&map, in, dtype, B, L_local, D, L_local * D, D, backward ? kBldRC : kFwdRC,
-                           backward ? kBoxCols : kFwdDT)) ? 1 : 0;
+  a.use_tma = (!edge && make_map(&map, in, dtype, B, L_local, D, L_local * D, D, kFwdRC, kFwdDT)) ? 1 : 0;
+  a.use_tma_store = make_map(&omap, out, dtype, B, L_local, D, L_local * D, D, kFwdRC, kFwdDT) ? 1 : 0;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (!backward) {
-    a.use_tma_store = make_map(&omap, out, dtype, B, L_local, D, L_local * D, D, kFwdRC, kFwdDT) ? 1 : 0;
-    return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, oe - ob, st, map, omap);
-  }
-  const int64_t ntl = (oe - ob + a.TL - 1) / a.TL;
-  if (ntl > 0x7fffffffLL || ndt > 65535 || B > 65535) return fail(CTA_EUNSUPPORTED, "grid too large");
-  dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(B));
-  const cudaError_t e = launch_bld_bwd(a, &map, &map, dtype, steps, causal ? 1 : 0, 0, grid, bld_smem_bytes(dtype, 0), st);
-  if (e != cudaSuccess) return cuda_fail(e, "shard backward launch");
-  return ok();
+  return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, oe - ob, st, map, omap, backward ? 1 : 0);
 }
 
 }  // extern "C"

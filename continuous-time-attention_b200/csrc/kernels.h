@@ -26,8 +26,7 @@ constexpr int kFwdThreads = 32;
 constexpr int kFwdDT = 128;
 constexpr int kFwdRC = 8;
 constexpr int kFwdStages = 4;    // input chunks in flight
-constexpr int kFwdMinCtas = 20;      // register budget: one-warp CTAs per SM for steps <= 5
-constexpr int kFwdMinCtasDeep = 12;  // ... and for steps >= 6 (more state per lane)
+constexpr int kFwdMinCtas = 20;  // register budget (one-warp CTAs per SM) of the shallow variants
 constexpr int kFwdOutSlots = 2;  // output staging chunks for the TMA stores
 constexpr int kBoxCols = 256;    // TMA box inner extent of the backward maps (max 256)
 constexpr int kBldMaxWords = (kBldMaxTL + 2 * 2 * kMaxSteps + kBldRC + 31) / 32 + 1;
@@ -98,8 +97,9 @@ struct BdlArgs {
 };
 
 // launchers (return cudaError_t of the launch)
+// march kernel: forward (adjoint = 0) or the adjoint without d(alpha) (adjoint = 1)
 cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, int dtype,
-                           int steps, int causal, dim3 grid, size_t smem, cudaStream_t st);
+                           int steps, int causal, int adjoint, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bld_bwd(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap, int dtype,
                            int steps, int causal, int with_dalpha, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st);

@@ -148,9 +148,19 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
 #pragma unroll
   for (int i = 0; i < E8; ++i) e[i] = pk(va[i], vbv[i]);
 
-  const uint32_t fa = fixed_bits<CAUSAL>(a, ra, pa, true);
-  const uint32_t fb = fixed_bits<CAUSAL>(a, rbw, pb, vb);
-  const bool slow = __any_sync(0xffffffffu, (fa | fb) != 0u);
+  // Windows that lie strictly inside the domain (and calls without a mask) have
+  // no fixed position: skip the per-position bookkeeping there (warp-uniform).
+  const int64_t lo_fixed = CAUSAL ? 1 : 0, hi_fixed = CAUSAL ? a.L : a.L - 1;
+  const int64_t wa0 = (wa - ra * nwin) * kBdlOut - HLN * E8;
+  const int64_t wb0 = vb ? (wb - rbw * nwin) * kBdlOut - HLN * E8 : wa0;
+  const bool interior = a.mask == nullptr && vb && wa0 > lo_fixed && wa0 + 32 * E8 - 1 < hi_fixed &&
+                        wb0 > lo_fixed && wb0 + 32 * E8 - 1 < hi_fixed;
+  uint32_t fa = 0u, fb = 0u;
+  if (!interior) {
+    fa = fixed_bits<CAUSAL>(a, ra, pa, true);
+    fb = fixed_bits<CAUSAL>(a, rbw, pb, vb);
+  }
+  const bool slow = !interior && __any_sync(0xffffffffu, (fa | fb) != 0u);
 
   float al[kMaxSteps];
 #pragma unroll
@@ -191,7 +201,7 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
         pf2 av[E8];
 #pragma unroll
         for (int i = 0; i < E8; ++i) {
-          av[i] = pmul(alv, e[i]);
+          av[i] = pmul_sep(alv, e[i], zn);
           if (SLOW) av[i] = sel_fixed(fa, fb, i, 0ull, av[i]);
         }
         if (CAUSAL) {
