@@ -75,7 +75,7 @@ template <typename T, int S, bool CAUSAL, bool ADJ>
 __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ>()))
     bld_march_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                      const BldArgs a) {
-  using Q = Quad<T>;
+  using Q = ColVec<T, kFwdVec>;
   using V = typename Q::V;
   // halo rows above the tile: the causal forward reads 2S rows back, its
   // adjoint (anti-causal) only reads forward
@@ -96,10 +96,14 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   __shared__ uint32_t zbits[kBldMaxWords + 2];
 
   const Seg sg = resolve_seg(a, blockIdx.z);
-  const int64_t l0 = a.out_begin + static_cast<int64_t>(blockIdx.x) * a.TL;
+  // column tile fastest: the CTAs launched together cover whole rows of the same
+  // row tile, so each DRAM page is read (and written) by neighbouring CTAs at once
+  const int ndt = (a.D + kFwdDT - 1) / kFwdDT;
+  const int dtile = static_cast<int>(blockIdx.x % ndt);
+  const int64_t l0 = a.out_begin + static_cast<int64_t>(blockIdx.x / ndt) * a.TL;
   const int64_t oend = a.out_end < sg.n ? a.out_end : sg.n;
   if (l0 >= oend) return;
-  const int d0 = blockIdx.y * kFwdDT;
+  const int d0 = dtile * kFwdDT;
   const int64_t jb = l0 - HL - PAD;  // first march row
   const int nout = static_cast<int>(oend - l0 < a.TL ? oend - l0 : a.TL);
   const int nrows = PRO + nout;
@@ -143,11 +147,11 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
 #pragma unroll
   for (int k = 0; k < S; ++k) P1a[k] = P2a[k] = P1b[k] = P2b[k] = G1a[k] = G1b[k] = G2a[k] = G2b[k] = 0ull;
 
-  // column quad of this lane
-  const int cb = tid * 4;
+  // column group of this lane
+  const int cb = tid * kFwdVec;
   const int col = d0 + cb;
   const bool col_ok = col < a.D;
-  const bool quad_ok = a.y_quad_ok != 0 && col + 3 < a.D;
+  const bool quad_ok = a.y_quad_ok != 0 && col + kFwdVec - 1 < a.D;
   T* const ybase = static_cast<T*>(a.y) + static_cast<int64_t>(sg.bcoord) * a.ysB + sg.row0 * a.ysL + col;
   const int soff = cb;  // element offset of this lane in a slot row
 
@@ -160,7 +164,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       upk(pa, v[0], v[1]);
       upk(pb, v[2], v[3]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < kFwdVec; ++j)
         if (col + j < a.D) yp[j] = Elem<T>::from_f(v[j]);
     }
   };

@@ -199,7 +199,8 @@ BldArgs blank_bld() {
 
 bool quad_ok(const void* y, int dtype, int64_t nb, int64_t D, int64_t sB, int64_t sL) {
   const int64_t es = static_cast<int64_t>(dtype_size(dtype));
-  return reinterpret_cast<uintptr_t>(y) % (4 * es) == 0 && D % 4 == 0 && sL % 4 == 0 && (nb == 1 || sB % 4 == 0);
+  const int64_t v = kFwdVec;
+  return reinterpret_cast<uintptr_t>(y) % (v * es) == 0 && D % v == 0 && sL % v == 0 && (nb == 1 || sB % v == 0);
 }
 
 int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int64_t tile_rows, cudaStream_t st,
@@ -207,10 +208,11 @@ int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int
   const int64_t ntl = (tile_rows + a.TL - 1) / a.TL;
   const int64_t ndt = (a.D + kFwdDT - 1) / kFwdDT;
   if (ntl <= 0 || nbatch <= 0) return ok();
-  if (ntl > 0x7fffffffLL || ndt > 65535 || nbatch > 65535)
+  if (ntl * ndt > 0x7fffffffLL || nbatch > 65535)
     return fail(CTA_EUNSUPPORTED, "grid too large (tiles %lld, D tiles %lld, batch %lld)", (long long)ntl,
                 (long long)ndt, (long long)nbatch);
-  dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(nbatch));
+  // x = row tile * column tiles + column tile (column tile fastest)
+  dim3 grid(static_cast<unsigned>(ntl * ndt), 1u, static_cast<unsigned>(nbatch));
   const cudaError_t e =
       launch_bld_fwd(a, &xmap, &ymap, dtype, steps, causal, adjoint, grid, fwd_smem_bytes(dtype), st);
   if (e != cudaSuccess) return cuda_fail(e, "bld forward launch");

@@ -195,7 +195,8 @@ __device__ __forceinline__ pf2 pst_c(pf2 p2, pf2 p1, pf2 c, pf2 al, pf2 m2, pf2 
 __device__ __forceinline__ pf2 plap(pf2 lo, pf2 mid, pf2 hi, pf2 m2) { return padd(pfma(mid, m2, hi), lo); }
 __device__ __forceinline__ pf2 psel(bool p, pf2 a, pf2 b) { return p ? a : b; }
 
-// four consecutive columns <-> two pairs
+// VEC (2 or 4) consecutive columns of one lane <-> one or two pairs
+template <typename T, int VEC> struct ColVec;
 template <typename T> struct Quad;
 template <> struct Quad<__nv_bfloat16> {
   using V = uint2;
@@ -234,6 +235,25 @@ template <> struct Quad<float> {
     upk(a, r.x, r.y);
     upk(b, r.z, r.w);
     return r;
+  }
+};
+template <typename T> struct ColVec<T, 4> : Quad<T> {};
+template <typename T> struct ColVec<T, 2> {
+  // one pair; the second pair of the interface is unused and stays zero
+  using V = typename std::conditional<sizeof(T) == 4, float2, uint32_t>::type;
+  __device__ __forceinline__ static void split(V v, pf2& a, pf2& b) {
+    if constexpr (sizeof(T) == 4) a = pk(v.x, v.y);
+    else a = Quad<T>::w2p(v);
+    b = 0ull;
+  }
+  __device__ __forceinline__ static V join(pf2 a, pf2) {
+    if constexpr (sizeof(T) == 4) {
+      float2 r;
+      upk(a, r.x, r.y);
+      return r;
+    } else {
+      return Quad<T>::p2w(a);
+    }
   }
 };
 

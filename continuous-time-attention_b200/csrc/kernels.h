@@ -22,8 +22,12 @@ constexpr int kBldStages = 4;                 // chunks in flight per CTA
 constexpr int kBldMaxTL = 2048;               // max output rows per CTA tile
 // forward kernel: one warp per CTA running its own pipeline; 4 columns per
 // lane (two packed pairs) -> 128-column tiles, one TMA box per 8-row chunk
+#ifndef CTA_FWD_VEC
+#define CTA_FWD_VEC 4
+#endif
 constexpr int kFwdThreads = 32;
-constexpr int kFwdDT = 128;
+constexpr int kFwdVec = CTA_FWD_VEC;  // columns per lane: 4 (two packed pairs) or 2 (one pair)
+constexpr int kFwdDT = 32 * kFwdVec;
 constexpr int kFwdRC = 8;
 constexpr int kFwdStages = 4;    // input chunks in flight
 constexpr int kFwdMinCtas = 20;  // register budget (one-warp CTAs per SM) of the shallow variants

@@ -17,7 +17,10 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().with_name("libcta_stencil.so")
+import os
+
+# CTA_STENCIL_LIB selects another build of the library (e.g. a tuning variant)
+LIB_PATH = Path(os.environ.get("CTA_STENCIL_LIB") or Path(__file__).resolve().with_name("libcta_stencil.so"))
 
 CTA_OK, CTA_EINVAL, CTA_EUNSUPPORTED, CTA_ECUDA = 0, 1, 2, 3
 SHARD_INTERIOR, SHARD_LO_EDGE, SHARD_HI_EDGE = 0, 1, 2

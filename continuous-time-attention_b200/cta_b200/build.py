@@ -62,16 +62,23 @@ def is_stale() -> bool:
     return any(f.stat().st_mtime > t for f in _inputs())
 
 
-def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -> Path:
-    """Compile every kernel translation unit for sm_100a and link the library."""
-    if not force and not is_stale():
+def build(force: bool = False, verbose: bool = False, jobs: int | None = None, defines: tuple = (),
+          out: Path | None = None) -> Path:
+    """Compile every kernel translation unit for sm_100a and link the library.
+
+    `defines` (e.g. ("CTA_FWD_VEC=2",)) and `out` build a tuning variant into
+    another file; the default build is the in-tree libcta_stencil.so.
+    """
+    target = Path(out) if out is not None else LIB_PATH
+    if not force and not defines and out is None and not is_stale():
         return LIB_PATH
     nvcc = _nvcc()
-    BUILD_DIR.mkdir(parents=True, exist_ok=True)
-    incs = ["-I", str(INCLUDE), "-I", str(CSRC)]
+    build_dir = BUILD_DIR if not defines else BUILD_DIR / ("var_" + "_".join(d.replace("=", "") for d in defines))
+    build_dir.mkdir(parents=True, exist_ok=True)
+    incs = ["-I", str(INCLUDE), "-I", str(CSRC)] + [f"-D{d}" for d in defines]
 
     def compile_one(name: str) -> Path:
-        obj = BUILD_DIR / (Path(name).stem + ".o")
+        obj = build_dir / (Path(name).stem + ".o")
         cmd = [nvcc, *ARCH_FLAGS, *CFLAGS, *incs, "-c", str(CSRC / name), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
@@ -86,14 +93,14 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     with ThreadPoolExecutor(max_workers=jobs or min(len(SOURCES), os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_one, SOURCES))
 
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = target.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(tmp), *map(str, objs),
            "-Xlinker", f"-soname={LIB_NAME}"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, target)
+    return target
 
 
 def main(argv: list[str] | None = None) -> int:
