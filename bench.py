@@ -487,6 +487,49 @@ def run_sharded(args, rank, world, local_rank):
                  "hbm_gbs_per_gpu": bytes_rank / per / 1e9, "hbm_frac": bytes_rank / per / 1e9 / peak})
 
 
+
+def run_kernels(args, rank, world, local_rank):
+    """Per-kernel table on bf16 x[1, L, D] (and its [1, D, L] transpose): fused forward,
+    adjoint, adjoint with d(alpha), and the [B, D, L] kernels, steps 2/4/8, graph-timed,
+    inputs rotating through buffers larger than L2."""
+    from cta_b200 import ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L, D = args.L, args.D
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    nb = max(2, min(16, (4 * l2) // (L * D * 2) + 1))
+    xs = [torch.randn(1, L, D, device=dev, dtype=torch.bfloat16) for _ in range(nb)]
+    gs = [torch.randn(1, L, D, device=dev, dtype=torch.bfloat16) for _ in range(nb)]
+    ys = [torch.empty_like(xs[0]) for _ in range(nb)]
+    xt = [t.transpose(1, 2).contiguous() for t in xs]
+    stream = torch.cuda.current_stream(dev)
+    peak, _ = _peaks()
+    unit = L * D * 2
+    rows = []
+
+    def timed(name, steps, fn, streams):
+        gl = GraphLoop(fn, nb * max(1, 32 // nb))
+        t, n = gl.time(max(200, args.steps // 20), stream)
+        per = t / n
+        gbs = streams * unit / per / 1e9
+        rows.append({"kernel": name, "steps": steps, "us": round(per * 1e6, 2), "GB/s": round(gbs, 1),
+                     "frac": round(gbs / peak, 3), "bytes_per_launch": streams * unit})
+
+    for S in (2, 4, 8):
+        timed("bld_forward", S, lambda i, S=S: ops.bld_forward(xs[i % nb], [0.1] * S, S, out=ys[i % nb]), 2)
+        timed("bld_adjoint", S, lambda i, S=S: ops.bld_backward(gs[i % nb], [0.1] * S, S), 2)
+        timed("bld_forward_causal", S,
+              lambda i, S=S: ops.bld_forward(xs[i % nb], [0.1] * S, S, causal=True, out=ys[i % nb]), 2)
+        timed("bdl_forward", S, lambda i, S=S: ops.bdl_simple(xt[i % nb], 0.1, S), 2)
+        timed("bdl_adjoint", S, lambda i, S=S: ops.bdl_simple(xt[i % nb], 0.1, S, backward=True), 2)
+    for S in (1, 4):
+        timed("bld_adjoint_dalpha", S,
+              lambda i, S=S: ops.bld_backward(gs[i % nb], [0.1] * S, S, x=xs[i % nb], need_dalpha=True), 3)
+    _emit(rank, {"workload": "kernels", "L": L, "D": D, "dtype": "bf16", "peak_GB/s": peak, "timing":
+                 "CUDA events over CUDA-graph replays, inputs rotating over >= 4x L2", "rows": rows})
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -498,9 +541,10 @@ def main() -> None:
     ap.add_argument("--stencil-steps", type=int, default=4)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["fused_fwd", "varlen", "block", "sharded"], default="fused_fwd",
+    ap.add_argument("--workload", choices=["fused_fwd", "varlen", "block", "sharded", "kernels"], default="fused_fwd",
                     help="fused_fwd: headline single-GPU forward; varlen: 64-sequence packed mixer, D=4096; "
-                         "block: PDE-Transformer LM fwd+bwd; sharded: L=1M x 4096 split over the ranks")
+                         "block: PDE-Transformer LM fwd+bwd; sharded: L=1M x 4096 split over the ranks; "
+                         "kernels: per-kernel timing table")
     ap.add_argument("--mode", choices=["full", "kernel"], default="full",
                     help="kernel: only warmup + timed launches of the fused kernel (for ncu)")
     args = ap.parse_args()
@@ -522,7 +566,8 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        {"fused_fwd": run_ours, "varlen": run_varlen, "block": run_block, "sharded": run_sharded}[args.workload](
+        {"fused_fwd": run_ours, "varlen": run_varlen, "block": run_block, "sharded": run_sharded,
+         "kernels": run_kernels}[args.workload](
             args, rank, world, local_rank)
     finally:
         if world > 1:
