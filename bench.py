@@ -491,7 +491,8 @@ def run_sharded(args, rank, world, local_rank):
 def run_kernels(args, rank, world, local_rank):
     """Per-kernel table on bf16 x[1, L, D] (and its [1, D, L] transpose): fused forward,
     adjoint, adjoint with d(alpha), and the [B, D, L] kernels, steps 2/4/8, graph-timed,
-    inputs rotating through buffers larger than L2."""
+    inputs and outputs rotating through buffers larger than L2 (an output allocated
+    inside the graph would be the same L2-resident buffer on every replay)."""
     from cta_b200 import ops
 
     dev = torch.device("cuda", local_rank)
@@ -503,6 +504,7 @@ def run_kernels(args, rank, world, local_rank):
     gs = [torch.randn(1, L, D, device=dev, dtype=torch.bfloat16) for _ in range(nb)]
     ys = [torch.empty_like(xs[0]) for _ in range(nb)]
     xt = [t.transpose(1, 2).contiguous() for t in xs]
+    yt = [torch.empty_like(xt[0]) for _ in range(nb)]
     stream = torch.cuda.current_stream(dev)
     peak, _ = _peaks()
     unit = L * D * 2
@@ -518,14 +520,15 @@ def run_kernels(args, rank, world, local_rank):
 
     for S in (2, 4, 8):
         timed("bld_forward", S, lambda i, S=S: ops.bld_forward(xs[i % nb], [0.1] * S, S, out=ys[i % nb]), 2)
-        timed("bld_adjoint", S, lambda i, S=S: ops.bld_backward(gs[i % nb], [0.1] * S, S), 2)
+        timed("bld_adjoint", S, lambda i, S=S: ops.bld_backward(gs[i % nb], [0.1] * S, S, out=ys[i % nb]), 2)
         timed("bld_forward_causal", S,
               lambda i, S=S: ops.bld_forward(xs[i % nb], [0.1] * S, S, causal=True, out=ys[i % nb]), 2)
-        timed("bdl_forward", S, lambda i, S=S: ops.bdl_simple(xt[i % nb], 0.1, S), 2)
-        timed("bdl_adjoint", S, lambda i, S=S: ops.bdl_simple(xt[i % nb], 0.1, S, backward=True), 2)
+        timed("bdl_forward", S, lambda i, S=S: ops.bdl_simple(xt[i % nb], 0.1, S, out=yt[i % nb]), 2)
+        timed("bdl_adjoint", S, lambda i, S=S: ops.bdl_simple(xt[i % nb], 0.1, S, backward=True, out=yt[i % nb]), 2)
     for S in (1, 4):
         timed("bld_adjoint_dalpha", S,
-              lambda i, S=S: ops.bld_backward(gs[i % nb], [0.1] * S, S, x=xs[i % nb], need_dalpha=True), 3)
+              lambda i, S=S: ops.bld_backward(gs[i % nb], [0.1] * S, S, x=xs[i % nb], need_dalpha=True,
+                                              out=ys[i % nb]), 3)
     _emit(rank, {"workload": "kernels", "L": L, "D": D, "dtype": "bf16", "peak_GB/s": peak, "timing":
                  "CUDA events over CUDA-graph replays, inputs rotating over >= 4x L2", "rows": rows})
 

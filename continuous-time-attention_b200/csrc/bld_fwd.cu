@@ -61,14 +61,21 @@ __device__ void fill_fwd_chunk(const BldArgs& a, const Seg& s, int64_t jrow0, in
 // ADJ = false: forward, x -> y.  ADJ = true: the adjoint of the same `steps`
 // steps applied to a gradient, g -> dx (without d(alpha)); it shares the whole
 // pipeline, only the per-row update and the halo side differ.
-// Register budget: variants with little per-level state are held to the
-// budget of kFwdMinCtas resident CTAs per SM; the deep ones (more steps, the
-// adjoint's larger state, fp32 chunks) are left uncapped so they never spill.
+//
+// Register budget.  A variant keeps, per lane and level, two rows of state for
+// each of its two column pairs (the adjoint also one or two rows of g), so its
+// register need grows with `steps`, and fastest for the causal adjoint.  The
+// minimum resident CTAs per SM handed to __launch_bounds__ is the largest of
+// 20/16/12/8 (5/4/3/2 warps per SM sub-partition, whose register file holds
+// 16384 registers) at which ptxas compiles the variant without spilling (checked
+// with -Xptxas -v for every variant); the host sizes the grid from the
+// occupancy the variant really gets (bld_march_ctas_per_sm).
 template <typename T, int S, bool CAUSAL, bool ADJ>
 constexpr int march_min_ctas() {
-  return ((!ADJ && S <= (sizeof(T) == 4 ? 4 : 5)) || (ADJ && !CAUSAL && S <= 3) || (ADJ && CAUSAL && S <= 2))
-             ? kFwdMinCtas
-             : 1;
+  constexpr bool F32 = sizeof(T) == 4;
+  if (!ADJ) return S <= 4 ? kFwdMinCtas : (S == 5 || (S == 6 && F32)) ? 16 : 12;
+  if (!CAUSAL) return S <= (F32 ? 2 : 3) ? kFwdMinCtas : S <= 5 ? 16 : 12;
+  return S <= 2 ? kFwdMinCtas : S <= (F32 ? 4 : 3) ? 16 : S <= 5 ? 12 : 8;
 }
 
 template <typename T, int S, bool CAUSAL, bool ADJ>
@@ -269,14 +276,11 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   auto march_chunk = [&](auto slow_tag, auto kind_tag, int c, const T* buf) {
     constexpr int KIND = decltype(kind_tag)::value;
     const int t0 = c * kFwdRC;
-    V in[kFwdRC];
-#pragma unroll
-    for (int i = 0; i < kFwdRC; ++i) in[i] = *reinterpret_cast<const V*>(buf + soff + i * kFwdDT);
     T* st = stage + ((c - NPRO) & 1) * CHUNK + soff;
     static_for<kFwdRC>([&](auto I) {
       constexpr int i = decltype(I)::value;
       pf2 xa, xb;
-      Q::split(in[i], xa, xb);
+      Q::split(*reinterpret_cast<const V*>(buf + soff + i * kFwdDT), xa, xb);
       if constexpr (KIND < NPRO) {
         step_row(slow_tag, std::integral_constant<int, KIND * kFwdRC + i>{}, jb + t0 + i, xa, xb);
       } else {
@@ -360,52 +364,70 @@ size_t fwd_smem_bytes(int dtype) {
 
 namespace {
 
-template <typename T, int S, bool CAUSAL, bool ADJ>
-cudaError_t launch_fwd_t(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, dim3 grid, size_t smem,
-                         cudaStream_t st) {
-  auto kern = bld_march_kernel<T, S, CAUSAL, ADJ>;
-  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
-  if (e != cudaSuccess) return e;
-  kern<<<grid, kFwdThreads, smem, st>>>(*xmap, *ymap, a);
-  return cudaGetLastError();
-}
-
 template <typename T, bool CAUSAL, bool ADJ>
-cudaError_t fwd_steps(const BldArgs& a, const CUtensorMap* m, const CUtensorMap* ym, int steps, dim3 g, size_t sm,
-                      cudaStream_t st) {
+const void* march_ptr(int steps) {
   switch (steps) {
-    case 1: return launch_fwd_t<T, 1, CAUSAL, ADJ>(a, m, ym, g, sm, st);
-    case 2: return launch_fwd_t<T, 2, CAUSAL, ADJ>(a, m, ym, g, sm, st);
-    case 3: return launch_fwd_t<T, 3, CAUSAL, ADJ>(a, m, ym, g, sm, st);
-    case 4: return launch_fwd_t<T, 4, CAUSAL, ADJ>(a, m, ym, g, sm, st);
-    case 5: return launch_fwd_t<T, 5, CAUSAL, ADJ>(a, m, ym, g, sm, st);
-    case 6: return launch_fwd_t<T, 6, CAUSAL, ADJ>(a, m, ym, g, sm, st);
-    case 7: return launch_fwd_t<T, 7, CAUSAL, ADJ>(a, m, ym, g, sm, st);
-    case 8: return launch_fwd_t<T, 8, CAUSAL, ADJ>(a, m, ym, g, sm, st);
-    default: return cudaErrorInvalidValue;
+    case 1: return reinterpret_cast<const void*>(bld_march_kernel<T, 1, CAUSAL, ADJ>);
+    case 2: return reinterpret_cast<const void*>(bld_march_kernel<T, 2, CAUSAL, ADJ>);
+    case 3: return reinterpret_cast<const void*>(bld_march_kernel<T, 3, CAUSAL, ADJ>);
+    case 4: return reinterpret_cast<const void*>(bld_march_kernel<T, 4, CAUSAL, ADJ>);
+    case 5: return reinterpret_cast<const void*>(bld_march_kernel<T, 5, CAUSAL, ADJ>);
+    case 6: return reinterpret_cast<const void*>(bld_march_kernel<T, 6, CAUSAL, ADJ>);
+    case 7: return reinterpret_cast<const void*>(bld_march_kernel<T, 7, CAUSAL, ADJ>);
+    case 8: return reinterpret_cast<const void*>(bld_march_kernel<T, 8, CAUSAL, ADJ>);
+    default: return nullptr;
   }
 }
 
 template <typename T>
-cudaError_t fwd_dtype(const BldArgs& a, const CUtensorMap* m, const CUtensorMap* ym, int steps, int causal, int adj,
-                      dim3 g, size_t sm, cudaStream_t st) {
-  if (adj)
-    return causal ? fwd_steps<T, true, true>(a, m, ym, steps, g, sm, st)
-                  : fwd_steps<T, false, true>(a, m, ym, steps, g, sm, st);
-  return causal ? fwd_steps<T, true, false>(a, m, ym, steps, g, sm, st)
-                : fwd_steps<T, false, false>(a, m, ym, steps, g, sm, st);
+const void* march_ptr_t(int steps, int causal, int adj) {
+  if (adj) return causal ? march_ptr<T, true, true>(steps) : march_ptr<T, false, true>(steps);
+  return causal ? march_ptr<T, true, false>(steps) : march_ptr<T, false, false>(steps);
+}
+
+const void* march_kernel(int dtype, int steps, int causal, int adj) {
+  switch (dtype) {
+    case kF32: return march_ptr_t<float>(steps, causal, adj);
+    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, adj);
+    case kF16: return march_ptr_t<__half>(steps, causal, adj);
+    default: return nullptr;
+  }
 }
 
 }  // namespace
 
 cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, int dtype, int steps,
                            int causal, int adjoint, dim3 grid, size_t smem, cudaStream_t st) {
-  switch (dtype) {
-    case kF32: return fwd_dtype<float>(a, xmap, ymap, steps, causal, adjoint, grid, smem, st);
-    case kBF16: return fwd_dtype<__nv_bfloat16>(a, xmap, ymap, steps, causal, adjoint, grid, smem, st);
-    case kF16: return fwd_dtype<__half>(a, xmap, ymap, steps, causal, adjoint, grid, smem, st);
-    default: return cudaErrorInvalidValue;
-  }
+  const void* kern = march_kernel(dtype, steps, causal, adjoint);
+  if (kern == nullptr) return cudaErrorInvalidValue;
+  cudaError_t e = ensure_smem_attr(kern, smem);
+  if (e != cudaSuccess) return e;
+  void* args[] = {const_cast<CUtensorMap*>(xmap), const_cast<CUtensorMap*>(ymap), const_cast<BldArgs*>(&a)};
+  return cudaLaunchKernel(kern, grid, dim3(kFwdThreads), args, smem, st);
+}
+
+int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint) {
+  struct Entry {
+    const void* kern;
+    int dev;
+    int n;
+  };
+  static Entry table[256];
+  static int used = 0;
+  static std::mutex mu;
+  const void* kern = march_kernel(dtype, steps, causal, adjoint);
+  if (kern == nullptr) return -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (table[i].kern == kern && table[i].dev == dev) return table[i].n;
+  const size_t smem = fwd_smem_bytes(dtype);
+  if (ensure_smem_attr(kern, smem) != cudaSuccess) return -1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kFwdThreads, smem) != cudaSuccess || n <= 0) return -1;
+  if (used < 256) table[used++] = Entry{kern, dev, n};
+  return n;
 }
 
 int read_device_error_bld_fwd(int clear) {

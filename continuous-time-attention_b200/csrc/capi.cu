@@ -164,6 +164,13 @@ int pick_tl(int64_t rows, int64_t parallel_ctas, int steps, int per_sm) {
   return static_cast<int>(tl);
 }
 
+// target resident CTAs per SM of a march kernel: the tuning value, capped by
+// the occupancy the variant gets (deep variants hold more registers)
+int march_per_sm(int dtype, int steps, int causal, int adjoint) {
+  const int occ = bld_march_ctas_per_sm(dtype, steps, causal, adjoint);
+  return occ > 0 ? std::min(g_tuning.fwd_ctas_per_sm, occ) : g_tuning.fwd_ctas_per_sm;
+}
+
 void fill_alpha(BldArgs& a, int steps, const float* alpha, const void* const* alpha_dev, int alpha_dev_dtype) {
   for (int k = 0; k < kMaxSteps; ++k) {
     a.alpha[k] = (alpha != nullptr && k < steps) ? alpha[k] : 0.f;
@@ -246,8 +253,9 @@ int cta_device_error(int clear) {
   const int a = read_device_error_bld_fwd(clear);
   const int b = read_device_error_bld_bwd(clear);
   const int c = read_device_error_bdl(clear);
-  if (a < 0 || b < 0 || c < 0) return -1;
-  return a != 0 ? a : (b != 0 ? b : c);
+  const int d = read_device_error_bld_dalpha(clear);
+  if (a < 0 || b < 0 || c < 0 || d < 0) return -1;
+  return a != 0 ? a : (b != 0 ? b : (c != 0 ? c : d));
 }
 
 // Tuning hook used by the benchmark sweeps (key 0: CTAs per SM target,
@@ -363,7 +371,7 @@ int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t 
   a.msL = mask_sL;
   fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-  a.TL = pick_tl(L, ndt * B, steps, g_tuning.fwd_ctas_per_sm);
+  a.TL = pick_tl(L, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, 0));
   a.out_begin = 0;
   a.out_end = L;
   a.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
@@ -378,8 +386,15 @@ int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t 
 int64_t cta_diffusion_bwd_bld_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype, int steps, int causal) {
   (void)dtype;
   (void)causal;
-  if (B <= 0 || L <= 0 || D <= 0 || steps < 1 || steps > kMaxSteps) return 256;
-  return 256 + dalpha_max_ctas(B, L, D) * steps * static_cast<int64_t>(sizeof(float));
+  if (B <= 0 || L <= 0 || D <= 0 || steps < 1 || steps > kMaxSteps) return kWsHeaderBytes;
+  if (steps <= kDaMaxSteps) {
+    // march kernel: partials of up to ceil(L/32) x ceil(D/128) x B CTAs, then the
+    // group sums (f64, 8-byte aligned)
+    const int64_t ctas = ((L + 31) / 32) * ((D + kFwdDT - 1) / kFwdDT) * B;
+    const int64_t ngroups = std::min<int64_t>(kWsMaxGroups, (ctas + 31) / 32);
+    return kWsHeaderBytes + ctas * steps * 4 + 4 + ngroups * steps * 8;
+  }
+  return kWsHeaderBytes + dalpha_max_ctas(B, L, D) * steps * static_cast<int64_t>(sizeof(float));
 }
 
 int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, float* dalpha, void* workspace,
@@ -432,7 +447,7 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
     m.msL = mask_sL;
     fill_alpha(m, steps, alpha, alpha_dev, alpha_dev_dtype);
     const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-    m.TL = pick_tl(L, ndt * B, steps, g_tuning.fwd_ctas_per_sm);
+    m.TL = pick_tl(L, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, 1));
     m.out_begin = 0;
     m.out_end = L;
     m.y_quad_ok = quad_ok(grad_in, dtype, B, D, d_sB, d_sL) ? 1 : 0;
@@ -442,6 +457,57 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
     m.use_tma = make_map(&gm, grad_out, dtype, B, L, D, g_sB, g_sL, kFwdRC, kFwdDT) ? 1 : 0;
     m.use_tma_store = make_map(&dm, grad_in, dtype, B, L, D, d_sB, d_sL, kFwdRC, kFwdDT) ? 1 : 0;
     return launch_fwd(m, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), gm, dm, 1);
+  }
+  if (steps <= kDaMaxSteps) {
+    // d(alpha), steps 1..4: the one-warp march carrying both wavefronts
+    BldArgs m = blank_bld();
+    m.g = grad_out;
+    m.x = x;
+    m.y = grad_in;
+    m.gsB = g_sB;
+    m.gsL = g_sL;
+    m.xsB = x_sB;
+    m.xsL = x_sL;
+    m.ysB = d_sB;
+    m.ysL = d_sL;
+    m.L = L;
+    m.D = static_cast<int>(D);
+    m.nbatch = static_cast<int>(B);
+    m.global_len = L;
+    m.mask = mask;
+    m.mask_dtype = mask_dtype;
+    m.msB = mask_sB;
+    m.msL = mask_sL;
+    fill_alpha(m, steps, alpha, alpha_dev, alpha_dev_dtype);
+    const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
+    const int occ = bld_dalpha_ctas_per_sm(dtype, steps, causal ? 1 : 0);
+    m.TL = pick_tl(L, ndt * B, steps, occ > 0 ? std::min(g_tuning.fwd_ctas_per_sm, occ) : 8);
+    m.out_begin = 0;
+    m.out_end = L;
+    const int64_t ntl = (L + m.TL - 1) / m.TL;
+    if (ntl * ndt > 0x7fffffffLL || B > 65535 || ntl * ndt * B > 0x7fffffffLL)
+      return fail(CTA_EUNSUPPORTED, "grid too large (tiles %lld, D tiles %lld, batch %lld)", (long long)ntl,
+                  (long long)ndt, (long long)B);
+    m.num_ctas = static_cast<int>(ntl * ndt * B);
+    const int64_t per_group = 32 * ((m.num_ctas + 32LL * kWsMaxGroups - 1) / (32LL * kWsMaxGroups));
+    m.dalpha_group = static_cast<int>(per_group);
+    m.counter = static_cast<unsigned int*>(workspace);
+    m.dalpha_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeaderBytes);
+    m.dalpha = dalpha;
+    m.y_quad_ok = quad_ok(grad_in, dtype, B, D, d_sB, d_sL) ? 1 : 0;
+    CUtensorMap gm, xm, dm;
+    std::memset(&gm, 0, sizeof(gm));
+    std::memset(&xm, 0, sizeof(xm));
+    std::memset(&dm, 0, sizeof(dm));
+    const bool tg = make_map(&gm, grad_out, dtype, B, L, D, g_sB, g_sL, kFwdRC, kFwdDT);
+    const bool tx = make_map(&xm, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT);
+    m.use_tma = (tg && tx) ? 1 : 0;
+    m.use_tma_store = make_map(&dm, grad_in, dtype, B, L, D, d_sB, d_sL, kFwdRC, kFwdDT) ? 1 : 0;
+    dim3 grid(static_cast<unsigned>(ntl * ndt), 1u, static_cast<unsigned>(B));
+    const cudaError_t e =
+        launch_bld_dalpha(m, &gm, &xm, &dm, dtype, steps, causal ? 1 : 0, grid, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "bld backward (d(alpha)) launch");
+    return ok();
   }
   BldArgs a = blank_bld();
   a.g = grad_out;
@@ -479,7 +545,7 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
   if (da) {
     a.num_ctas = static_cast<int>(ntl * ndt * B);
     a.counter = static_cast<unsigned int*>(workspace);
-    a.dalpha_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+    a.dalpha_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeaderBytes);
     a.dalpha = dalpha;
   }
   const cudaError_t e = launch_bld_bwd(a, &gmap, &xmap, dtype, steps, causal ? 1 : 0, da ? 1 : 0, grid,
@@ -517,7 +583,7 @@ int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t
   // the waves balanced across unequal lengths (halo overhead 2*steps/TL)
   const int64_t avg = std::max<int64_t>(1, total_rows / nseq);
   a.TL = g_tuning.tl_override > 0
-             ? pick_tl(avg, ndt * nseq, steps, g_tuning.fwd_ctas_per_sm)
+             ? pick_tl(avg, ndt * nseq, steps, march_per_sm(dtype, steps, 0, 0))
              : static_cast<int>(std::min<int64_t>(512, std::max<int64_t>(64, ((avg / 8 + 15) / 16) * 16)));
   a.out_begin = 0;
   a.out_end = max_len;
@@ -590,7 +656,7 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
   for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
   a.TL = edge ? static_cast<int>(std::min<int64_t>(kBldMaxTL, ((oe - ob + kBldRC - 1) / kBldRC) * kBldRC))
-              : pick_tl(oe - ob, ndt * B, steps, g_tuning.fwd_ctas_per_sm);
+              : pick_tl(oe - ob, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, backward ? 1 : 0));
   a.out_begin = ob;
   a.out_end = oe;
   a.y_quad_ok = quad_ok(out, dtype, B, D, L_local * D, D) ? 1 : 0;

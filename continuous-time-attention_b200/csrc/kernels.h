@@ -33,6 +33,11 @@ constexpr int kFwdStages = 4;    // input chunks in flight
 constexpr int kFwdMinCtas = 20;  // register budget (one-warp CTAs per SM) of the shallow variants
 constexpr int kFwdOutSlots = 2;  // output staging chunks for the TMA stores
 constexpr int kBoxCols = 256;    // TMA box inner extent of the backward maps (max 256)
+// d(alpha) workspace: a fixed header of completion counters (so that no shape's
+// partial sums can land where another shape's counters live), then partials
+constexpr int64_t kWsHeaderBytes = 8192;
+constexpr int kWsMaxGroups = static_cast<int>(kWsHeaderBytes / 4) - 1;
+constexpr int kDaMaxSteps = 4;  // steps handled by the march d(alpha) kernel
 constexpr int kBldMaxWords = (kBldMaxTL + 2 * 2 * kMaxSteps + kBldRC + 31) / 32 + 1;
 
 struct BldArgs {
@@ -74,6 +79,7 @@ struct BldArgs {
   unsigned int* counter;   // zero on entry, left zero on exit
   float* dalpha;           // [steps] fp32 result
   int num_ctas;
+  int dalpha_group;        // CTAs per reduction group (march d(alpha) kernel)
 };
 
 // ---------------------------------------------------------------------------
@@ -101,12 +107,22 @@ struct BdlArgs {
 };
 
 // launchers (return cudaError_t of the launch)
+// resident one-warp CTAs per SM of a march kernel variant on the current device
+// (occupancy query, cached), or -1
+int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint);
 // march kernel: forward (adjoint = 0) or the adjoint without d(alpha) (adjoint = 1)
 cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, int dtype,
                            int steps, int causal, int adjoint, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bld_bwd(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap, int dtype,
                            int steps, int causal, int with_dalpha, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st);
+
+// march kernel with d(alpha), steps 1..kDaMaxSteps
+cudaError_t launch_bld_dalpha(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap,
+                              const CUtensorMap* ymap, int dtype, int steps, int causal, dim3 grid, cudaStream_t st);
+int bld_dalpha_ctas_per_sm(int dtype, int steps, int causal);
+size_t dalpha_smem_bytes(int dtype);
+int read_device_error_bld_dalpha(int clear);
 
 // sets the thread-local message returned by cta_last_error()
 void set_last_error(const char* fmt, ...) __attribute__((format(printf, 1, 2)));

@@ -20,8 +20,8 @@
 
 namespace {
 
-// 256 B header (the completion counter) + 65536 fp32 partial sums = 262400 B per device.
-constexpr int64_t kScratchHeader = 256;
+// Counter header (kWsHeaderBytes = 8 KiB) + 65536 fp32 partial sums = 270336 B per device.
+constexpr int64_t kScratchHeader = cta::kWsHeaderBytes;
 constexpr int64_t kScratchPartials = 65536;
 constexpr int64_t kScratchBytes = kScratchHeader + kScratchPartials * static_cast<int64_t>(sizeof(float));
 
@@ -69,10 +69,10 @@ extern "C" int cta_diffusion_bwd_bld_noalloc(const void* grad_out, void* grad_in
       cta::set_last_error("cta_diffusion_bwd_bld_noalloc: could not look up the device address of the scratch");
       return rc;
     }
-    // the completion counter must start at zero; the partials are rewritten by every call
+    // the completion counters must start at zero; the partials are rewritten by every call
     const cudaError_t e = cudaMemsetAsync(scratch, 0, kScratchHeader, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {
-      cta::set_last_error("cta_diffusion_bwd_bld_noalloc: clearing the scratch counter failed: %s",
+      cta::set_last_error("cta_diffusion_bwd_bld_noalloc: clearing the scratch counters failed: %s",
                           cudaGetErrorString(e));
       return CTA_ECUDA;
     }

@@ -26,7 +26,7 @@ BUILD_DIR = SRC_ROOT / "_build"
 LIB_NAME = "libcta_stencil.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["capi.cu", "bld_fwd.cu", "bld_bwd.cu", "stencil_bdl.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "bld_fwd.cu", "bld_bwd.cu", "bld_dalpha.cu", "stencil_bdl.cu", "noalloc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = [
     "-O3",
@@ -77,17 +77,27 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None, d
     build_dir.mkdir(parents=True, exist_ok=True)
     incs = ["-I", str(INCLUDE), "-I", str(CSRC)] + [f"-D{d}" for d in defines]
 
+    headers = [f for f in _inputs() if f.suffix != ".cu"]
+    newest_header = max((f.stat().st_mtime for f in headers), default=0.0)
+
     def compile_one(name: str) -> Path:
         obj = build_dir / (Path(name).stem + ".o")
         cmd = [nvcc, *ARCH_FLAGS, *CFLAGS, *incs, "-c", str(CSRC / name), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), flush=True)
+        # an object is reused when it is newer than its source and every header
+        # and was built by the same command
+        stamp = obj.with_suffix(".cmd")
+        if (not force and not verbose and obj.exists() and stamp.exists() and stamp.read_text() == " ".join(cmd)
+                and obj.stat().st_mtime > max((CSRC / name).stat().st_mtime, newest_header)):
+            return obj
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"nvcc failed for {name}:\n{res.stdout}\n{res.stderr}")
         if verbose and (res.stdout or res.stderr):
             print(res.stdout + res.stderr, flush=True)
+        stamp.write_text(" ".join(cmd))
         return obj
 
     with ThreadPoolExecutor(max_workers=jobs or min(len(SOURCES), os.cpu_count() or 1)) as ex:

@@ -62,6 +62,17 @@ def _mask_args(mask: Optional[torch.Tensor], B: int, L: int, device: torch.devic
     return mask, _lib.mask_code(mask.dtype), mask.stride(0), mask.stride(1)
 
 
+def _out(out: Optional[torch.Tensor], shape, like: torch.Tensor, contiguous: bool = False) -> torch.Tensor:
+    """The caller's output buffer after checking it, or a new one."""
+    if out is None:
+        return torch.empty(shape, dtype=like.dtype, device=like.device)
+    if tuple(out.shape) != tuple(shape) or out.dtype != like.dtype or out.device != like.device:
+        raise ValueError(f"out must be {tuple(shape)} {like.dtype} on {like.device}")
+    if out.stride(-1) != 1 or (contiguous and not out.is_contiguous()):
+        raise ValueError("out must have a contiguous last axis" + (" and be contiguous" if contiguous else ""))
+    return out
+
+
 # ---------------------------------------------------------------------------
 # [B, D, L]
 # ---------------------------------------------------------------------------
@@ -82,7 +93,7 @@ def bdl(
     if x.stride(2) != 1 or x.stride(0) != x.shape[1] * x.stride(1):
         x = x.contiguous()
     B, D, L = x.shape
-    y = torch.empty_like(x, memory_format=torch.contiguous_format) if out is None else out
+    y = _out(out, x.shape, x, contiguous=True)
     fa, pa, pcode, keep = _alpha_args(alphas, steps, x.device)
     m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
     lib = _lib.load()
@@ -96,13 +107,14 @@ def bdl(
     return y
 
 
-def bdl_simple(x: torch.Tensor, alpha: float, steps: int, backward: bool = False) -> torch.Tensor:
+def bdl_simple(x: torch.Tensor, alpha: float, steps: int, backward: bool = False,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Reference kernel API path: one host alpha, no mask, non-causal."""
     _require_cuda(x, "x")
     if not x.is_contiguous():
         x = x.contiguous()
     B, D, L = x.shape
-    y = torch.empty_like(x)
+    y = _out(out, x.shape, x, contiguous=True)
     lib = _lib.load()
     fn = lib.cta_diffusion_bwd_bdl if backward else lib.cta_diffusion_fwd_bdl
     with _lib.on_device(x):
@@ -136,7 +148,7 @@ def bld_forward(
         raise ValueError("x must have shape (B, L, D)")
     x = _bld_view(x)
     B, L, D = x.shape
-    y = torch.empty((B, L, D), dtype=x.dtype, device=x.device) if out is None else out
+    y = _out(out, (B, L, D), x)
     fa, pa, pcode, keep = _alpha_args(alphas, steps, x.device)
     m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
     lib = _lib.load()
@@ -177,12 +189,13 @@ def bld_backward(
     causal: bool = False,
     mask: Optional[torch.Tensor] = None,
     need_dalpha: bool = False,
+    out: Optional[torch.Tensor] = None,
 ):
     """grad_in = A_1^T .. A_S^T grad_out; with need_dalpha also d(alpha_k) (fp32 [steps])."""
     _require_cuda(grad_out, "grad_out")
     g = _bld_view(grad_out)
     B, L, D = g.shape
-    dx = torch.empty((B, L, D), dtype=g.dtype, device=g.device)
+    dx = _out(out, (B, L, D), g)
     fa, pa, pcode, keep = _alpha_args(alphas, steps, g.device)
     m, mcode, msb, msl = _mask_args(mask, B, L, g.device)
     lib = _lib.load()
@@ -235,7 +248,7 @@ def varlen_forward(
     if not cu_seqlens.is_contiguous():
         cu_seqlens = cu_seqlens.contiguous()
     T, D = x.shape
-    y = torch.empty((T, D), dtype=x.dtype, device=x.device) if out is None else out
+    y = _out(out, (T, D), x, contiguous=True)
     nseq = cu_seqlens.numel() - 1
     lib = _lib.load()
     with _lib.on_device(x):

@@ -120,13 +120,13 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
  * reference).  For callers that cannot provide fresh device memory -- an engine
  * that has reserved almost the whole GPU for its own pool, or a latency-critical
  * path that must not pay cudaMalloc's implicit synchronisation -- the d(alpha)
- * scratch comes from a fixed array inside the library (262400 bytes per device,
+ * scratch comes from a fixed array inside the library (270336 bytes per device,
  * held until the process exits).  Same arguments as cta_diffusion_bwd_bld minus
  * the workspace.  Shapes whose reduction needs more scratch than that (more than
  * 65536 CTA x step partial sums) are rejected with CTA_EINVAL.  The first call on
  * a device looks up the array's device address; make that first call before
  * any stream capture.  The array is shared by every call on a device and keeps
- * the previous call's contents (the completion counter is cleared at the start
+ * the previous call's contents (the completion counters are cleared at the start
  * of each call), so calls whose work overlaps on the GPU race and must be
  * serialised by the caller.  Calls no cudaMalloc, cudaFree or allocating
  * library routine. */

@@ -125,6 +125,56 @@ def test_backward_dalpha_repeatable():
     assert torch.equal(r1, r2)  # deterministic reduction, workspace reusable
 
 
+def test_out_buffers():
+    """Caller-provided outputs: written in place and checked for shape and dtype."""
+    torch.manual_seed(8)
+    ops = _ops()
+    x = torch.randn(2, 300, 264, device="cuda", dtype=torch.bfloat16)
+    g = torch.randn_like(x)
+    y = torch.full_like(x, 7.0)
+    assert ops.bld_forward(x, [0.1] * 4, 4, out=y) is y
+    assert torch.equal(y, ops.bld_forward(x, [0.1] * 4, 4))
+    dx = torch.full_like(x, 7.0)
+    r, _ = ops.bld_backward(g, [0.1] * 4, 4, out=dx)
+    assert r is dx and torch.equal(dx, ops.bld_backward(g, [0.1] * 4, 4)[0])
+    xt = x.transpose(1, 2).contiguous()
+    yt = torch.empty_like(xt)
+    assert ops.bdl_simple(xt, 0.1, 4, out=yt) is yt
+    assert torch.equal(yt, ops.bdl_simple(xt, 0.1, 4))
+    with pytest.raises(ValueError):
+        ops.bld_forward(x, [0.1] * 4, 4, out=torch.empty(2, 300, 263, device="cuda", dtype=torch.bfloat16))
+    with pytest.raises(ValueError):
+        ops.bld_backward(g, [0.1] * 4, 4, out=torch.empty_like(x, dtype=torch.float32))
+    with pytest.raises(ValueError):
+        ops.bdl_simple(xt, 0.1, 4, out=torch.empty_like(x).transpose(1, 2))
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_dalpha_tiling_invariance(causal):
+    """d(alpha) through more CTAs than first-level reduction groups of 32 can
+    hold (65536 CTAs, groups of 64), against the default tiling: dx bit-identical,
+    d(alpha) equal up to the summation order (fp32 [32, 65536, 128])."""
+    from cta_b200 import _lib
+    torch.manual_seed(9)
+    ops = _ops()
+    B, L, D = 32, 65536, 128
+    # coherent data (a periodic parabola along L, a positive gradient), so that
+    # d(alpha) is not a cancelling sum and its rounding stays near fp32 epsilon
+    rows = (torch.arange(L, device="cuda", dtype=torch.float32) % 64 - 32) ** 2 / 1024
+    x = (rows[None, :, None] + 1e-3 * torch.randn(B, L, D, device="cuda")).contiguous()
+    g = torch.rand_like(x)
+    al = [0.1, 0.05, 0.12, 0.02]
+    prev = _lib.set_tuning(1, 32)
+    try:
+        dx1, da1 = ops.bld_backward(g, al, 4, x=x, causal=causal, need_dalpha=True)
+    finally:
+        _lib.set_tuning(1, prev)
+    dx2, da2 = ops.bld_backward(g, al, 4, x=x, causal=causal, need_dalpha=True)
+    assert torch.equal(dx1, dx2)
+    assert (da1 - da2).abs().max().item() <= 1e-5 * da2.abs().max().item(), (da1, da2)
+    assert _lib.device_error() == 0
+
+
 @pytest.mark.parametrize("steps", [1, 2, 3, 4, 8])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_varlen_reference_rule(steps, dtype):
