@@ -17,7 +17,7 @@
 // for the causal stencil), so a lane keeps two rows of state per level in
 // registers and every intermediate level stays on chip.  Input rows arrive in
 // shared memory through a ring of TMA tile loads (8 rows x 128 columns per
-// chunk, 4 chunks in flight, one mbarrier per slot); finished rows are staged
+// chunk, 3 chunks in flight, one mbarrier per slot); finished rows are staged
 // in shared memory and leave through TMA tile stores, 8 rows at a time.  HBM
 // traffic is one read of the input (halo rows are re-read from L2 by the
 // neighbouring tile) and one write of the output.
@@ -66,16 +66,17 @@ __device__ void fill_fwd_chunk(const BldArgs& a, const Seg& s, int64_t jrow0, in
 // each of its two column pairs (the adjoint also one or two rows of g), so its
 // register need grows with `steps`, and fastest for the causal adjoint.  The
 // minimum resident CTAs per SM handed to __launch_bounds__ is the largest of
-// 20/16/12/8 (5/4/3/2 warps per SM sub-partition, whose register file holds
-// 16384 registers) at which ptxas compiles the variant without spilling (checked
-// with -Xptxas -v for every variant); the host sizes the grid from the
-// occupancy the variant really gets (bld_march_ctas_per_sm).
+// 16/12/8 (4/3/2 warps per SM sub-partition, whose register file holds 16384
+// registers) at which ptxas compiles the variant without spilling, checked with
+// -Xptxas -v for every variant (only the 16-bit steps-8 forward and causal
+// adjoint keep a few bytes of spill at 168 and 255 registers); the host sizes
+// the grid from the occupancy the variant really gets (bld_march_ctas_per_sm).
 template <typename T, int S, bool CAUSAL, bool ADJ>
 constexpr int march_min_ctas() {
   constexpr bool F32 = sizeof(T) == 4;
   if (!ADJ) return S <= 4 ? kFwdMinCtas : (S == 5 || (S == 6 && F32)) ? 16 : 12;
-  if (!CAUSAL) return S <= (F32 ? 2 : 3) ? kFwdMinCtas : S <= 5 ? 16 : 12;
-  return S <= 2 ? kFwdMinCtas : S <= (F32 ? 4 : 3) ? 16 : S <= 5 ? 12 : 8;
+  if (!CAUSAL) return S <= 3 ? kFwdMinCtas : S <= 5 ? 16 : (S == 8 && F32) ? 8 : 12;
+  return S <= 3 ? (kFwdMinCtas < 16 ? kFwdMinCtas : 16) : S <= 5 ? 12 : 8;
 }
 
 template <typename T, int S, bool CAUSAL, bool ADJ>
@@ -277,10 +278,17 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
     constexpr int KIND = decltype(kind_tag)::value;
     const int t0 = c * kFwdRC;
     T* st = stage + ((c - NPRO) & 1) * CHUNK + soff;
+    // the chunk's rows are read from shared memory up front (CTA_FWD_PRELOAD=1)
+    // or as each row is reached
+    V in[kFwdRC];
+    if constexpr (CTA_FWD_PRELOAD) {
+#pragma unroll
+      for (int i = 0; i < kFwdRC; ++i) in[i] = *reinterpret_cast<const V*>(buf + soff + i * kFwdDT);
+    }
     static_for<kFwdRC>([&](auto I) {
       constexpr int i = decltype(I)::value;
       pf2 xa, xb;
-      Q::split(*reinterpret_cast<const V*>(buf + soff + i * kFwdDT), xa, xb);
+      Q::split(CTA_FWD_PRELOAD ? in[i] : *reinterpret_cast<const V*>(buf + soff + i * kFwdDT), xa, xb);
       if constexpr (KIND < NPRO) {
         step_row(slow_tag, std::integral_constant<int, KIND * kFwdRC + i>{}, jb + t0 + i, xa, xb);
       } else {

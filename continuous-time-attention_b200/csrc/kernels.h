@@ -29,8 +29,17 @@ constexpr int kFwdThreads = 32;
 constexpr int kFwdVec = CTA_FWD_VEC;  // columns per lane: 4 (two packed pairs) or 2 (one pair)
 constexpr int kFwdDT = 32 * kFwdVec;
 constexpr int kFwdRC = 8;
-constexpr int kFwdStages = 4;    // input chunks in flight
-constexpr int kFwdMinCtas = 20;  // register budget (one-warp CTAs per SM) of the shallow variants
+#ifndef CTA_FWD_STAGES
+#define CTA_FWD_STAGES 3
+#endif
+#ifndef CTA_FWD_PRELOAD
+#define CTA_FWD_PRELOAD 1
+#endif
+#ifndef CTA_FWD_MIN_CTAS
+#define CTA_FWD_MIN_CTAS 16
+#endif
+constexpr int kFwdStages = CTA_FWD_STAGES;     // input chunks in flight
+constexpr int kFwdMinCtas = CTA_FWD_MIN_CTAS;  // register budget (one-warp CTAs per SM) of the shallow variants
 constexpr int kFwdOutSlots = 2;  // output staging chunks for the TMA stores
 constexpr int kBoxCols = 256;    // TMA box inner extent of the backward maps (max 256)
 // d(alpha) workspace: a fixed header of completion counters (so that no shape's
