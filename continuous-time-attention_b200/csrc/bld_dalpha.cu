@@ -75,19 +75,26 @@ constexpr size_t da_smem() {
 }
 
 // Plain-load fill of one chunk ([8][128]) of a [B, L, D] stream, for tensors
-// TMA cannot address.
+// TMA cannot address and for L-shard edges: rows before / after the local
+// shard come from the halo buffers lo / hi ([nbatch, nlo|nhi, D]), if given.
 template <typename T>
-__device__ void fill_da_chunk(const BldArgs& a, const void* src, int64_t sB, int64_t sL, const Seg& s,
-                              int64_t jrow0, int d0, T* dst) {
+__device__ void fill_da_chunk(const BldArgs& a, const void* src, int64_t sB, int64_t sL, const void* lo, int nlo,
+                              const void* hi, int nhi, const Seg& s, int64_t jrow0, int d0, T* dst) {
   const T zero = Elem<T>::from_f(0.f);
   for (int idx = threadIdx.x; idx < kFwdRC * kFwdDT; idx += kFwdThreads) {
     const int i = idx / kFwdDT;
     const int cc = idx - i * kFwdDT;
     const int64_t tr = s.row0 + jrow0 + i;
     const int col = d0 + cc;
-    T v = zero;
-    if (tr >= 0 && tr < a.L && col < a.D) v = static_cast<const T*>(src)[static_cast<int64_t>(s.bcoord) * sB + tr * sL + col];
-    dst[i * kFwdDT + cc] = v;
+    const T* rowp = nullptr;
+    if (tr >= 0 && tr < a.L) {
+      rowp = static_cast<const T*>(src) + static_cast<int64_t>(s.bcoord) * sB + tr * sL;
+    } else if (tr < 0 && lo != nullptr && tr >= -nlo) {
+      rowp = static_cast<const T*>(lo) + (static_cast<int64_t>(s.bcoord) * nlo + (nlo + tr)) * a.D;
+    } else if (tr >= a.L && hi != nullptr && tr - a.L < nhi) {
+      rowp = static_cast<const T*>(hi) + (static_cast<int64_t>(s.bcoord) * nhi + (tr - a.L)) * a.D;
+    }
+    dst[i * kFwdDT + cc] = (rowp != nullptr && col < a.D) ? rowp[col] : zero;
   }
 }
 
@@ -371,8 +378,10 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
       if (use_tma) {
         if (!mbar_wait_bounded(&full_bar[slot], (c / NST) & 1)) e = 1;
       } else {
-        fill_da_chunk<T>(a, a.g, a.gsB, a.gsL, sg, jbg + c * kFwdRC, d0, gbuf);
-        fill_da_chunk<T>(a, a.x, a.xsB, a.xsL, sg, jbx + c * kFwdRC, d0, xbuf);
+        fill_da_chunk<T>(a, a.g, a.gsB, a.gsL, a.g_lo_ext, a.g_hext_lo, a.g_hi_ext, a.g_hext_hi, sg,
+                         jbg + c * kFwdRC, d0, gbuf);
+        fill_da_chunk<T>(a, a.x, a.xsB, a.xsL, a.lo_ext, a.hext_lo, a.hi_ext, a.hext_hi, sg, jbx + c * kFwdRC, d0,
+                         xbuf);
         __syncwarp();
       }
       if (!e) march_chunk(slow_tag, kind_tag, c, gbuf, xbuf);
@@ -476,7 +485,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     for (int g = tid; g < ngroups; g += 32) v += __ldcg(gsum + static_cast<int64_t>(g) * S + k);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (tid == 0) a.dalpha[k] = static_cast<float>(v);
+    if (tid == 0) a.dalpha[k] = static_cast<float>(a.dalpha_accumulate ? static_cast<double>(a.dalpha[k]) + v : v);
   }
   if (tid == 0) *a.counter = 0u;
 }

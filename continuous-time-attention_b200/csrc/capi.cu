@@ -226,6 +226,41 @@ int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int
   return ok();
 }
 
+// Grid, workspace layout, tensor maps and launch of the march d(alpha) kernel
+// over output rows [m.out_begin, m.out_end) of m's streams (g, x -> y); `tiled`
+// = TMA may address the three tensors (dense, whole-tensor rows).
+int launch_dalpha_march(BldArgs& m, int dtype, int steps, int causal, int64_t B, int64_t L, int64_t D,
+                        void* workspace, float* dalpha, bool accumulate, bool tiled, cudaStream_t st) {
+  const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
+  const int64_t rows = m.out_end - m.out_begin;
+  if (rows <= 0) return ok();
+  const int occ = bld_dalpha_ctas_per_sm(dtype, steps, causal);
+  m.TL = pick_tl(rows, ndt * B, steps, occ > 0 ? std::min(g_tuning.fwd_ctas_per_sm, occ) : 8);
+  const int64_t ntl = (rows + m.TL - 1) / m.TL;
+  if (ntl * ndt > 0x7fffffffLL || B > 65535 || ntl * ndt * B > 0x7fffffffLL)
+    return fail(CTA_EUNSUPPORTED, "grid too large (tiles %lld, D tiles %lld, batch %lld)", (long long)ntl,
+                (long long)ndt, (long long)B);
+  m.num_ctas = static_cast<int>(ntl * ndt * B);
+  m.dalpha_group = static_cast<int>(32 * ((m.num_ctas + 32LL * kWsMaxGroups - 1) / (32LL * kWsMaxGroups)));
+  m.dalpha_accumulate = accumulate ? 1 : 0;
+  m.counter = static_cast<unsigned int*>(workspace);
+  m.dalpha_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeaderBytes);
+  m.dalpha = dalpha;
+  m.y_quad_ok = quad_ok(m.y, dtype, B, D, m.ysB, m.ysL) ? 1 : 0;
+  CUtensorMap gm, xm, dm;
+  std::memset(&gm, 0, sizeof(gm));
+  std::memset(&xm, 0, sizeof(xm));
+  std::memset(&dm, 0, sizeof(dm));
+  const bool tg = tiled && make_map(&gm, m.g, dtype, B, L, D, m.gsB, m.gsL, kFwdRC, kFwdDT);
+  const bool tx = tiled && make_map(&xm, m.x, dtype, B, L, D, m.xsB, m.xsL, kFwdRC, kFwdDT);
+  m.use_tma = (tg && tx) ? 1 : 0;
+  m.use_tma_store = make_map(&dm, m.y, dtype, B, L, D, m.ysB, m.ysL, kFwdRC, kFwdDT) ? 1 : 0;
+  dim3 grid(static_cast<unsigned>(ntl * ndt), 1u, static_cast<unsigned>(B));
+  const cudaError_t e = launch_bld_dalpha(m, &gm, &xm, &dm, dtype, steps, causal, grid, st);
+  if (e != cudaSuccess) return cuda_fail(e, "bld backward (d(alpha)) launch");
+  return ok();
+}
+
 int64_t dalpha_max_ctas(int64_t B, int64_t L, int64_t D) {
   const int64_t ntl = (L + 31) / 32;  // pick_tl never goes below 32 rows
   const int64_t ndt = (D + kBldDT - 1) / kBldDT;
@@ -479,35 +514,10 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
     m.msB = mask_sB;
     m.msL = mask_sL;
     fill_alpha(m, steps, alpha, alpha_dev, alpha_dev_dtype);
-    const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-    const int occ = bld_dalpha_ctas_per_sm(dtype, steps, causal ? 1 : 0);
-    m.TL = pick_tl(L, ndt * B, steps, occ > 0 ? std::min(g_tuning.fwd_ctas_per_sm, occ) : 8);
     m.out_begin = 0;
     m.out_end = L;
-    const int64_t ntl = (L + m.TL - 1) / m.TL;
-    if (ntl * ndt > 0x7fffffffLL || B > 65535 || ntl * ndt * B > 0x7fffffffLL)
-      return fail(CTA_EUNSUPPORTED, "grid too large (tiles %lld, D tiles %lld, batch %lld)", (long long)ntl,
-                  (long long)ndt, (long long)B);
-    m.num_ctas = static_cast<int>(ntl * ndt * B);
-    const int64_t per_group = 32 * ((m.num_ctas + 32LL * kWsMaxGroups - 1) / (32LL * kWsMaxGroups));
-    m.dalpha_group = static_cast<int>(per_group);
-    m.counter = static_cast<unsigned int*>(workspace);
-    m.dalpha_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeaderBytes);
-    m.dalpha = dalpha;
-    m.y_quad_ok = quad_ok(grad_in, dtype, B, D, d_sB, d_sL) ? 1 : 0;
-    CUtensorMap gm, xm, dm;
-    std::memset(&gm, 0, sizeof(gm));
-    std::memset(&xm, 0, sizeof(xm));
-    std::memset(&dm, 0, sizeof(dm));
-    const bool tg = make_map(&gm, grad_out, dtype, B, L, D, g_sB, g_sL, kFwdRC, kFwdDT);
-    const bool tx = make_map(&xm, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT);
-    m.use_tma = (tg && tx) ? 1 : 0;
-    m.use_tma_store = make_map(&dm, grad_in, dtype, B, L, D, d_sB, d_sL, kFwdRC, kFwdDT) ? 1 : 0;
-    dim3 grid(static_cast<unsigned>(ntl * ndt), 1u, static_cast<unsigned>(B));
-    const cudaError_t e =
-        launch_bld_dalpha(m, &gm, &xm, &dm, dtype, steps, causal ? 1 : 0, grid, static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) return cuda_fail(e, "bld backward (d(alpha)) launch");
-    return ok();
+    return launch_dalpha_march(m, dtype, steps, causal ? 1 : 0, B, L, D, workspace, dalpha, false, true,
+                               static_cast<cudaStream_t>(stream));
   }
   BldArgs a = blank_bld();
   a.g = grad_out;
@@ -667,6 +677,90 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
   a.use_tma_store = make_map(&omap, out, dtype, B, L_local, D, L_local * D, D, kFwdRC, kFwdDT) ? 1 : 0;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, oe - ob, st, map, omap, backward ? 1 : 0);
+}
+
+int cta_diffusion_shard_bld_dalpha(const void* grad_out, const void* x, void* grad_in, float* dalpha,
+                                   void* workspace, int64_t workspace_bytes, int64_t B, int64_t L_local, int64_t D,
+                                   int64_t pos_offset, int64_t global_len, const void* g_lo_halo, int64_t g_lo_rows,
+                                   const void* g_hi_halo, int64_t g_hi_rows, const void* x_lo_halo,
+                                   int64_t x_lo_rows, const void* x_hi_halo, int64_t x_hi_rows, int part, int dtype,
+                                   int steps, int causal, const float* alpha, void* stream) {
+  int rc = check_common(dtype, steps);
+  if (rc) return rc;
+  if (steps > kDaMaxSteps)
+    return fail(CTA_EUNSUPPORTED, "sharded d(alpha) supports steps 1..%d, got %d", kDaMaxSteps, steps);
+  if (alpha == nullptr) return fail(CTA_EINVAL, "alpha: need host coefficients");
+  if (B < 0 || L_local < 0 || D < 0 || pos_offset < 0) return fail(CTA_EINVAL, "negative shape");
+  if (B == 0 || L_local == 0 || D == 0) return ok();
+  if (grad_out == nullptr || x == nullptr || grad_in == nullptr || dalpha == nullptr)
+    return fail(CTA_EINVAL, "null tensor pointer");
+  if (pos_offset + L_local > global_len) return fail(CTA_EINVAL, "shard exceeds the global sequence");
+  if (global_len < 3) return fail(CTA_EINVAL, "global length < 3 is the identity; handled by the caller");
+  if (workspace == nullptr || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(CTA_EINVAL, "dalpha needs a 256-byte aligned workspace");
+  const int64_t need = cta_diffusion_bwd_bld_workspace_bytes(B, L_local, D, dtype, steps, causal);
+  if (workspace_bytes < need)
+    return fail(CTA_EINVAL, "workspace too small: %lld < %lld bytes", (long long)workspace_bytes, (long long)need);
+  // rows each stream needs beyond an output row: g below (and above when
+  // non-causal), x above (and below when non-causal)
+  const int glo = causal ? 0 : steps, ghi = causal ? 2 * steps : steps;
+  const int xlo = causal ? 2 * steps : steps, xhi = causal ? 0 : steps;
+  const int hl = std::max(glo, xlo), hr = std::max(ghi, xhi);
+  const bool has_lo = pos_offset > 0;
+  const bool has_hi = pos_offset + L_local < global_len;
+  const int64_t ib = has_lo ? std::min<int64_t>(hl, L_local) : 0;
+  const int64_t ie = has_hi ? std::max<int64_t>(L_local - hr, ib) : L_local;
+  int64_t ob = 0, oe = 0;
+  if (part == CTA_SHARD_INTERIOR) {
+    ob = ib;
+    oe = ie;
+  } else if (part == CTA_SHARD_LO_EDGE) {
+    ob = 0;
+    oe = ib;
+  } else if (part == CTA_SHARD_HI_EDGE) {
+    ob = ie;
+    oe = L_local;
+  } else {
+    return fail(CTA_EINVAL, "bad shard part %d", part);
+  }
+  if (oe <= ob) return ok();
+  const bool edge = part != CTA_SHARD_INTERIOR;
+  if (edge) {
+    if (has_lo && ((glo > 0 && (g_lo_halo == nullptr || g_lo_rows < glo)) ||
+                   (xlo > 0 && (x_lo_halo == nullptr || x_lo_rows < xlo))))
+      return fail(CTA_EINVAL, "lo halos missing or shorter than %d (g) / %d (x) rows", glo, xlo);
+    if (has_hi && ((ghi > 0 && (g_hi_halo == nullptr || g_hi_rows < ghi)) ||
+                   (xhi > 0 && (x_hi_halo == nullptr || x_hi_rows < xhi))))
+      return fail(CTA_EINVAL, "hi halos missing or shorter than %d (g) / %d (x) rows", ghi, xhi);
+    for (int64_t r : {g_lo_rows, g_hi_rows, x_lo_rows, x_hi_rows})
+      if (r < 0 || r > (1 << 20)) return fail(CTA_EINVAL, "bad halo row counts");
+  }
+  BldArgs m = blank_bld();
+  m.g = grad_out;
+  m.x = x;
+  m.y = grad_in;
+  m.gsB = m.xsB = m.ysB = L_local * D;
+  m.gsL = m.xsL = m.ysL = D;
+  m.L = L_local;
+  m.D = static_cast<int>(D);
+  m.nbatch = static_cast<int>(B);
+  m.pos_offset = pos_offset;
+  m.global_len = global_len;
+  if (edge) {
+    m.g_lo_ext = (has_lo && g_lo_rows > 0) ? g_lo_halo : nullptr;
+    m.g_hi_ext = (has_hi && g_hi_rows > 0) ? g_hi_halo : nullptr;
+    m.g_hext_lo = m.g_lo_ext ? static_cast<int>(g_lo_rows) : 0;
+    m.g_hext_hi = m.g_hi_ext ? static_cast<int>(g_hi_rows) : 0;
+    m.lo_ext = (has_lo && x_lo_rows > 0) ? x_lo_halo : nullptr;
+    m.hi_ext = (has_hi && x_hi_rows > 0) ? x_hi_halo : nullptr;
+    m.hext_lo = m.lo_ext ? static_cast<int>(x_lo_rows) : 0;
+    m.hext_hi = m.hi_ext ? static_cast<int>(x_hi_rows) : 0;
+  }
+  fill_alpha(m, steps, alpha, nullptr, 0);
+  m.out_begin = ob;
+  m.out_end = oe;
+  return launch_dalpha_march(m, dtype, steps, causal ? 1 : 0, B, L_local, D, workspace, dalpha, true, !edge,
+                             static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

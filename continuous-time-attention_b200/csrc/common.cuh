@@ -307,7 +307,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
-// 3-D tiled TMA load (no multicast): coordinates are (column, row, batch).
+// 3-D tiled TMA load into this CTA's own shared memory: coordinates are (column, row, batch).
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {
   asm volatile(
@@ -317,7 +317,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// 3-D tiled TMA store from shared memory (no multicast, no reduction); the
+// 3-D tiled TMA store from shared memory (plain store, no reduction); the
 // coordinates must be non-negative, elements past the tensor end are dropped.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
   asm volatile(

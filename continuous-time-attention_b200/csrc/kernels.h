@@ -89,6 +89,12 @@ struct BldArgs {
   float* dalpha;           // [steps] fp32 result
   int num_ctas;
   int dalpha_group;        // CTAs per reduction group (march d(alpha) kernel)
+  int dalpha_accumulate;   // add the result to dalpha[] instead of overwriting it
+  // L-shard halos of the gradient stream for the d(alpha) kernel (lo_ext/hi_ext
+  // above hold the x stream's): [nbatch, g_hext_lo|hi, D]
+  const void* g_lo_ext;
+  const void* g_hi_ext;
+  int g_hext_lo, g_hext_hi;
 };
 
 // ---------------------------------------------------------------------------

@@ -291,3 +291,50 @@ def shard_part(
             int(backward), float(alpha), st.cuda_stream,
         )
     _lib.check(rc)
+
+
+def shard_part_dalpha(
+    g_local: torch.Tensor,
+    x_local: torch.Tensor,
+    dx_out: torch.Tensor,
+    dalpha: torch.Tensor,
+    part: int,
+    *,
+    pos_offset: int,
+    global_len: int,
+    alphas: Sequence[float],
+    steps: int,
+    causal: bool = False,
+    g_lo: Optional[torch.Tensor] = None,
+    g_hi: Optional[torch.Tensor] = None,
+    x_lo: Optional[torch.Tensor] = None,
+    x_hi: Optional[torch.Tensor] = None,
+    stream: Optional[torch.cuda.Stream] = None,
+) -> None:
+    """One launch over a part of an L-shard's backward with d(alpha): writes the
+    part's rows of dx_out and ADDS the part's d(alpha) sum to `dalpha` (fp32 [steps])."""
+    B, Lloc, D = g_local.shape
+    if tuple(x_local.shape) != (B, Lloc, D) or x_local.dtype != g_local.dtype:
+        raise ValueError("x_local must match g_local in shape and dtype")
+    if dalpha.dtype != torch.float32 or dalpha.numel() < steps or not dalpha.is_contiguous():
+        raise ValueError("dalpha must be a contiguous fp32 tensor of at least `steps` entries")
+    for h in (g_lo, g_hi, x_lo, x_hi):
+        if h is not None and (not h.is_contiguous() or h.shape[0] != B or h.shape[2] != D or h.dtype != g_local.dtype):
+            raise ValueError("halo must be a contiguous (B, rows, D) tensor of the shard's dtype")
+    rows = [h.shape[1] if h is not None else 0 for h in (g_lo, g_hi, x_lo, x_hi)]
+    if len(alphas) != steps:
+        raise ValueError("need one alpha per step")
+    st = stream if stream is not None else torch.cuda.current_stream(g_local.device)
+    lib = _lib.load()
+    code = _lib.dtype_code(g_local.dtype)
+    ws_bytes = int(lib.cta_diffusion_bwd_bld_workspace_bytes(B, Lloc, D, code, steps, int(causal)))
+    with torch.cuda.stream(st):
+        ws = _workspace(g_local.device, ws_bytes)
+    with _lib.on_device(g_local):
+        rc = lib.cta_diffusion_shard_bld_dalpha(
+            _lib.ptr(g_local), _lib.ptr(x_local), _lib.ptr(dx_out), _lib.ptr(dalpha), _lib.ptr(ws), ws_bytes, B, Lloc,
+            D, int(pos_offset), int(global_len), _lib.ptr(g_lo), rows[0], _lib.ptr(g_hi), rows[1], _lib.ptr(x_lo),
+            rows[2], _lib.ptr(x_hi), rows[3], int(part), code, steps, int(causal),
+            _lib.float_array([float(a) for a in alphas]), st.cuda_stream,
+        )
+    _lib.check(rc)

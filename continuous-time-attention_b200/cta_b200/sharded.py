@@ -16,9 +16,13 @@ Only the two global ends of the sequence use the copy boundary; shard edges
 are interior rows.  The reference has no multi-device path (it runs the
 stencil on one device); results are identical to the unsharded stencil.
 
+The backward with d(alpha) (learnable per-step alphas) exchanges halos of both
+the gradient and the forward input x, sums each rank's d(alpha) over its own
+rows (interior + edge parts, in that order) and all-reduces the `steps` sums.
+
 The compute step is injectable (``compute=``) so that the exchange protocol can
 be exercised on CPU ranks (gloo) in the tests; the default is the sm_100a
-kernels through :func:`cta_b200.ops.shard_part`.
+kernels through :func:`cta_b200.ops.shard_part` / ``shard_part_dalpha``.
 """
 from __future__ import annotations
 
@@ -30,7 +34,7 @@ import torch.distributed as dist
 
 from . import _lib
 
-__all__ = ["ShardSpec", "halo_rows", "sharded_diffusion", "even_shards"]
+__all__ = ["ShardSpec", "halo_rows", "sharded_diffusion", "sharded_diffusion_backward_dalpha", "even_shards"]
 
 
 @dataclass(frozen=True)
@@ -157,3 +161,127 @@ def sharded_diffusion(
     compute(_lib.SHARD_LO_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
     compute(_lib.SHARD_HI_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
     return out
+
+
+def halo_rows_dalpha(steps: int, causal: bool) -> dict[str, tuple[int, int]]:
+    """Rows (before, after) the shard that the backward with d(alpha) needs, per
+    stream: the gradient g and the forward input x."""
+    if causal:
+        return {"g": (0, 2 * steps), "x": (2 * steps, 0)}
+    return {"g": (steps, steps), "x": (steps, steps)}
+
+
+def partition_dalpha(spec: ShardSpec, steps: int, causal: bool) -> dict[int, tuple[int, int]]:
+    """Local output rows of each launch part of the backward with d(alpha)
+    (the rule of cta_diffusion_shard_bld_dalpha)."""
+    h = halo_rows_dalpha(steps, causal)
+    hl, hr = max(h["g"][0], h["x"][0]), max(h["g"][1], h["x"][1])
+    L = spec.local_len
+    has_lo = spec.pos_offset > 0
+    has_hi = spec.pos_offset + L < spec.global_len
+    ib = min(hl, L) if has_lo else 0
+    ie = max(L - hr, ib) if has_hi else L
+    return {_lib.SHARD_INTERIOR: (ib, ie), _lib.SHARD_LO_EDGE: (0, ib), _lib.SHARD_HI_EDGE: (ie, L)}
+
+
+def _default_compute_dalpha(part, g_local, x_local, dx, dalpha, *, g_lo, g_hi, x_lo, x_hi, spec, alphas, steps,
+                            causal):
+    from . import ops
+
+    ops.shard_part_dalpha(g_local, x_local, dx, dalpha, part, pos_offset=spec.pos_offset,
+                          global_len=spec.global_len, alphas=alphas, steps=steps, causal=causal, g_lo=g_lo,
+                          g_hi=g_hi, x_lo=x_lo, x_hi=x_hi)
+
+
+def sharded_diffusion_backward_dalpha(
+    g_local: torch.Tensor,
+    x_local: torch.Tensor,
+    spec: ShardSpec,
+    *,
+    alphas,
+    steps: int,
+    causal: bool = False,
+    group: Optional[dist.ProcessGroup] = None,
+    comm_stream: Optional[torch.cuda.Stream] = None,
+    compute: Optional[Callable] = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Backward of `steps` fused steps with per-step `alphas` on this rank's
+    shard: returns (dx_local, dalpha), dalpha (fp32 [steps]) summed over all
+    ranks of `group`.  Every rank must call this with the same arguments."""
+    if g_local.dim() != 3 or tuple(x_local.shape) != tuple(g_local.shape):
+        raise ValueError("g_local and x_local must both be (B, L_local, D)")
+    if not 1 <= steps <= _lib.MAX_STEPS:
+        raise ValueError(f"steps must be in 1..{_lib.MAX_STEPS}, got {steps}")
+    alphas = [float(a) for a in alphas]
+    if len(alphas) != steps:
+        raise ValueError("need one alpha per step")
+    B, Lloc, D = g_local.shape
+    if Lloc != spec.local_len:
+        raise ValueError(f"g_local has {Lloc} rows, spec says {spec.local_len}")
+    h = halo_rows_dalpha(steps, causal)
+    need_lo = max(h["g"][0], h["x"][0])
+    need_hi = max(h["g"][1], h["x"][1])
+    prev_rank = spec.rank - 1 if spec.rank > 0 else None
+    next_rank = spec.rank + 1 if spec.rank + 1 < spec.world else None
+    if (prev_rank is not None and need_hi and Lloc < need_hi) or (next_rank is not None and need_lo and Lloc < need_lo):
+        raise ValueError("shard shorter than the halo it must provide")
+    if compute is None:
+        compute = _default_compute_dalpha
+    g_local = g_local.contiguous()
+    x_local = x_local.contiguous()
+    dev = g_local.device
+    dx = torch.empty_like(g_local)
+    dalpha = torch.zeros(steps, dtype=torch.float32, device=dev)
+    if spec.global_len < 3:
+        dx.copy_(g_local)
+        return dx, dalpha
+    on_gpu = dev.type == "cuda"
+    cur = torch.cuda.current_stream(dev) if on_gpu else None
+
+    def buf(rows, present):
+        return torch.empty((B, rows, D), dtype=g_local.dtype, device=dev) if (present and rows) else None
+
+    halos = {
+        "g_lo": buf(h["g"][0], prev_rank is not None), "x_lo": buf(h["x"][0], prev_rank is not None),
+        "g_hi": buf(h["g"][1], next_rank is not None), "x_hi": buf(h["x"][1], next_rank is not None),
+    }
+
+    def post_exchange():
+        ops = []
+        for name, t in (("g", g_local), ("x", x_local)):
+            lo, hi = h[name]
+            # my first `hi` rows are the previous rank's hi halo; my last `lo` rows the next rank's lo halo
+            if prev_rank is not None and hi:
+                ops.append(dist.P2POp(dist.isend, t[:, :hi].contiguous(), prev_rank, group))
+            if next_rank is not None and lo:
+                ops.append(dist.P2POp(dist.isend, t[:, Lloc - lo :].contiguous(), next_rank, group))
+            if halos[name + "_lo"] is not None:
+                ops.append(dist.P2POp(dist.irecv, halos[name + "_lo"], prev_rank, group))
+            if halos[name + "_hi"] is not None:
+                ops.append(dist.P2POp(dist.irecv, halos[name + "_hi"], next_rank, group))
+        return dist.batch_isend_irecv(ops) if ops else []
+
+    kw = dict(spec=spec, alphas=alphas, steps=steps, causal=causal)
+    none = dict(g_lo=None, g_hi=None, x_lo=None, x_hi=None)
+    if on_gpu:
+        comm = comm_stream if comm_stream is not None else torch.cuda.Stream(device=dev)
+        comm.wait_stream(cur)
+        with torch.cuda.stream(comm):
+            works = post_exchange()
+            for w in works:
+                w.wait()
+        compute(_lib.SHARD_INTERIOR, g_local, x_local, dx, dalpha, **none, **kw)
+        cur.wait_stream(comm)
+        for t in halos.values():
+            if t is not None:
+                t.record_stream(cur)
+    else:
+        works = post_exchange()
+        compute(_lib.SHARD_INTERIOR, g_local, x_local, dx, dalpha, **none, **kw)
+        for w in works:
+            w.wait()
+    compute(_lib.SHARD_LO_EDGE, g_local, x_local, dx, dalpha, **halos, **kw)
+    compute(_lib.SHARD_HI_EDGE, g_local, x_local, dx, dalpha, **halos, **kw)
+    if spec.world > 1:
+        dist.all_reduce(dalpha, op=dist.ReduceOp.SUM, group=group)
+    return dx, dalpha

@@ -167,6 +167,24 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
                             int64_t hi_rows, int part, int dtype, int steps, int causal, int backward, float alpha,
                             void* stream);
 
+/* One part of an L-shard's fused backward WITH d(alpha), steps 1..4 (no
+ * counterpart in the reference, which is single-device; together with an
+ * all-reduce of the per-rank sums it is the sharded form of
+ * cta_diffusion_bwd_bld with dalpha).  grad_out, x and grad_in are the local
+ * contiguous [B, L_local, D] shards.  Halos are [B, rows, D] contiguous: g_lo /
+ * x_lo are the rows just before the shard, g_hi / x_hi just after.  Needed rows:
+ * non-causal steps of each halo; causal 2*steps of g_hi and x_lo (g_lo, x_hi
+ * unused).  Halos are read only by the edge parts.  The part's d(alpha) sum is
+ * ADDED to dalpha (fp32 [steps], zeroed by the caller before the first part);
+ * run the parts in one stream so the sum order is fixed.  `workspace` as for
+ * cta_diffusion_bwd_bld with L = L_local.  Returns CTA_EUNSUPPORTED for steps > 4. */
+int cta_diffusion_shard_bld_dalpha(const void* grad_out, const void* x, void* grad_in, float* dalpha,
+                                   void* workspace, int64_t workspace_bytes, int64_t B, int64_t L_local, int64_t D,
+                                   int64_t pos_offset, int64_t global_len, const void* g_lo_halo, int64_t g_lo_rows,
+                                   const void* g_hi_halo, int64_t g_hi_rows, const void* x_lo_halo,
+                                   int64_t x_lo_rows, const void* x_hi_halo, int64_t x_hi_rows, int part, int dtype,
+                                   int steps, int causal, const float* alpha, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -248,3 +248,35 @@ def window_bld(
         mid = torch.where(fixed[:, 1:-1, :], u[:, 1:-1, :], mid)
         u = torch.cat([u[:, :1, :], mid, u[:, -1:, :]], dim=1)
     return u[:, out_start - win_start : out_stop - win_start, :].to(x_window.dtype)
+
+
+def window_bld_grads(
+    g_window: torch.Tensor, x_window: torch.Tensor, *, win_start: int, global_len: int, out_start: int,
+    out_stop: int, alphas: Sequence[float], causal: bool = False,
+):
+    """(dx rows [out_start, out_stop), d(alpha_k) summed over those rows only) of
+    the fused stack of layers (src/models/pde_layers.py:113-188, :218-219, fp32
+    between steps, no mask) over a global sequence of global_len rows, given only
+    global rows [win_start, win_start + n) of the forward input and of the output
+    gradient.  The window must reach `steps` rows beyond the output rows on each
+    side (2*steps before them and 2*steps after them for the causal stencil);
+    rows outside it read as zero and cannot reach the output rows.  d(alpha) is
+    taken per row through a per-row copy of each alpha, so that a shard sums
+    only its own rows."""
+    n = x_window.shape[1]
+    pos = torch.arange(win_start, win_start + n)
+    upd = ((pos >= 2) & (pos <= global_len - 1)) if causal else ((pos >= 1) & (pos <= global_len - 2))
+    upd = upd.view(1, n, 1)
+    xr = x_window.to(torch.float32).detach().clone().requires_grad_(True)
+    per_row = [torch.full((1, n, 1), float(a)).requires_grad_(True) for a in alphas]
+    u = xr
+    for a in per_row:
+        z = torch.zeros_like(u[:, :1])
+        up = torch.cat([z, z, u], dim=1) if causal else torch.cat([z, u, z], dim=1)
+        # pde_layers.py:143-175 : (x[i+1] - 2x[i]) + x[i-1], causal (x[i] - 2x[i-1]) + x[i-2]
+        lap = up[:, 2:] - 2.0 * up[:, 1:-1] + up[:, :-2]
+        u = torch.where(upd, u + a * lap, u)
+    (u * g_window.to(torch.float32)).sum().backward()
+    o0, o1 = out_start - win_start, out_stop - win_start
+    dalpha = torch.stack([a.grad[:, o0:o1].double().sum() for a in per_row])
+    return xr.grad[:, o0:o1].detach(), dalpha

@@ -48,6 +48,22 @@ def _worker(rank, world, port, q):
             ref = full[:, spec.pos_offset : spec.pos_offset + spec.local_len]
             torch.cuda.synchronize()
             results.append(bool(torch.equal(y, ref)))
+        from cta_b200.sharded import sharded_diffusion_backward_dalpha
+
+        for steps, causal in [(4, False), (3, True)]:
+            torch.manual_seed(1)
+            x = torch.randn(2, 3001, 512, dtype=torch.bfloat16).cuda()
+            g = torch.randn(2, 3001, 512, dtype=torch.bfloat16).cuda()
+            al = [0.1, 0.05, 0.12, 0.02][:steps]
+            spec = even_shards(3001, world, rank)
+            sl = slice(spec.pos_offset, spec.pos_offset + spec.local_len)
+            dx, da = sharded_diffusion_backward_dalpha(g[:, sl], x[:, sl], spec, alphas=al, steps=steps,
+                                                       causal=causal)
+            full_dx, full_da = ops.bld_backward(g, al, steps, x=x, causal=causal, need_dalpha=True)
+            torch.cuda.synchronize()
+            scale = max(1.0, full_da.abs().max().item())
+            results.append(bool(torch.equal(dx, full_dx[:, sl])) and
+                           (da - full_da).abs().max().item() <= 1e-5 * scale)
         q.put((rank, results))
         dist.destroy_process_group()
     except Exception as e:  # noqa: BLE001
@@ -72,4 +88,4 @@ def test_two_gpu_sharded_matches_single_gpu():
     while not q.empty():
         r, v = q.get()
         res[r] = v
-    assert res == {0: [True] * 4, 1: [True] * 4}, res
+    assert res == {0: [True] * 6, 1: [True] * 6}, res

@@ -70,3 +70,69 @@ def test_short_shards_need_both_halos():
     full = ops.bld_forward(x, [0.1] * 8, 8)
     y = _run_sharded(x, 4, 8, False, backward=False)
     assert torch.equal(y, full)
+
+
+def _run_sharded_dalpha(g, x, P, steps, causal, alphas):
+    from cta_b200 import _lib, ops
+    from cta_b200.sharded import even_shards, halo_rows_dalpha
+
+    B, L, D = g.shape
+    h = halo_rows_dalpha(steps, causal)
+    outs, das = [], []
+    for r in range(P):
+        spec = even_shards(L, P, r)
+        a, b = spec.pos_offset, spec.pos_offset + spec.local_len
+
+        def halos(t, name):
+            lo, hi = h[name]
+            return (t[:, a - lo : a].contiguous() if (a > 0 and lo) else None,
+                    t[:, b : b + hi].contiguous() if (b < L and hi) else None)
+
+        g_lo, g_hi = halos(g, "g")
+        x_lo, x_hi = halos(x, "x")
+        dx = torch.empty_like(g[:, a:b])
+        da = torch.zeros(steps, dtype=torch.float32, device=g.device)
+        for part in (_lib.SHARD_INTERIOR, _lib.SHARD_LO_EDGE, _lib.SHARD_HI_EDGE):
+            ops.shard_part_dalpha(g[:, a:b].contiguous(), x[:, a:b].contiguous(), dx, da, part, pos_offset=a,
+                                  global_len=L, alphas=alphas, steps=steps, causal=causal, g_lo=g_lo, g_hi=g_hi,
+                                  x_lo=x_lo, x_hi=x_hi)
+        outs.append(dx)
+        das.append(da)
+    return torch.cat(outs, dim=1), torch.stack(das).sum(0)
+
+
+@pytest.mark.parametrize("P", [2, 3])
+@pytest.mark.parametrize("steps", [1, 2, 3, 4])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("dtype,D", [(torch.float32, 512), (torch.bfloat16, 264), (torch.float32, 6)])
+def test_sharded_backward_dalpha_equals_unsharded(P, steps, causal, dtype, D):
+    """Interior + edge parts of every shard (halos of g and x sliced from the full
+    tensors): dx bit-identical to the unsharded d(alpha) kernel, the summed
+    d(alpha) equal up to the summation order, and both against the oracle."""
+    from cta_b200 import _lib, ops
+
+    torch.manual_seed(P * 10 + steps)
+    al = [0.1, 0.05, 0.12, 0.02][:steps]
+    x = torch.randn(2, 1001, D, device="cuda").to(dtype)
+    g = torch.randn(2, 1001, D, device="cuda").to(dtype)
+    full_dx, full_da = ops.bld_backward(g, al, steps, x=x, causal=causal, need_dalpha=True)
+    dx, da = _run_sharded_dalpha(g, x, P, steps, causal, al)
+    assert torch.equal(dx, full_dx)
+    scale = max(1.0, full_da.abs().max().item())
+    assert (da - full_da).abs().max().item() <= 1e-5 * scale, (da, full_da)
+    if dtype == torch.float32 and D == 6:
+        dx_ref, da_ref = O.grads(lambda t, *a: O.fused_stack(t, list(a), layout="bld", causal=causal), x.cpu(),
+                                 g.cpu(), [torch.tensor([v]) for v in al])
+        assert (dx.cpu() - dx_ref).abs().max().item() <= 1e-5 * dx_ref.abs().max().item()
+        assert (da.cpu() - torch.cat(da_ref)).abs().max().item() <= 1e-4 * scale
+    assert _lib.device_error() == 0
+
+
+def test_sharded_dalpha_rejects_deep_steps():
+    from cta_b200 import _lib, ops
+
+    g = torch.randn(1, 64, 8, device="cuda")
+    da = torch.zeros(8, device="cuda")
+    with pytest.raises(RuntimeError, match="steps 1..4"):
+        ops.shard_part_dalpha(g, g, torch.empty_like(g), da, _lib.SHARD_INTERIOR, pos_offset=0, global_len=64,
+                              alphas=[0.1] * 8, steps=8)

@@ -90,3 +90,25 @@ def test_window_oracle_matches_full():
         lo, hi = max(0, a - 8), min(300, b + 8)
         w = O.window_bld(x[:, lo:hi], win_start=lo, global_len=300, out_start=a, out_stop=b, alpha=0.1, steps=8)
         assert torch.equal(w, full[:, a:b])
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_window_grads_oracle_matches_full(causal):
+    """Per-window dx rows and row-restricted d(alpha) sums add up to the full
+    autograd gradients of the fused stack (the checker of the sharded backward)."""
+    torch.manual_seed(8)
+    B, L, D, al = 2, 90, 6, [0.1, 0.05, 0.12, 0.02]
+    x, g = torch.randn(B, L, D), torch.randn(B, L, D)
+    dx_ref, da_ref = O.grads(lambda t, *a: O.fused_stack(t, list(a), layout="bld", causal=causal), x, g,
+                             [torch.tensor([v]) for v in al])
+    da_ref = torch.cat(da_ref)
+    h = 2 * len(al) if causal else len(al)
+    dxs, das = [], torch.zeros(len(al), dtype=torch.float64)
+    for a, b in [(0, 31), (31, 32), (32, 90)]:
+        lo, hi = max(0, a - h), min(L, b + h)
+        dx, da = O.window_bld_grads(g[:, lo:hi], x[:, lo:hi], win_start=lo, global_len=L, out_start=a, out_stop=b,
+                                    alphas=al, causal=causal)
+        dxs.append(dx)
+        das += da
+    torch.testing.assert_close(torch.cat(dxs, 1), dx_ref, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(das.float(), da_ref, rtol=1e-5, atol=1e-5)
