@@ -350,7 +350,32 @@ int cta_diffusion_bdl_ex(const void* in, void* out, int64_t B, int64_t D, int64_
     a.alpha_dev[k] = (alpha_dev != nullptr && k < steps) ? alpha_dev[k] : nullptr;
   }
   a.alpha_dev_dtype = alpha_dev_dtype;
-  const cudaError_t e = launch_bdl(a, dtype, steps, causal ? 1 : 0, backward ? 1 : 0, static_cast<cudaStream_t>(stream));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // TMA form when both tensors are addressable: [B*D rows, L] maps, boxes of two
+  // rows x 256 positions (loads) and two rows x 240 positions (stores)
+  CUtensorMap imap, omap;
+  std::memset(&imap, 0, sizeof(imap));
+  std::memset(&omap, 0, sizeof(omap));
+  const int64_t rows = B * D;
+  if (make_map(&imap, in, dtype, 1, rows, L, rows * in_row_stride, in_row_stride, kBdlRows, kBdlWin) &&
+      make_map(&omap, out, dtype, 1, rows, L, rows * out_row_stride, out_row_stride, kBdlRows, kBdlOut)) {
+    const int64_t nwin = (L + kBdlOut - 1) / kBdlOut;
+    const int64_t pairs = (rows + kBdlRows - 1) / kBdlRows;
+    const int occ = bdl_march_ctas_per_sm(dtype, steps, causal ? 1 : 0, backward ? 1 : 0);
+    const int per_sm = occ > 0 ? std::min(g_tuning.fwd_ctas_per_sm, occ) : g_tuning.fwd_ctas_per_sm;
+    const int64_t target = static_cast<int64_t>(num_sms()) * per_sm;
+    const int64_t tw = std::max<int64_t>(1, (pairs * nwin + target - 1) / target);
+    const int64_t nseg = (nwin + tw - 1) / tw;
+    if (pairs * nseg <= 0x7fffffffLL) {
+      a.tw = static_cast<int>(tw);
+      a.nseg = static_cast<int>(nseg);
+      const cudaError_t e = launch_bdl_march(a, &imap, &omap, dtype, steps, causal ? 1 : 0, backward ? 1 : 0,
+                                             static_cast<unsigned>(pairs * nseg), st);
+      if (e != cudaSuccess) return cuda_fail(e, "bdl launch");
+      return ok();
+    }
+  }
+  const cudaError_t e = launch_bdl(a, dtype, steps, causal ? 1 : 0, backward ? 1 : 0, st);
   if (e != cudaSuccess) return cuda_fail(e, "bdl launch");
   return ok();
 }

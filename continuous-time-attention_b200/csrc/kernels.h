@@ -103,6 +103,14 @@ struct BldArgs {
 constexpr int kBdlThreads = 256;  // 8 warps, each owns two 256-wide windows
 constexpr int kBdlElems = 8;      // positions per lane
 constexpr int kBdlOut = 240;      // output positions per window (30 lanes)
+constexpr int kBdlWin = 256;      // loaded positions per window (32 lanes x 8)
+constexpr int kBdlRows = 2;       // rows per one-warp CTA of the TMA form (pair halves)
+constexpr int kBdlStages = 4;     // input windows in flight per CTA (TMA form)
+// staging slot of the TMA form: kBdlRows x kBdlOut elements, rounded up to 128 bytes
+template <typename T>
+constexpr int bdl_out_slot_elems() {
+  return ((kBdlRows * kBdlOut * static_cast<int>(sizeof(T)) + 127) / 128) * 128 / static_cast<int>(sizeof(T));
+}
 
 struct BdlArgs {
   const void* in;   // forward: x.  backward: grad_out
@@ -119,6 +127,8 @@ struct BdlArgs {
   float alpha[kMaxSteps];
   const void* alpha_dev[kMaxSteps];
   int alpha_dev_dtype;
+  // TMA form: windows per CTA and CTAs per row pair
+  int tw, nseg;
 };
 
 // launchers (return cudaError_t of the launch)
@@ -131,6 +141,11 @@ cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUte
 cudaError_t launch_bld_bwd(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap, int dtype,
                            int steps, int causal, int with_dalpha, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st);
+// [B, D, L] TMA form: in map box {kBdlWin, kBdlRows}, out map box {kBdlOut, kBdlRows}
+cudaError_t launch_bdl_march(const BdlArgs& a, const CUtensorMap* imap, const CUtensorMap* omap, int dtype,
+                             int steps, int causal, int backward, unsigned grid, cudaStream_t st);
+int bdl_march_ctas_per_sm(int dtype, int steps, int causal, int backward);
+size_t bdl_march_smem_bytes(int dtype);
 
 // march kernel with d(alpha), steps 1..kDaMaxSteps
 cudaError_t launch_bld_dalpha(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap,

@@ -117,6 +117,125 @@ __device__ __forceinline__ pf2 sel_fixed(uint32_t fa, uint32_t fb, int i, pf2 ke
   return pk(((fa >> i) & 1u) ? k0 : u0, ((fb >> i) & 1u) ? k1 : u1);
 }
 
+// 8 positions of two rows from shared memory, packed: row A in the low half,
+// row B in the high half of each pair
+template <typename T>
+__device__ __forceinline__ void bdl_smem_pairs(const T* ra, const T* rb, pf2 (&e)[E8]) {
+  using E = Elem<T>;
+  if constexpr (sizeof(T) == 2) {
+    const uint4 qa = *reinterpret_cast<const uint4*>(ra);
+    const uint4 qb = *reinterpret_cast<const uint4*>(rb);
+    const typename E::Pair* pa = reinterpret_cast<const typename E::Pair*>(&qa);
+    const typename E::Pair* pb = reinterpret_cast<const typename E::Pair*>(&qb);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 fa = E::unpack(pa[i]), fb = E::unpack(pb[i]);
+      e[2 * i] = pk(fa.x, fb.x);
+      e[2 * i + 1] = pk(fa.y, fb.y);
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float4 qa = *reinterpret_cast<const float4*>(ra + 4 * h);
+      const float4 qb = *reinterpret_cast<const float4*>(rb + 4 * h);
+      e[4 * h] = pk(qa.x, qb.x);
+      e[4 * h + 1] = pk(qa.y, qb.y);
+      e[4 * h + 2] = pk(qa.z, qb.z);
+      e[4 * h + 3] = pk(qa.w, qb.w);
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void bdl_smem_store_pairs(T* ra, T* rb, const pf2 (&e)[E8]) {
+  using E = Elem<T>;
+  float va[E8], vb[E8];
+#pragma unroll
+  for (int i = 0; i < E8; ++i) upk(e[i], va[i], vb[i]);
+  if constexpr (sizeof(T) == 2) {
+    uint4 qa, qb;
+    typename E::Pair* pa = reinterpret_cast<typename E::Pair*>(&qa);
+    typename E::Pair* pb = reinterpret_cast<typename E::Pair*>(&qb);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      pa[i] = E::pack(make_float2(va[2 * i], va[2 * i + 1]));
+      pb[i] = E::pack(make_float2(vb[2 * i], vb[2 * i + 1]));
+    }
+    *reinterpret_cast<uint4*>(ra) = qa;
+    *reinterpret_cast<uint4*>(rb) = qb;
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      *reinterpret_cast<float4*>(ra + 4 * h) = make_float4(va[4 * h], va[4 * h + 1], va[4 * h + 2], va[4 * h + 3]);
+      *reinterpret_cast<float4*>(rb + 4 * h) = make_float4(vb[4 * h], vb[4 * h + 1], vb[4 * h + 2], vb[4 * h + 3]);
+    }
+  }
+}
+
+// All `steps` levels of one 256-position window (8 positions per lane, two
+// independent windows packed in the halves of each pair), in registers; the
+// neighbours of a lane's first and last position come from the adjacent lanes.
+// fa / fb: fixed-position bits of the two windows (SLOW only).
+template <int S, bool CAUSAL, bool BWD, bool SLOW>
+__device__ __forceinline__ void window_levels(pf2 (&e)[E8], uint32_t fa, uint32_t fb, const float (&al)[kMaxSteps],
+                                              pf2 m2, pf2 zn) {
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    if (!BWD) {
+      const pf2 alv = pbc(al[s]);
+      pf2 n[E8];
+      if (CAUSAL) {
+        const pf2 m2n = shfl_up_p(e[E8 - 2], 1), m1n = shfl_up_p(e[E8 - 1], 1);
+#pragma unroll
+        for (int i = 0; i < E8; ++i) {
+          const pf2 p2 = i >= 2 ? e[i - 2] : (i == 1 ? m1n : m2n);
+          const pf2 p1 = i >= 1 ? e[i - 1] : m1n;
+          n[i] = pst_c(p2, p1, e[i], alv, m2, zn);
+        }
+      } else {
+        const pf2 lft = shfl_up_p(e[E8 - 1], 1), rgt = shfl_down_p(e[0], 1);
+#pragma unroll
+        for (int i = 0; i < E8; ++i) {
+          const pf2 l = i > 0 ? e[i - 1] : lft;
+          const pf2 r = i < E8 - 1 ? e[i + 1] : rgt;
+          n[i] = pst_nc(l, e[i], r, alv, m2, zn);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < E8; ++i) e[i] = SLOW ? sel_fixed(fa, fb, i, e[i], n[i]) : n[i];
+    } else {
+      // adjoint of forward step S-1-s: a = alpha * g on updated positions
+      const pf2 alv = pbc(al[S - 1 - s]);
+      pf2 av[E8];
+#pragma unroll
+      for (int i = 0; i < E8; ++i) {
+        av[i] = pmul_sep(alv, e[i], zn);
+        if (SLOW) av[i] = sel_fixed(fa, fb, i, 0ull, av[i]);
+      }
+      if (CAUSAL) {
+        const pf2 q1 = shfl_down_p(av[0], 1), q2 = shfl_down_p(av[1], 1);
+#pragma unroll
+        for (int i = 0; i < E8; ++i) {
+          const pf2 a1 = i + 1 < E8 ? av[i + 1] : (i + 1 == E8 ? q1 : q2);
+          const pf2 a2 = i + 2 < E8 ? av[i + 2] : (i + 2 == E8 ? q1 : q2);
+          e[i] = padd(e[i], plap(a2, a1, av[i], m2));  // (a[i] - 2a[i+1]) + a[i+2]
+        }
+      } else {
+        const pf2 lft = shfl_up_p(av[E8 - 1], 1), rgt = shfl_down_p(av[0], 1);
+        pf2 n[E8];
+#pragma unroll
+        for (int i = 0; i < E8; ++i) {
+          const pf2 l = i > 0 ? av[i - 1] : lft;
+          const pf2 r = i < E8 - 1 ? av[i + 1] : rgt;
+          n[i] = padd(e[i], plap(l, av[i], r, m2));
+        }
+#pragma unroll
+        for (int i = 0; i < E8; ++i) e[i] = n[i];
+      }
+    }
+  }
+}
+
 }  // namespace
 
 template <typename T, int S, bool CAUSAL, bool BWD>
@@ -169,66 +288,8 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
   const pf2 m2 = pbc(-2.f);
   const pf2 zn = pbc(a.neg_zero);
 
-  auto run = [&](auto slow_tag) {
-    constexpr bool SLOW = decltype(slow_tag)::value;
-#pragma unroll
-    for (int s = 0; s < S; ++s) {
-      if (!BWD) {
-        const pf2 alv = pbc(al[s]);
-        pf2 n[E8];
-        if (CAUSAL) {
-          const pf2 m2n = shfl_up_p(e[E8 - 2], 1), m1n = shfl_up_p(e[E8 - 1], 1);
-#pragma unroll
-          for (int i = 0; i < E8; ++i) {
-            const pf2 p2 = i >= 2 ? e[i - 2] : (i == 1 ? m1n : m2n);
-            const pf2 p1 = i >= 1 ? e[i - 1] : m1n;
-            n[i] = pst_c(p2, p1, e[i], alv, m2, zn);
-          }
-        } else {
-          const pf2 lft = shfl_up_p(e[E8 - 1], 1), rgt = shfl_down_p(e[0], 1);
-#pragma unroll
-          for (int i = 0; i < E8; ++i) {
-            const pf2 l = i > 0 ? e[i - 1] : lft;
-            const pf2 r = i < E8 - 1 ? e[i + 1] : rgt;
-            n[i] = pst_nc(l, e[i], r, alv, m2, zn);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < E8; ++i) e[i] = SLOW ? sel_fixed(fa, fb, i, e[i], n[i]) : n[i];
-      } else {
-        // adjoint of forward step S-1-s: a = alpha * g on updated positions
-        const pf2 alv = pbc(al[S - 1 - s]);
-        pf2 av[E8];
-#pragma unroll
-        for (int i = 0; i < E8; ++i) {
-          av[i] = pmul_sep(alv, e[i], zn);
-          if (SLOW) av[i] = sel_fixed(fa, fb, i, 0ull, av[i]);
-        }
-        if (CAUSAL) {
-          const pf2 q1 = shfl_down_p(av[0], 1), q2 = shfl_down_p(av[1], 1);
-#pragma unroll
-          for (int i = 0; i < E8; ++i) {
-            const pf2 a1 = i + 1 < E8 ? av[i + 1] : (i + 1 == E8 ? q1 : q2);
-            const pf2 a2 = i + 2 < E8 ? av[i + 2] : (i + 2 == E8 ? q1 : q2);
-            e[i] = padd(e[i], plap(a2, a1, av[i], m2));  // (a[i] - 2a[i+1]) + a[i+2]
-          }
-        } else {
-          const pf2 lft = shfl_up_p(av[E8 - 1], 1), rgt = shfl_down_p(av[0], 1);
-          pf2 n[E8];
-#pragma unroll
-          for (int i = 0; i < E8; ++i) {
-            const pf2 l = i > 0 ? av[i - 1] : lft;
-            const pf2 r = i < E8 - 1 ? av[i + 1] : rgt;
-            n[i] = padd(e[i], plap(l, av[i], r, m2));
-          }
-#pragma unroll
-          for (int i = 0; i < E8; ++i) e[i] = n[i];
-        }
-      }
-    }
-  };
-  if (slow) run(std::true_type{});
-  else run(std::false_type{});
+  if (slow) window_levels<S, CAUSAL, BWD, true>(e, fa, fb, al, m2, zn);
+  else window_levels<S, CAUSAL, BWD, false>(e, fa, fb, al, m2, zn);
 
   if (lane >= HLN && lane < 32 - HRN) {
 #pragma unroll
@@ -236,6 +297,110 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
     store_window<T>(a, ra, pa, va);
     if (vb) store_window<T>(a, rbw, pb, vbv);
   }
+}
+
+// ---------------------------------------------------------------------------
+// TMA pipeline form (dense rows that TMA can address).  A CTA is one warp
+// owning two rows (packed in the halves of every pair) and a run of
+// consecutive windows along L.  Each window's 256 x 2 input box arrives
+// through a ring of TMA loads (kBdlStages deep, one mbarrier per slot), the
+// levels run in registers as above, and the 240 x 2 finished positions leave
+// through a staged TMA store, so loads, arithmetic and stores of successive
+// windows overlap inside the warp.
+// ---------------------------------------------------------------------------
+template <typename T, int S, bool CAUSAL, bool BWD>
+__global__ void __launch_bounds__(32, 16)
+    bdl_march_kernel(const __grid_constant__ CUtensorMap imap, const __grid_constant__ CUtensorMap omap,
+                     const BdlArgs a) {
+  constexpr int HLN = CAUSAL ? (BWD ? 0 : 2) : 1;
+  constexpr int HRN = CAUSAL ? (BWD ? 2 : 0) : 1;
+  constexpr int NST = kBdlStages;
+  constexpr int IN_CHUNK = kBdlRows * kBdlWin;                    // elements per input slot
+  constexpr int OUT_SLOT = bdl_out_slot_elems<T>();               // elements per staging slot (128-B multiple)
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  T* ring = reinterpret_cast<T*>(smem_raw);
+  T* stage = ring + NST * IN_CHUNK;
+  __shared__ __align__(8) uint64_t full_bar[NST];
+
+  const int lane = threadIdx.x;
+  const int64_t nwin = (a.L + kBdlOut - 1) / kBdlOut;
+  const int64_t rp = blockIdx.x / a.nseg;
+  const int64_t w0 = static_cast<int64_t>(blockIdx.x % a.nseg) * a.tw;
+  const int64_t w1 = w0 + a.tw < nwin ? w0 + a.tw : nwin;
+  if (w0 >= w1) return;
+  const int nw = static_cast<int>(w1 - w0);
+  const int64_t r0 = 2 * rp;
+  const bool vb = r0 + 1 < a.rows;
+
+  if (lane == 0) {
+    prefetch_tmap(&imap);
+    prefetch_tmap(&omap);
+#pragma unroll
+    for (int s = 0; s < NST; ++s) mbar_init(&full_bar[s], 1);
+    fence_mbar_init();
+  }
+  auto issue = [&](int i) {
+    const int slot = i % NST;
+    mbar_arrive_expect_tx(&full_bar[slot], IN_CHUNK * sizeof(T));
+    tma_load_3d(ring + slot * IN_CHUNK, &imap, &full_bar[slot], static_cast<int>((w0 + i) * kBdlOut - HLN * E8),
+                static_cast<int>(r0), 0);
+  };
+  if (lane == 0) {
+    for (int i = 0; i < nw && i < NST; ++i) issue(i);
+  }
+  float al[kMaxSteps];
+#pragma unroll
+  for (int k = 0; k < kMaxSteps; ++k)
+    if (k < S) al[k] = a.alpha_dev[k] != nullptr ? load_scalar(a.alpha_dev[k], a.alpha_dev_dtype) : a.alpha[k];
+  const pf2 m2 = pbc(-2.f);
+  const pf2 zn = pbc(a.neg_zero);
+  const int64_t lo_fixed = CAUSAL ? 1 : 0, hi_fixed = CAUSAL ? a.L : a.L - 1;
+
+  for (int i = 0; i < nw; ++i) {
+    const int slot = i % NST;
+    int err = mbar_wait_bounded(&full_bar[slot], (i / NST) & 1) ? 0 : 1;
+    const int64_t ws = (w0 + i) * kBdlOut - HLN * E8;  // first loaded position of the window
+    const int64_t p = ws + lane * E8;
+    if (!err) {
+      const T* buf = ring + slot * IN_CHUNK + lane * E8;
+      pf2 e[E8];
+      bdl_smem_pairs<T>(buf, buf + kBdlWin, e);
+      const bool interior = a.mask == nullptr && ws > lo_fixed && ws + kBdlWin - 1 < hi_fixed;
+      uint32_t fa = 0u, fb = 0u;
+      if (!interior) {
+        fa = fixed_bits<CAUSAL>(a, r0, p, true);
+        fb = fixed_bits<CAUSAL>(a, r0 + 1, p, vb);
+      }
+      if (!interior && __any_sync(0xffffffffu, (fa | fb) != 0u))
+        window_levels<S, CAUSAL, BWD, true>(e, fa, fb, al, m2, zn);
+      else
+        window_levels<S, CAUSAL, BWD, false>(e, fa, fb, al, m2, zn);
+      if (lane >= HLN && lane < 32 - HRN) {
+        T* st = stage + (i & 1) * OUT_SLOT + (lane - HLN) * E8;
+        bdl_smem_store_pairs<T>(st, st + kBdlOut, e);
+      }
+      fence_proxy_async_smem();
+    }
+    // the store issued after the previous window must have finished reading the
+    // staging slot that the next window overwrites
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+    if (__any_sync(0xffffffffu, err)) {
+      if (lane == 0) {
+        atomicExch(&g_bdl_error, kDevTimeout);
+        for (int j = i; j < nw && j < i + NST; ++j) mbar_wait_bounded(&full_bar[j % NST], (j / NST) & 1);
+        bulk_wait_all();
+      }
+      __syncwarp();
+      return;
+    }
+    if (lane == 0) {
+      tma_store_3d(&omap, stage + (i & 1) * OUT_SLOT, static_cast<int>((w0 + i) * kBdlOut), static_cast<int>(r0), 0);
+      bulk_commit();
+      if (i + NST < nw) issue(i + NST);
+    }
+  }
+  if (lane == 0) bulk_wait_all();
 }
 
 namespace {
@@ -266,6 +431,41 @@ cudaError_t by_steps(const BdlArgs& a, int steps, cudaStream_t st) {
   }
 }
 
+template <typename T, int S, bool C, bool B>
+const void* march_ptr_s() {
+  return reinterpret_cast<const void*>(bdl_march_kernel<T, S, C, B>);
+}
+
+template <typename T, bool C, bool B>
+const void* march_ptr(int steps) {
+  switch (steps) {
+    case 1: return march_ptr_s<T, 1, C, B>();
+    case 2: return march_ptr_s<T, 2, C, B>();
+    case 3: return march_ptr_s<T, 3, C, B>();
+    case 4: return march_ptr_s<T, 4, C, B>();
+    case 5: return march_ptr_s<T, 5, C, B>();
+    case 6: return march_ptr_s<T, 6, C, B>();
+    case 7: return march_ptr_s<T, 7, C, B>();
+    case 8: return march_ptr_s<T, 8, C, B>();
+    default: return nullptr;
+  }
+}
+
+template <typename T>
+const void* march_ptr_t(int steps, int causal, int bwd) {
+  if (causal) return bwd ? march_ptr<T, true, true>(steps) : march_ptr<T, true, false>(steps);
+  return bwd ? march_ptr<T, false, true>(steps) : march_ptr<T, false, false>(steps);
+}
+
+const void* bdl_march_ptr(int dtype, int steps, int causal, int bwd) {
+  switch (dtype) {
+    case kF32: return march_ptr_t<float>(steps, causal, bwd);
+    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, bwd);
+    case kF16: return march_ptr_t<__half>(steps, causal, bwd);
+    default: return nullptr;
+  }
+}
+
 template <typename T>
 cudaError_t by_mode(const BdlArgs& a, int steps, int causal, int bwd, cudaStream_t st) {
   if (causal) return bwd ? by_steps<T, true, true>(a, steps, st) : by_steps<T, true, false>(a, steps, st);
@@ -281,6 +481,29 @@ cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int b
     case kF16: return by_mode<__half>(a, steps, causal, backward, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+size_t bdl_march_smem_bytes(int dtype) {
+  return dtype == kF32 ? (kBdlStages * kBdlRows * kBdlWin + 2 * bdl_out_slot_elems<float>()) * sizeof(float)
+                       : (kBdlStages * kBdlRows * kBdlWin + 2 * bdl_out_slot_elems<__half>()) * 2;
+}
+
+cudaError_t launch_bdl_march(const BdlArgs& a, const CUtensorMap* imap, const CUtensorMap* omap, int dtype,
+                             int steps, int causal, int backward, unsigned grid, cudaStream_t st) {
+  const void* kern = bdl_march_ptr(dtype, steps, causal, backward);
+  if (kern == nullptr) return cudaErrorInvalidValue;
+  const size_t smem = bdl_march_smem_bytes(dtype);
+  void* args[] = {const_cast<CUtensorMap*>(imap), const_cast<CUtensorMap*>(omap), const_cast<BdlArgs*>(&a)};
+  return cudaLaunchKernel(kern, dim3(grid), dim3(32), args, smem, st);
+}
+
+int bdl_march_ctas_per_sm(int dtype, int steps, int causal, int backward) {
+  const void* kern = bdl_march_ptr(dtype, steps, causal, backward);
+  if (kern == nullptr) return -1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 32, bdl_march_smem_bytes(dtype)) != cudaSuccess)
+    return -1;
+  return n;
 }
 
 int read_device_error_bdl(int clear) {
