@@ -498,6 +498,29 @@ def run_kernels(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     L, D = args.L, args.D
+    if args.mode == "kernel":
+        # bare launches of ONE kernel (--kernel) for profilers: two buffers per tensor
+        S = args.stencil_steps
+        xs = [torch.randn(1, L, D, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+        gs = [torch.randn_like(xs[0]) for _ in range(2)]
+        ys = [torch.empty_like(xs[0]) for _ in range(2)]
+        xt = [t.transpose(1, 2).contiguous() for t in xs]
+        yt = [torch.empty_like(xt[0]) for _ in range(2)]
+        calls = {
+            "bld_forward": lambda i: ops.bld_forward(xs[i % 2], [0.1] * S, S, out=ys[i % 2]),
+            "bld_adjoint": lambda i: ops.bld_backward(gs[i % 2], [0.1] * S, S, out=ys[i % 2]),
+            "bld_adjoint_dalpha": lambda i: ops.bld_backward(gs[i % 2], [0.1] * S, S, x=xs[i % 2],
+                                                             need_dalpha=True, out=ys[i % 2]),
+            "bdl_forward": lambda i: ops.bdl_simple(xt[i % 2], 0.1, S, out=yt[i % 2]),
+            "bdl_adjoint": lambda i: ops.bdl_simple(xt[i % 2], 0.1, S, backward=True, out=yt[i % 2]),
+        }
+        fn = calls[args.kernel]
+        for i in range(args.warmup):
+            fn(i)
+        t = _time_launches(fn, args.steps, torch.cuda.current_stream(dev))
+        _emit(rank, {"mode": "kernel", "kernel": args.kernel, "steps": S, "launches": args.steps,
+                     "us_per_call": t / args.steps * 1e6, "L": L, "D": D})
+        return
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     nb = max(2, min(16, (4 * l2) // (L * D * 2) + 1))
     xs = [torch.randn(1, L, D, device=dev, dtype=torch.bfloat16) for _ in range(nb)]
@@ -548,6 +571,9 @@ def main() -> None:
                     help="fused_fwd: headline single-GPU forward; varlen: 64-sequence packed mixer, D=4096; "
                          "block: PDE-Transformer LM fwd+bwd; sharded: L=1M x 4096 split over the ranks; "
                          "kernels: per-kernel timing table")
+    ap.add_argument("--kernel", default="bld_forward",
+                    choices=["bld_forward", "bld_adjoint", "bld_adjoint_dalpha", "bdl_forward", "bdl_adjoint"],
+                    help="with --workload kernels --mode kernel: the one kernel to launch")
     ap.add_argument("--mode", choices=["full", "kernel"], default="full",
                     help="kernel: only warmup + timed launches of the fused kernel (for ncu)")
     args = ap.parse_args()
