@@ -402,12 +402,29 @@ def run_varlen(args, rank, world, local_rank):
     peak, _ = _peaks()
     per = t / k
     gbs = 2 * T * D * 2 / per / 1e9
+    # the decoder layer's next line, residual + mixer(x): fused into the launch
+    # (reads x and residual, writes the sum) against mixer then a torch add
+    res = torch.randn(T, D, device=dev, dtype=torch.bfloat16)
+
+    def fused(i):
+        mixer(xs[i % nb], attn_metadata=md, residual=res)
+
+    def two_pass(i):
+        res + mixer(xs[i % nb], attn_metadata=md)
+
+    for fn in (fused, two_pass):
+        for i in range(3):
+            fn(i)
+    t_fused = _max_over_ranks(_time_launches(fused, k, stream), dev, world) / k
+    t_two = _max_over_ranks(_time_launches(two_pass, k, stream), dev, world) / k
     _emit(rank, {"metric": METRIC, "value": T * world / per, "unit": "tokens/s", "n_gpus": world, "steps": k,
                  "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True, "scaling": "weak",
                  "dtype": "bf16", "data": "synthetic",
                  "config": {"workload": "varlen_mixer", "nseq": 64, "tokens": T, "D": D,
                             "steps": args.stencil_steps, "rule": "reference zero-pad to max_query_len"},
-                 "hbm_gbs": gbs, "hbm_frac": gbs / peak, "gpu_launches": k})
+                 "hbm_gbs": gbs, "hbm_frac": gbs / peak, "gpu_launches": k,
+                 "residual_add": {"fused_ms": t_fused * 1e3, "two_pass_ms": t_two * 1e3,
+                                  "fused_hbm_frac": 3 * T * D * 2 / t_fused / 1e9 / peak}})
 
 
 def run_block(args, rank, world, local_rank):

@@ -71,18 +71,23 @@ __device__ void fill_fwd_chunk(const BldArgs& a, const Seg& s, int64_t jrow0, in
 // -Xptxas -v for every variant (only the 16-bit steps-8 forward and causal
 // adjoint keep a few bytes of spill at 168 and 255 registers); the host sizes
 // the grid from the occupancy the variant really gets (bld_march_ctas_per_sm).
-template <typename T, int S, bool CAUSAL, bool ADJ>
+template <typename T, int S, bool CAUSAL, bool ADJ, bool RES = false>
 constexpr int march_min_ctas() {
   constexpr bool F32 = sizeof(T) == 4;
-  if (!ADJ) return S <= 4 ? kFwdMinCtas : (S == 5 || (S == 6 && F32)) ? 16 : 12;
+  if (!ADJ) return S <= 4 ? kFwdMinCtas : (S == 5 || (S == 6 && F32 && !RES)) ? 16 : 12;
   if (!CAUSAL) return S <= 3 ? kFwdMinCtas : S <= 5 ? 16 : (S == 8 && F32) ? 8 : 12;
   return S <= 3 ? (kFwdMinCtas < 16 ? kFwdMinCtas : 16) : S <= 5 ? 12 : 8;
 }
 
-template <typename T, int S, bool CAUSAL, bool ADJ>
-__global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ>()))
+// RES (non-causal forward only): y = residual + stencil(x) in the same pass.
+// The residual rows of each full output chunk are brought by a TMA load into
+// the staging slot that chunk is about to use, issued one chunk ahead; the
+// lanes add them in place and the TMA store sends the sum out.
+template <typename T, int S, bool CAUSAL, bool ADJ, bool RES>
+__global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ, RES>()))
     bld_march_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
-                     const BldArgs a) {
+                     const __grid_constant__ CUtensorMap rmap, const BldArgs a) {
+  static_assert(!RES || (!ADJ && !CAUSAL), "the residual form is the non-causal forward");
   using Q = ColVec<T, kFwdVec>;
   using V = typename Q::V;
   // halo rows above the tile: the causal forward reads 2S rows back, its
@@ -100,6 +105,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   T* ring = reinterpret_cast<T*>(smem_raw);
   T* stage = ring + kFwdStages * CHUNK;  // output staging for the TMA stores
   __shared__ __align__(8) uint64_t full_bar[kFwdStages];
+  __shared__ __align__(8) uint64_t res_bar[RES ? 2 : 1];
   __shared__ uint32_t fbits[kBldMaxWords + 2];
   __shared__ uint32_t zbits[kBldMaxWords + 2];
 
@@ -116,6 +122,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   const int nout = static_cast<int>(oend - l0 < a.TL ? oend - l0 : a.TL);
   const int nrows = PRO + nout;
   const int nch = (nrows + kFwdRC - 1) / kFwdRC;
+  const int nfull_end = nrows / kFwdRC;  // chunks [NPRO, nfull_end) are full
   const int tid = threadIdx.x;
   const bool use_tma = a.use_tma != 0;
   const bool tstore = a.use_tma_store != 0;
@@ -125,8 +132,20 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
     if (tstore) prefetch_tmap(&ymap);
 #pragma unroll
     for (int s = 0; s < kFwdStages; ++s) mbar_init(&full_bar[s], 1);
+    if constexpr (RES) {
+      prefetch_tmap(&rmap);
+      mbar_init(&res_bar[0], 1);
+      mbar_init(&res_bar[1], 1);
+    }
     fence_mbar_init();
   }
+  // full output chunk c's residual rows into its staging slot
+  auto issue_res = [&](int c) {
+    const int slot = (c - NPRO) & 1;
+    mbar_arrive_expect_tx(&res_bar[slot], CHUNK * sizeof(T));
+    tma_load_3d(stage + slot * CHUNK, &rmap, &res_bar[slot], d0, static_cast<int>(sg.row0 + l0 + c * kFwdRC - PRO),
+                sg.bcoord);
+  };
   auto issue = [&](int c) {
     const int slot = c % kFwdStages;
     mbar_arrive_expect_tx(&full_bar[slot], CHUNK * sizeof(T));
@@ -161,19 +180,29 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   const bool col_ok = col < a.D;
   const bool quad_ok = a.y_quad_ok != 0 && col + kFwdVec - 1 < a.D;
   T* const ybase = static_cast<T*>(a.y) + static_cast<int64_t>(sg.bcoord) * a.ysB + sg.row0 * a.ysL + col;
+  const T* const rbase =
+      RES ? static_cast<const T*>(a.residual) + static_cast<int64_t>(sg.bcoord) * a.rsB + sg.row0 * a.rsL + col
+          : nullptr;
   const int soff = cb;  // element offset of this lane in a slot row
 
   auto store_row = [&](int64_t orow, pf2 pa, pf2 pb) {
     T* yp = ybase + orow * a.ysL;
     if (quad_ok) {
-      *reinterpret_cast<V*>(yp) = Q::join(pa, pb);
+      V y = Q::join(pa, pb);
+      if constexpr (RES) y = vec_add_round<Q>(y, *reinterpret_cast<const V*>(rbase + orow * a.rsL));
+      *reinterpret_cast<V*>(yp) = y;
     } else if (col_ok) {
       float v[4];
       upk(pa, v[0], v[1]);
       upk(pb, v[2], v[3]);
 #pragma unroll
-      for (int j = 0; j < kFwdVec; ++j)
-        if (col + j < a.D) yp[j] = Elem<T>::from_f(v[j]);
+      for (int j = 0; j < kFwdVec; ++j) {
+        if (col + j < a.D) {
+          T t = Elem<T>::from_f(v[j]);
+          if constexpr (RES) t = Elem<T>::from_f(Elem<T>::to_f(t) + Elem<T>::to_f(rbase[orow * a.rsL + j]));
+          yp[j] = t;
+        }
+      }
     }
   };
 
@@ -295,8 +324,14 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
         step_row(slow_tag, std::integral_constant<int, -1>{}, jb + t0 + i, xa, xb);
         const int64_t orow = l0 + t0 + i - PRO;
         if constexpr (KIND == NPRO) {
-          if (tstore) *reinterpret_cast<V*>(st + i * kFwdDT) = Q::join(xa, xb);
-          else store_row(orow, xa, xb);
+          if (tstore) {
+            V y = Q::join(xa, xb);
+            // RES: the slot row holds the residual (TMA-loaded for this chunk)
+            if constexpr (RES) y = vec_add_round<Q>(y, *reinterpret_cast<const V*>(st + i * kFwdDT));
+            *reinterpret_cast<V*>(st + i * kFwdDT) = y;
+          } else {
+            store_row(orow, xa, xb);
+          }
         } else {
           if (t0 + i < nrows) store_row(orow, xa, xb);
         }
@@ -318,6 +353,9 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       fill_fwd_chunk<T>(a, sg, jb + c * kFwdRC, d0, ring + slot * CHUNK);
       __syncwarp();
     }
+    if constexpr (RES && FULL) {
+      if (tstore && !err && !mbar_wait_bounded(&res_bar[(c - NPRO) & 1], ((c - NPRO) >> 1) & 1)) err = 1;
+    }
     if (!err) march_chunk(slow_tag, kind_tag, c, buf);
     if (FULL && tstore) fence_proxy_async_smem();
     // the store issued after the previous chunk must have finished reading the
@@ -331,6 +369,9 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
         if (use_tma)
           for (int cc = c; cc < nch && cc < c + kFwdStages; ++cc)
             mbar_wait_bounded(&full_bar[cc % kFwdStages], (cc / kFwdStages) & 1);
+        // the residual load of this chunk, if one was issued (a completed phase passes at once)
+        if (RES && tstore && c >= NPRO && c < nfull_end)
+          mbar_wait_bounded(&res_bar[(c - NPRO) & 1], ((c - NPRO) >> 1) & 1);
         if (tstore) bulk_wait_all();
       }
       __syncwarp();
@@ -342,6 +383,9 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
         tma_store_3d(&ymap, stage + ((c - NPRO) & 1) * CHUNK, d0, orow0, sg.bcoord);
         bulk_commit();
       }
+      // the next full chunk's staging slot was last read by the store of chunk
+      // c-1, which bulk_wait_read_all above has seen complete
+      if (RES && tstore && c + 1 >= NPRO && c + 1 < nfull_end) issue_res(c + 1);
       if (use_tma && c + kFwdStages < nch) issue(c + kFwdStages);
     }
     return true;
@@ -349,7 +393,6 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
 
   // prologue chunks, then a single-body loop over full chunks, then the
   // partial last chunk; the fast/slow choice is made once per tile
-  const int nfull_end = nrows / kFwdRC;  // chunks [NPRO, nfull_end) are full
   auto run = [&](auto slow_tag) -> bool {
     if (!do_chunk(slow_tag, std::integral_constant<int, 0>{}, 0)) return false;
     if constexpr (NPRO > 1) {
@@ -372,49 +415,52 @@ size_t fwd_smem_bytes(int dtype) {
 
 namespace {
 
-template <typename T, bool CAUSAL, bool ADJ>
+template <typename T, bool CAUSAL, bool ADJ, bool RES>
 const void* march_ptr(int steps) {
   switch (steps) {
-    case 1: return reinterpret_cast<const void*>(bld_march_kernel<T, 1, CAUSAL, ADJ>);
-    case 2: return reinterpret_cast<const void*>(bld_march_kernel<T, 2, CAUSAL, ADJ>);
-    case 3: return reinterpret_cast<const void*>(bld_march_kernel<T, 3, CAUSAL, ADJ>);
-    case 4: return reinterpret_cast<const void*>(bld_march_kernel<T, 4, CAUSAL, ADJ>);
-    case 5: return reinterpret_cast<const void*>(bld_march_kernel<T, 5, CAUSAL, ADJ>);
-    case 6: return reinterpret_cast<const void*>(bld_march_kernel<T, 6, CAUSAL, ADJ>);
-    case 7: return reinterpret_cast<const void*>(bld_march_kernel<T, 7, CAUSAL, ADJ>);
-    case 8: return reinterpret_cast<const void*>(bld_march_kernel<T, 8, CAUSAL, ADJ>);
+    case 1: return reinterpret_cast<const void*>(bld_march_kernel<T, 1, CAUSAL, ADJ, RES>);
+    case 2: return reinterpret_cast<const void*>(bld_march_kernel<T, 2, CAUSAL, ADJ, RES>);
+    case 3: return reinterpret_cast<const void*>(bld_march_kernel<T, 3, CAUSAL, ADJ, RES>);
+    case 4: return reinterpret_cast<const void*>(bld_march_kernel<T, 4, CAUSAL, ADJ, RES>);
+    case 5: return reinterpret_cast<const void*>(bld_march_kernel<T, 5, CAUSAL, ADJ, RES>);
+    case 6: return reinterpret_cast<const void*>(bld_march_kernel<T, 6, CAUSAL, ADJ, RES>);
+    case 7: return reinterpret_cast<const void*>(bld_march_kernel<T, 7, CAUSAL, ADJ, RES>);
+    case 8: return reinterpret_cast<const void*>(bld_march_kernel<T, 8, CAUSAL, ADJ, RES>);
     default: return nullptr;
   }
 }
 
 template <typename T>
-const void* march_ptr_t(int steps, int causal, int adj) {
-  if (adj) return causal ? march_ptr<T, true, true>(steps) : march_ptr<T, false, true>(steps);
-  return causal ? march_ptr<T, true, false>(steps) : march_ptr<T, false, false>(steps);
+const void* march_ptr_t(int steps, int causal, int adj, int res) {
+  if (res) return (causal || adj) ? nullptr : march_ptr<T, false, false, true>(steps);
+  if (adj) return causal ? march_ptr<T, true, true, false>(steps) : march_ptr<T, false, true, false>(steps);
+  return causal ? march_ptr<T, true, false, false>(steps) : march_ptr<T, false, false, false>(steps);
 }
 
-const void* march_kernel(int dtype, int steps, int causal, int adj) {
+const void* march_kernel(int dtype, int steps, int causal, int adj, int res) {
   switch (dtype) {
-    case kF32: return march_ptr_t<float>(steps, causal, adj);
-    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, adj);
-    case kF16: return march_ptr_t<__half>(steps, causal, adj);
+    case kF32: return march_ptr_t<float>(steps, causal, adj, res);
+    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, adj, res);
+    case kF16: return march_ptr_t<__half>(steps, causal, adj, res);
     default: return nullptr;
   }
 }
 
 }  // namespace
 
-cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, int dtype, int steps,
-                           int causal, int adjoint, dim3 grid, size_t smem, cudaStream_t st) {
-  const void* kern = march_kernel(dtype, steps, causal, adjoint);
+cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap,
+                           const CUtensorMap* rmap, int dtype, int steps, int causal, int adjoint, dim3 grid,
+                           size_t smem, cudaStream_t st) {
+  const void* kern = march_kernel(dtype, steps, causal, adjoint, a.residual != nullptr ? 1 : 0);
   if (kern == nullptr) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem_attr(kern, smem);
   if (e != cudaSuccess) return e;
-  void* args[] = {const_cast<CUtensorMap*>(xmap), const_cast<CUtensorMap*>(ymap), const_cast<BldArgs*>(&a)};
+  void* args[] = {const_cast<CUtensorMap*>(xmap), const_cast<CUtensorMap*>(ymap), const_cast<CUtensorMap*>(rmap),
+                  const_cast<BldArgs*>(&a)};
   return cudaLaunchKernel(kern, grid, dim3(kFwdThreads), args, smem, st);
 }
 
-int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint) {
+int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual) {
   struct Entry {
     const void* kern;
     int dev;
@@ -423,7 +469,7 @@ int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint) {
   static Entry table[256];
   static int used = 0;
   static std::mutex mu;
-  const void* kern = march_kernel(dtype, steps, causal, adjoint);
+  const void* kern = march_kernel(dtype, steps, causal, adjoint, residual);
   if (kern == nullptr) return -1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;

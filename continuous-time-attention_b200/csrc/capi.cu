@@ -166,8 +166,8 @@ int pick_tl(int64_t rows, int64_t parallel_ctas, int steps, int per_sm) {
 
 // target resident CTAs per SM of a march kernel: the tuning value, capped by
 // the occupancy the variant gets (deep variants hold more registers)
-int march_per_sm(int dtype, int steps, int causal, int adjoint) {
-  const int occ = bld_march_ctas_per_sm(dtype, steps, causal, adjoint);
+int march_per_sm(int dtype, int steps, int causal, int adjoint, int residual = 0) {
+  const int occ = bld_march_ctas_per_sm(dtype, steps, causal, adjoint, residual);
   return occ > 0 ? std::min(g_tuning.fwd_ctas_per_sm, occ) : g_tuning.fwd_ctas_per_sm;
 }
 
@@ -211,7 +211,9 @@ bool quad_ok(const void* y, int dtype, int64_t nb, int64_t D, int64_t sB, int64_
 }
 
 int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int64_t tile_rows, cudaStream_t st,
-               const CUtensorMap& xmap, const CUtensorMap& ymap, int adjoint = 0) {
+               const CUtensorMap& xmap, const CUtensorMap& ymap, int adjoint = 0,
+               const CUtensorMap* rmap = nullptr) {
+  static const CUtensorMap kNoMap = {};
   const int64_t ntl = (tile_rows + a.TL - 1) / a.TL;
   const int64_t ndt = (a.D + kFwdDT - 1) / kFwdDT;
   if (ntl <= 0 || nbatch <= 0) return ok();
@@ -221,7 +223,8 @@ int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int
   // x = row tile * column tiles + column tile (column tile fastest)
   dim3 grid(static_cast<unsigned>(ntl * ndt), 1u, static_cast<unsigned>(nbatch));
   const cudaError_t e =
-      launch_bld_fwd(a, &xmap, &ymap, dtype, steps, causal, adjoint, grid, fwd_smem_bytes(dtype), st);
+      launch_bld_fwd(a, &xmap, &ymap, rmap != nullptr ? rmap : &kNoMap, dtype, steps, causal, adjoint, grid,
+                     fwd_smem_bytes(dtype), st);
   if (e != cudaSuccess) return cuda_fail(e, "bld forward launch");
   return ok();
 }
@@ -399,10 +402,10 @@ int cta_diffusion_bwd_bdl(const void* grad_out, void* grad_in, int64_t B, int64_
 // ---------------------------------------------------------------------------
 // [B, L, D]
 // ---------------------------------------------------------------------------
-int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t D, int64_t x_sB, int64_t x_sL,
-                          int64_t y_sB, int64_t y_sL, int dtype, int steps, int causal, const float* alpha,
-                          const void* const* alpha_dev, int alpha_dev_dtype, const void* mask, int mask_dtype,
-                          int64_t mask_sB, int64_t mask_sL, void* stream) {
+static int fwd_bld_impl(const void* x, const void* residual, void* y, int64_t B, int64_t L, int64_t D, int64_t x_sB,
+                        int64_t x_sL, int64_t r_sB, int64_t r_sL, int64_t y_sB, int64_t y_sL, int dtype, int steps,
+                        int causal, const float* alpha, const void* const* alpha_dev, int alpha_dev_dtype,
+                        const void* mask, int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream) {
   int rc = check_common(dtype, steps);
   if (rc) return rc;
   rc = check_alpha(steps, alpha, alpha_dev, alpha_dev_dtype);
@@ -431,7 +434,7 @@ int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t 
   a.msL = mask_sL;
   fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-  a.TL = pick_tl(L, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, 0));
+  a.TL = pick_tl(L, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, 0, residual != nullptr ? 1 : 0));
   a.out_begin = 0;
   a.out_end = L;
   a.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
@@ -440,7 +443,36 @@ int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t 
   std::memset(&ymap, 0, sizeof(ymap));
   a.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
   a.use_tma_store = make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
-  return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), xmap, ymap);
+  CUtensorMap rmap;
+  std::memset(&rmap, 0, sizeof(rmap));
+  if (residual != nullptr) {
+    if (causal) return fail(CTA_EUNSUPPORTED, "the fused residual add is the non-causal forward");
+    if (r_sL < D) return fail(CTA_EINVAL, "residual row stride smaller than D");
+    a.residual = residual;
+    a.rsB = r_sB;
+    a.rsL = r_sL;
+    if (!quad_ok(residual, dtype, B, D, r_sB, r_sL)) a.y_quad_ok = 0;
+    // full chunks take the residual through the staging buffer: it needs a map
+    if (!make_map(&rmap, residual, dtype, B, L, D, r_sB, r_sL, kFwdRC, kFwdDT)) a.use_tma_store = 0;
+  }
+  return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), xmap, ymap, 0, &rmap);
+}
+
+int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t D, int64_t x_sB, int64_t x_sL,
+                          int64_t y_sB, int64_t y_sL, int dtype, int steps, int causal, const float* alpha,
+                          const void* const* alpha_dev, int alpha_dev_dtype, const void* mask, int mask_dtype,
+                          int64_t mask_sB, int64_t mask_sL, void* stream) {
+  return fwd_bld_impl(x, nullptr, y, B, L, D, x_sB, x_sL, 0, 0, y_sB, y_sL, dtype, steps, causal, alpha, alpha_dev,
+                      alpha_dev_dtype, mask, mask_dtype, mask_sB, mask_sL, stream);
+}
+
+int cta_diffusion_fwd_bld_residual(const void* x, const void* residual, void* y, int64_t B, int64_t L, int64_t D,
+                                   int64_t x_sB, int64_t x_sL, int64_t r_sB, int64_t r_sL, int64_t y_sB,
+                                   int64_t y_sL, int dtype, int steps, const float* alpha, const void* mask,
+                                   int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream) {
+  if (residual == nullptr) return fail(CTA_EINVAL, "null residual pointer");
+  return fwd_bld_impl(x, residual, y, B, L, D, x_sB, x_sL, r_sB, r_sL, y_sB, y_sL, dtype, steps, 0, alpha, nullptr,
+                      0, mask, mask_dtype, mask_sB, mask_sL, stream);
 }
 
 int64_t cta_diffusion_bwd_bld_workspace_bytes(int64_t B, int64_t L, int64_t D, int dtype, int steps, int causal) {
@@ -589,9 +621,9 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
   return ok();
 }
 
-int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t D, int64_t x_sL, int64_t y_sL,
-                             const int32_t* cu_seqlens, int64_t nseq, int64_t max_len, int pad_to_max, int dtype,
-                             int steps, float alpha, void* stream) {
+static int fwd_varlen_impl(const void* x, const void* residual, void* y, int64_t total_rows, int64_t D,
+                           int64_t x_sL, int64_t r_sL, int64_t y_sL, const int32_t* cu_seqlens, int64_t nseq,
+                           int64_t max_len, int pad_to_max, int dtype, int steps, float alpha, void* stream) {
   int rc = check_common(dtype, steps);
   if (rc) return rc;
   if (total_rows < 0 || D < 0 || nseq < 0 || max_len < 0) return fail(CTA_EINVAL, "negative shape");
@@ -618,7 +650,7 @@ int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t
   // the waves balanced across unequal lengths (halo overhead 2*steps/TL)
   const int64_t avg = std::max<int64_t>(1, total_rows / nseq);
   a.TL = g_tuning.tl_override > 0
-             ? pick_tl(avg, ndt * nseq, steps, march_per_sm(dtype, steps, 0, 0))
+             ? pick_tl(avg, ndt * nseq, steps, march_per_sm(dtype, steps, 0, 0, residual != nullptr ? 1 : 0))
              : static_cast<int>(std::min<int64_t>(512, std::max<int64_t>(64, ((avg / 8 + 15) / 16) * 16)));
   a.out_begin = 0;
   a.out_end = max_len;
@@ -628,7 +660,33 @@ int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t
   std::memset(&ymap, 0, sizeof(ymap));
   a.use_tma = make_map(&xmap, x, dtype, 1, total_rows, D, 0, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
   a.use_tma_store = make_map(&ymap, y, dtype, 1, total_rows, D, 0, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
-  return launch_fwd(a, dtype, steps, 0, nseq, max_len, static_cast<cudaStream_t>(stream), xmap, ymap);
+  CUtensorMap rmap;
+  std::memset(&rmap, 0, sizeof(rmap));
+  if (residual != nullptr) {
+    if (r_sL < D) return fail(CTA_EINVAL, "residual row stride smaller than D");
+    a.residual = residual;
+    a.rsB = 0;
+    a.rsL = r_sL;
+    if (!quad_ok(residual, dtype, 1, D, 0, r_sL)) a.y_quad_ok = 0;
+    if (!make_map(&rmap, residual, dtype, 1, total_rows, D, 0, r_sL, kFwdRC, kFwdDT)) a.use_tma_store = 0;
+  }
+  return launch_fwd(a, dtype, steps, 0, nseq, max_len, static_cast<cudaStream_t>(stream), xmap, ymap, 0, &rmap);
+}
+
+int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t D, int64_t x_sL, int64_t y_sL,
+                             const int32_t* cu_seqlens, int64_t nseq, int64_t max_len, int pad_to_max, int dtype,
+                             int steps, float alpha, void* stream) {
+  return fwd_varlen_impl(x, nullptr, y, total_rows, D, x_sL, 0, y_sL, cu_seqlens, nseq, max_len, pad_to_max, dtype,
+                         steps, alpha, stream);
+}
+
+int cta_diffusion_fwd_varlen_residual(const void* x, const void* residual, void* y, int64_t total_rows, int64_t D,
+                                      int64_t x_sL, int64_t r_sL, int64_t y_sL, const int32_t* cu_seqlens,
+                                      int64_t nseq, int64_t max_len, int pad_to_max, int dtype, int steps,
+                                      float alpha, void* stream) {
+  if (residual == nullptr) return fail(CTA_EINVAL, "null residual pointer");
+  return fwd_varlen_impl(x, residual, y, total_rows, D, x_sL, r_sL, y_sL, cu_seqlens, nseq, max_len, pad_to_max,
+                         dtype, steps, alpha, stream);
 }
 
 int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_local, int64_t D, int64_t pos_offset,

@@ -238,6 +238,16 @@ template <> struct Quad<float> {
   }
 };
 template <typename T> struct ColVec<T, 4> : Quad<T> {};
+
+// y + r for two element vectors of T (y as stored, i.e. already rounded to T),
+// added in fp32 and rounded once: an elementwise add of two tensors of type T
+template <typename Q>
+__device__ __forceinline__ typename Q::V vec_add_round(typename Q::V y, typename Q::V r) {
+  pf2 ya, yb, ra, rb;
+  Q::split(y, ya, yb);
+  Q::split(r, ra, rb);
+  return Q::join(padd(ya, ra), padd(yb, rb));
+}
 template <typename T> struct ColVec<T, 2> {
   // one pair; the second pair of the interface is unused and stays zero
   using V = typename std::conditional<sizeof(T) == 4, float2, uint32_t>::type;

@@ -90,6 +90,10 @@ struct BldArgs {
   int num_ctas;
   int dalpha_group;        // CTAs per reduction group (march d(alpha) kernel)
   int dalpha_accumulate;   // add the result to dalpha[] instead of overwriting it
+  // forward only: y = residual + stencil(x), the residual [B, L, D] / [T, D]
+  // with element strides (rsB, rsL), added as an elementwise add of type T
+  const void* residual;
+  int64_t rsB, rsL;
   // L-shard halos of the gradient stream for the d(alpha) kernel (lo_ext/hi_ext
   // above hold the x stream's): [nbatch, g_hext_lo|hi, D]
   const void* g_lo_ext;
@@ -134,10 +138,12 @@ struct BdlArgs {
 // launchers (return cudaError_t of the launch)
 // resident one-warp CTAs per SM of a march kernel variant on the current device
 // (occupancy query, cached), or -1
-int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint);
+int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual = 0);
 // march kernel: forward (adjoint = 0) or the adjoint without d(alpha) (adjoint = 1)
-cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap, int dtype,
-                           int steps, int causal, int adjoint, dim3 grid, size_t smem, cudaStream_t st);
+// rmap: residual map (box as ymap), read only when a.residual is set (non-causal forward)
+cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap,
+                           const CUtensorMap* rmap, int dtype, int steps, int causal, int adjoint, dim3 grid,
+                           size_t smem, cudaStream_t st);
 cudaError_t launch_bld_bwd(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap, int dtype,
                            int steps, int causal, int with_dalpha, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st);

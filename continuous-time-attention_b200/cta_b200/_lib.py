@@ -65,6 +65,12 @@ _SIGNATURES = {
                                               c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
                                               c_int, POINTER(c_float), POINTER(c_void_p), c_int, c_void_p, c_int,
                                               c_int64, c_int64, c_void_p]),
+    "cta_diffusion_fwd_varlen_residual": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                                                  c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_float,
+                                                  c_void_p]),
+    "cta_diffusion_fwd_bld_residual": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                                               c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+                                               POINTER(c_float), c_void_p, c_int, c_int64, c_int64, c_void_p]),
     "cta_diffusion_shard_bld_dalpha": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                                                c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                                                c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,

@@ -73,6 +73,12 @@ def _out(out: Optional[torch.Tensor], shape, like: torch.Tensor, contiguous: boo
     return out
 
 
+def _residual_view(residual: torch.Tensor, shape, like: torch.Tensor) -> torch.Tensor:
+    if tuple(residual.shape) != tuple(shape) or residual.dtype != like.dtype or residual.device != like.device:
+        raise ValueError(f"residual must be {tuple(shape)} {like.dtype} on {like.device}")
+    return residual if residual.stride(-1) == 1 else residual.contiguous()
+
+
 # ---------------------------------------------------------------------------
 # [B, D, L]
 # ---------------------------------------------------------------------------
@@ -141,8 +147,12 @@ def bld_forward(
     causal: bool = False,
     mask: Optional[torch.Tensor] = None,
     out: Optional[torch.Tensor] = None,
+    residual: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
-    """`steps` fused steps on [B, L, D] (feature axis contiguous), one launch."""
+    """`steps` fused steps on [B, L, D] (feature axis contiguous), one launch.
+
+    With `residual` (non-causal, host alphas) the same launch returns
+    residual + stencil(x), equal bit for bit to the two-pass result."""
     _require_cuda(x, "x")
     if x.dim() != 3:
         raise ValueError("x must have shape (B, L, D)")
@@ -152,6 +162,19 @@ def bld_forward(
     fa, pa, pcode, keep = _alpha_args(alphas, steps, x.device)
     m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
     lib = _lib.load()
+    if residual is not None:
+        r = _residual_view(residual, (B, L, D), x)
+        if causal or pa is not None:
+            raise ValueError("the fused residual add takes the non-causal stencil with host alphas")
+        with _lib.on_device(x):
+            rc = lib.cta_diffusion_fwd_bld_residual(
+                _lib.ptr(x), _lib.ptr(r), _lib.ptr(y), B, L, D, x.stride(0), x.stride(1), r.stride(0), r.stride(1),
+                y.stride(0), y.stride(1), _lib.dtype_code(x.dtype), steps, fa, _lib.ptr(m), mcode, msb, msl,
+                _lib.stream_ptr(x),
+            )
+        del keep
+        _lib.check(rc)
+        return y
     with _lib.on_device(x):
         rc = lib.cta_diffusion_fwd_bld(
             _lib.ptr(x), _lib.ptr(y), B, L, D, x.stride(0), x.stride(1), y.stride(0), y.stride(1),
@@ -234,6 +257,7 @@ def varlen_forward(
     *,
     pad_to_max: bool,
     out: Optional[torch.Tensor] = None,
+    residual: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """Packed [T, D] prefill with device cu_seqlens (int32, nseq+1); one launch."""
     _require_cuda(x, "x")
@@ -251,6 +275,16 @@ def varlen_forward(
     y = _out(out, (T, D), x, contiguous=True)
     nseq = cu_seqlens.numel() - 1
     lib = _lib.load()
+    if residual is not None:
+        r = _residual_view(residual, (T, D), x)
+        with _lib.on_device(x):
+            rc = lib.cta_diffusion_fwd_varlen_residual(
+                _lib.ptr(x), _lib.ptr(r), _lib.ptr(y), T, D, x.stride(0), r.stride(0), y.stride(0),
+                _lib.ptr(cu_seqlens), nseq, int(max_len), int(pad_to_max), _lib.dtype_code(x.dtype), steps,
+                float(alpha), _lib.stream_ptr(x),
+            )
+        _lib.check(rc)
+        return y
     with _lib.on_device(x):
         rc = lib.cta_diffusion_fwd_varlen(
             _lib.ptr(x), _lib.ptr(y), T, D, x.stride(0), y.stride(0), _lib.ptr(cu_seqlens), nseq, int(max_len),

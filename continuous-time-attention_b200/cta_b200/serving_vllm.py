@@ -132,26 +132,38 @@ class CtaPostAttnMixer(nn.Module):
         *,
         attn_metadata: Optional[object] = None,
         is_prefill: Optional[bool] = None,
+        residual: Optional[torch.Tensor] = None,
     ) -> torch.Tensor:
+        """The mixer of src/cta/serving_vllm.py:225-273.  With `residual` it
+        returns residual + mixer(x), the decoder layer's next line
+        (serving/vllm/patches/vllm_0_13_0_cta_post_attn.patch:66-68), with the add
+        fused into the stencil's last launch where there is one."""
+        out, fused = self._mix(x, attn_metadata=attn_metadata, is_prefill=is_prefill, residual=residual)
+        if residual is not None and not fused:
+            out = residual + out
+        return out
+
+    def _mix(self, x, *, attn_metadata, is_prefill, residual):
+        """(output, residual already added)."""
         if x.ndim == 2:
-            return self._forward_packed(x, attn_metadata=attn_metadata, is_prefill=is_prefill)
+            return self._mix_packed(x, attn_metadata=attn_metadata, is_prefill=is_prefill, residual=residual)
         if not self.config.enabled:
-            return x
+            return x, False
         if self.config.prefill_only:
             if is_prefill is None:
                 is_prefill = _infer_prefill(attn_metadata)
             if not is_prefill:
-                return x
+                return x, False
         seq_dim = 2 if self.config.layout == "bdl" else 1
         steps = self._resolve_steps(x.size(seq_dim))
         if steps <= 0:
-            return x
+            return x, False
         if x.device.type != "cuda":
             raise ValueError("x must be on CUDA")
         if x.ndim != 3:
             raise ValueError(f"expected x.ndim == 3, got {x.ndim}")
         if x.size(seq_dim) < 3:
-            return x
+            return x, False
         ctx = record_function("cta_post_attn_mixer") if self.config.trace else nullcontext()
         alpha = float(self.config.alpha)
         with ctx:
@@ -161,16 +173,18 @@ class CtaPostAttnMixer(nn.Module):
                     s = min(_lib.MAX_STEPS, steps - i)
                     if self.config.layout == "bdl":
                         out = ops.bdl_simple(out, alpha, s)
+                    elif residual is not None and i + s == steps:
+                        return ops.bld_forward(out, [alpha] * s, s, residual=residual), True
                     else:
                         out = ops.bld_forward(out, [alpha] * s, s)
-                return out
+                return out, False
             # reference's non-fused path: one step at a time, rounded each step
             if self.config.layout == "bdl":
-                return diffusion_triton(x, alpha=alpha, steps=steps)
+                return diffusion_triton(x, alpha=alpha, steps=steps), False
             out = x
             for _ in range(steps):
                 out = ops.bld_forward(out, [alpha], 1)
-            return out
+            return out, False
 
     def _device_qsl(self, qsl: object, device: torch.device) -> torch.Tensor:
         if isinstance(qsl, torch.Tensor):
@@ -187,24 +201,36 @@ class CtaPostAttnMixer(nn.Module):
         is_prefill: Optional[bool],
     ) -> torch.Tensor:
         """Packed [T, H] prefill (src/cta/serving_vllm.py:275-303), one launch."""
+        return self._mix_packed(x, attn_metadata=attn_metadata, is_prefill=is_prefill, residual=None)[0]
+
+    def _mix_packed(
+        self,
+        x: torch.Tensor,
+        *,
+        attn_metadata: Optional[object],
+        is_prefill: Optional[bool],
+        residual: Optional[torch.Tensor] = None,
+    ):
+        """_forward_packed, optionally with the residual add fused into the last
+        launch.  Returns (output, residual already added)."""
         if not self.config.enabled:
-            return x
+            return x, False
         if attn_metadata is None:
-            return x
+            return x, False
         if self.config.prefill_only:
             if is_prefill is None:
                 is_prefill = _infer_prefill(attn_metadata)
             if not is_prefill:
-                return x
+                return x, False
         max_query_len = _to_int(getattr(attn_metadata, "max_query_len", None))
         query_start_loc = getattr(attn_metadata, "query_start_loc", None)
         if max_query_len is None or query_start_loc is None:
-            return x
+            return x, False
         if max_query_len < 3:
-            return x
+            return x, False
         steps = self._resolve_steps(max_query_len)
         if steps <= 0:
-            return x
+            return x, False
         if x.device.type != "cuda":
             raise ValueError("x must be on CUDA")
         cu = self._device_qsl(query_start_loc, x.device)
@@ -215,5 +241,7 @@ class CtaPostAttnMixer(nn.Module):
             out = x
             for i in range(0, steps, _lib.MAX_STEPS):
                 s = min(_lib.MAX_STEPS, steps - i)
-                out = ops.varlen_forward(out, cu, max_query_len, alpha, s, pad_to_max=pad)
-            return out
+                last = i + s == steps
+                out = ops.varlen_forward(out, cu, max_query_len, alpha, s, pad_to_max=pad,
+                                         residual=residual if last else None)
+            return out, residual is not None

@@ -149,6 +149,26 @@ int cta_diffusion_fwd_varlen(const void* x, void* y, int64_t total_rows, int64_t
                              const int32_t* cu_seqlens, int64_t nseq, int64_t max_len, int pad_to_max, int dtype,
                              int steps, float alpha, void* stream);
 
+/* Fused residual add of the vLLM decoder layer (no counterpart in the
+ * reference, whose patch computes `hidden_states = residual + mixer(x)` in two
+ * passes, serving/vllm/patches/vllm_0_13_0_cta_post_attn.patch:66-68):
+ * y = residual + stencil(x), the stencil result rounded to the tensor dtype
+ * first and the add done as the elementwise add of two tensors of that dtype,
+ * so the output equals the two-pass result bit for bit.  One pass: reads x and
+ * residual once, writes y once.  residual has y's shape; its own row stride.
+ * Non-causal forward only. */
+int cta_diffusion_fwd_varlen_residual(const void* x, const void* residual, void* y, int64_t total_rows, int64_t D,
+                                      int64_t x_sL, int64_t r_sL, int64_t y_sL, const int32_t* cu_seqlens,
+                                      int64_t nseq, int64_t max_len, int pad_to_max, int dtype, int steps,
+                                      float alpha, void* stream);
+
+/* The dense [B, L, D] form of cta_diffusion_fwd_varlen_residual (mask allowed,
+ * host alphas, non-causal). */
+int cta_diffusion_fwd_bld_residual(const void* x, const void* residual, void* y, int64_t B, int64_t L, int64_t D,
+                                   int64_t x_sB, int64_t x_sL, int64_t r_sB, int64_t r_sL, int64_t y_sB,
+                                   int64_t y_sL, int dtype, int steps, const float* alpha, const void* mask,
+                                   int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream);
+
 /* One shard of an L-sharded sequence ([B, L_local, D], contiguous): rows
  * [pos_offset, pos_offset + L_local) of a sequence of global_len rows.
  * lo_halo: [B, lo_rows, D] contiguous copy of the lo_rows rows just before the

@@ -53,7 +53,7 @@ def _mask(B, L, device="cpu"):
         m[0, L - 7:] = 0
         m[-1, 3] = 0
         m[-1, L // 2 : L // 2 + 2] = 0
-    return m
+    return m.to(device)
 
 
 @pytest.mark.parametrize("causal", [False, True])
@@ -207,3 +207,81 @@ def test_varlen_golden(golden):
         cu = torch.tensor(c["qsl"], dtype=torch.int32, device="cuda")
         y = _ops().varlen_forward(c["x"].cuda(), cu, c["max_len"], c["alpha"], c["steps"], pad_to_max=True)
         assert torch.equal(y.cpu(), c["y"])
+
+
+# ---------------------------------------------------------------------------
+# fused residual add (the decoder layer's `residual + mixer(attn_output)`)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("steps", [1, 2, 4, 5, 8])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("pad", [True, False])
+def test_varlen_residual_equals_two_pass(steps, dtype, pad):
+    """One launch of residual + stencil equals the two-pass result bit for bit,
+    and the reference rule equals the reference mixer + torch add."""
+    torch.manual_seed(20 + steps)
+    ops = _ops()
+    lens = [700, 3, 1, 0, 257, 64, 1999]
+    qsl = [0]
+    for n in lens:
+        qsl.append(qsl[-1] + n)
+    T, D = qsl[-1], 264
+    x = torch.randn(T, D).to(dtype)
+    r = torch.randn(T, D).to(dtype)
+    cu = torch.tensor(qsl, dtype=torch.int32, device="cuda")
+    y1 = ops.varlen_forward(x.cuda(), cu, max(lens), 0.1, steps, pad_to_max=pad, residual=r.cuda())
+    y2 = r.cuda() + ops.varlen_forward(x.cuda(), cu, max(lens), 0.1, steps, pad_to_max=pad)
+    assert torch.equal(y1, y2)
+    if pad:
+        ref = r + O.mixer_packed(x, qsl, max(lens), alpha=0.1, steps=steps)
+        assert torch.equal(y1.cpu(), ref)
+
+
+@pytest.mark.parametrize("shape", [(2, 1000, 512), (1, 77, 513), (3, 129, 264), (2, 3, 8)])
+@pytest.mark.parametrize("use_mask", [False, True])
+def test_bld_residual_equals_two_pass(shape, use_mask):
+    torch.manual_seed(21)
+    ops = _ops()
+    B, L, D = shape
+    for dtype in (torch.bfloat16, torch.float32):
+        x = torch.randn(B, L, D, device="cuda").to(dtype)
+        base = torch.randn(B, L, D + 8, device="cuda").to(dtype)
+        r = base[:, :, :D]  # rows with their own stride
+        m = _mask(B, L, "cuda") if use_mask else None
+        al = [0.1, 0.05, 0.12, 0.02]
+        y1 = ops.bld_forward(x, al, 4, mask=m, residual=r)
+        y2 = r + ops.bld_forward(x, al, 4, mask=m)
+        assert torch.equal(y1, y2), (shape, dtype)
+
+
+def test_bld_residual_rejects_causal_and_device_alphas():
+    ops = _ops()
+    x = torch.randn(1, 64, 32, device="cuda")
+    with pytest.raises(ValueError):
+        ops.bld_forward(x, [0.1] * 2, 2, causal=True, residual=x)
+    with pytest.raises(ValueError):
+        ops.bld_forward(x, [torch.tensor([0.1], device="cuda")], 1, residual=x)
+
+
+@pytest.mark.parametrize("varlen_mode", ["reference", "sequence"])
+def test_mixer_residual(varlen_mode):
+    """CtaPostAttnMixer(..., residual=r) returns r + mixer(x): fused on the packed
+    and [B, L, D] prefill paths, a plain add when the mixer is gated off."""
+    from types import SimpleNamespace
+
+    from cta_b200.serving_vllm import CtaConfig, CtaPostAttnMixer
+
+    torch.manual_seed(22)
+    mixer = CtaPostAttnMixer(CtaConfig(steps=4, alpha=0.1, varlen_mode=varlen_mode, trace=False))
+    lens = [300, 41, 1200]
+    qsl = torch.tensor([0, 300, 341, 1541], dtype=torch.int32, device="cuda")
+    x = torch.randn(1541, 512, device="cuda", dtype=torch.bfloat16)
+    r = torch.randn_like(x)
+    md = SimpleNamespace(max_query_len=max(lens), query_start_loc=qsl, is_prefill=True)
+    assert torch.equal(mixer(x, attn_metadata=md, residual=r), r + mixer(x, attn_metadata=md))
+    decode = SimpleNamespace(max_query_len=1, query_start_loc=qsl, is_prefill=False)
+    assert torch.equal(mixer(x, attn_metadata=decode, residual=r), r + x)
+    x3 = torch.randn(2, 700, 512, device="cuda", dtype=torch.bfloat16)
+    r3 = torch.randn_like(x3)
+    assert torch.equal(mixer(x3, is_prefill=True, residual=r3), r3 + mixer(x3, is_prefill=True))
+    long_mixer = CtaPostAttnMixer(CtaConfig(steps=11, alpha=0.1, max_steps=16, trace=False))
+    assert torch.equal(long_mixer(x3, is_prefill=True, residual=r3), r3 + long_mixer(x3, is_prefill=True))
