@@ -88,6 +88,9 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
     bld_march_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                      const __grid_constant__ CUtensorMap rmap, const BldArgs a) {
   static_assert(!RES || (!ADJ && !CAUSAL), "the residual form is the non-causal forward");
+  // every global read (cu_seqlens, mask, alphas, the streams) comes after the wait
+  pdl_launch_dependents();
+  pdl_wait();
   using Q = ColVec<T, kFwdVec>;
   using V = typename Q::V;
   // halo rows above the tile: the causal forward reads 2S rows back, its
@@ -457,7 +460,18 @@ cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUte
   if (e != cudaSuccess) return e;
   void* args[] = {const_cast<CUtensorMap*>(xmap), const_cast<CUtensorMap*>(ymap), const_cast<CUtensorMap*>(rmap),
                   const_cast<BldArgs*>(&a)};
-  return cudaLaunchKernel(kern, grid, dim3(kFwdThreads), args, smem, st);
+  if (!pdl_enabled()) return cudaLaunchKernel(kern, grid, dim3(kFwdThreads), args, smem, st);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kFwdThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
 int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual) {

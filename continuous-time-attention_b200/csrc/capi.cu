@@ -150,6 +150,7 @@ struct Tuning {
   int ctas_per_sm = 6;       // backward kernels (128-thread CTAs)
   int tl_override = 0;
   int fwd_ctas_per_sm = 16;  // forward kernels (one-warp CTAs): one full wave
+  int pdl = 0;               // march kernels launched with programmatic dependent launch
 };
 Tuning g_tuning;
 
@@ -272,6 +273,8 @@ int64_t dalpha_max_ctas(int64_t B, int64_t L, int64_t D) {
 
 }  // namespace
 
+int cta::pdl_enabled() { return g_tuning.pdl; }
+
 void cta::set_last_error(const char* fmt, ...) {
   char buf[512];
   va_list ap;
@@ -309,6 +312,9 @@ int cta_set_tuning(int key, int value) {
   } else if (key == 2) {
     prev = g_tuning.fwd_ctas_per_sm;
     g_tuning.fwd_ctas_per_sm = value > 0 ? value : 16;
+  } else if (key == 3) {
+    prev = g_tuning.pdl;
+    g_tuning.pdl = value != 0 ? 1 : 0;
   }
   return prev;
 }
@@ -760,6 +766,81 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
   a.use_tma_store = make_map(&omap, out, dtype, B, L_local, D, L_local * D, D, kFwdRC, kFwdDT) ? 1 : 0;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   return launch_fwd(a, dtype, steps, causal ? 1 : 0, B, oe - ob, st, map, omap, backward ? 1 : 0);
+}
+
+int64_t cta_pde_step_workspace_bytes(int64_t B, int64_t L, int64_t D) {
+  if (B <= 0 || L <= 0 || D <= 0) return 256;
+  PdeArgs p;
+  std::memset(&p, 0, sizeof(p));
+  p.L = L;
+  p.D = static_cast<int>(D);
+  p.nbatch = static_cast<int>(B);
+  return std::max<int64_t>(256, pde_step_num_ctas(p) * 2 * static_cast<int64_t>(sizeof(float)));
+}
+
+int cta_pde_step_bld(const void* x, const void* grad_out, void* y, float* dcoef, void* workspace,
+                     int64_t workspace_bytes, int64_t B, int64_t L, int64_t D, int64_t x_sB, int64_t x_sL,
+                     int64_t g_sB, int64_t g_sL, int64_t y_sB, int64_t y_sL, int dtype, int kind, int causal,
+                     int backward, const void* alpha_dev, const void* beta_dev, int coef_dtype, const void* mask,
+                     int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream) {
+  int rc = check_common(dtype, 1);
+  if (rc) return rc;
+  if (kind != CTA_PDE_ADVECTION && kind != CTA_PDE_REACTION) return fail(CTA_EINVAL, "bad PDE kind %d", kind);
+  if (alpha_dev == nullptr || beta_dev == nullptr) return fail(CTA_EINVAL, "alpha / beta device scalars missing");
+  if (coef_dtype != CTA_F32 && coef_dtype != CTA_BF16 && coef_dtype != CTA_F16)
+    return fail(CTA_EINVAL, "bad coefficient dtype %d", coef_dtype);
+  if (B < 0 || L < 0 || D < 0) return fail(CTA_EINVAL, "negative shape");
+  if (B > 65535) return fail(CTA_EUNSUPPORTED, "at most 65535 batch rows");
+  if (L > 0 && L < 3) return fail(CTA_EINVAL, "L < 3 is the identity; handled by the caller");
+  if (x == nullptr || y == nullptr || (backward && grad_out == nullptr))
+    return fail(CTA_EINVAL, "null tensor pointer");
+  if (x_sL < D || y_sL < D || (backward && g_sL < D)) return fail(CTA_EINVAL, "row stride smaller than D");
+  if (mask != nullptr && !valid_mask_dtype(mask_dtype)) return fail(CTA_EINVAL, "bad mask dtype %d", mask_dtype);
+  PdeArgs p;
+  std::memset(&p, 0, sizeof(p));
+  p.x = x;
+  p.g = grad_out;
+  p.y = y;
+  p.xsB = x_sB;
+  p.xsL = x_sL;
+  p.gsB = g_sB;
+  p.gsL = g_sL;
+  p.ysB = y_sB;
+  p.ysL = y_sL;
+  p.L = L;
+  p.D = static_cast<int>(D);
+  p.nbatch = static_cast<int>(B);
+  p.mask = mask;
+  p.mask_dtype = mask_dtype;
+  p.msB = mask_sB;
+  p.msL = mask_sL;
+  p.alpha_dev = alpha_dev;
+  p.beta_dev = beta_dev;
+  p.coef_dtype = coef_dtype;
+  p.x_vec = quad_ok(x, dtype, B, D, x_sB, x_sL) ? 1 : 0;
+  p.g_vec = (backward && quad_ok(grad_out, dtype, B, D, g_sB, g_sL)) ? 1 : 0;
+  p.y_vec = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
+  if (backward) {
+    if (dcoef == nullptr) return fail(CTA_EINVAL, "backward needs dcoef (fp32 [2])");
+    if (workspace == nullptr || reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+      return fail(CTA_EINVAL, "backward needs a 16-byte aligned workspace");
+    const int64_t need = cta_pde_step_workspace_bytes(B, L, D);
+    if (workspace_bytes < need)
+      return fail(CTA_EINVAL, "workspace too small: %lld < %lld bytes", (long long)workspace_bytes, (long long)need);
+    p.partial = static_cast<float*>(workspace);
+    p.dcoef = dcoef;
+  }
+  if (B == 0 || L == 0 || D == 0) {
+    if (backward) {
+      const cudaError_t e = cudaMemsetAsync(dcoef, 0, 2 * sizeof(float), static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e, "dcoef clear");
+    }
+    return ok();
+  }
+  const cudaError_t e = launch_pde_step(p, dtype, kind, causal ? 1 : 0, backward ? 1 : 0,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "pde step launch");
+  return ok();
 }
 
 int cta_diffusion_shard_bld_dalpha(const void* grad_out, const void* x, void* grad_in, float* dalpha,

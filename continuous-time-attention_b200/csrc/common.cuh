@@ -270,6 +270,13 @@ template <typename T> struct ColVec<T, 2> {
 // ---------------------------------------------------------------------------
 // shared-memory / mbarrier / TMA PTX wrappers
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  launch_dependents lets the next kernel of the
+// stream be scheduled as this grid's CTAs retire; wait blocks until every
+// prerequisite grid has completed and its memory operations are visible.  Both
+// are no-ops for a launch without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

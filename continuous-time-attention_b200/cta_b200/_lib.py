@@ -24,6 +24,7 @@ LIB_PATH = Path(os.environ.get("CTA_STENCIL_LIB") or Path(__file__).resolve().wi
 
 CTA_OK, CTA_EINVAL, CTA_EUNSUPPORTED, CTA_ECUDA = 0, 1, 2, 3
 SHARD_INTERIOR, SHARD_LO_EDGE, SHARD_HI_EDGE = 0, 1, 2
+PDE_ADVECTION, PDE_REACTION = 0, 1
 MAX_STEPS = 8
 
 _DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
@@ -71,6 +72,10 @@ _SIGNATURES = {
     "cta_diffusion_fwd_bld_residual": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                                                c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
                                                POINTER(c_float), c_void_p, c_int, c_int64, c_int64, c_void_p]),
+    "cta_pde_step_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "cta_pde_step_bld": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                                 c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_int, c_int,
+                                 c_void_p, c_void_p, c_int, c_void_p, c_int, c_int64, c_int64, c_void_p]),
     "cta_diffusion_shard_bld_dalpha": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                                                c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                                                c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,

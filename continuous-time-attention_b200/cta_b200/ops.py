@@ -189,13 +189,15 @@ def bld_forward(
 _WS: dict = {}
 
 
-def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Zero-initialised scratch for the d(alpha) reduction, one per (device, stream).
+def _workspace(device: torch.device, nbytes: int, tag: str = "dalpha") -> torch.Tensor:
+    """Zero-initialised scratch, one per (device, stream, tag).
 
-    The kernel leaves its completion counter at zero, so the buffer stays
-    reusable without clearing between calls on the same stream.
+    "dalpha": the d(alpha) reductions; their kernels leave the completion
+    counters at zero, so the buffer stays reusable without clearing between
+    calls on the same stream.  Other users take their own tag, so that nothing
+    else ever writes into those counters.
     """
-    key = (device, torch.cuda.current_stream(device).cuda_stream)
+    key = (device, torch.cuda.current_stream(device).cuda_stream, tag)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=device)
@@ -372,3 +374,58 @@ def shard_part_dalpha(
             _lib.float_array([float(a) for a in alphas]), st.cuda_stream,
         )
     _lib.check(rc)
+
+
+def pde_step(
+    x: torch.Tensor,
+    kind: int,
+    alpha: torch.Tensor,
+    beta: torch.Tensor,
+    *,
+    causal: bool = False,
+    mask: Optional[torch.Tensor] = None,
+    grad_out: Optional[torch.Tensor] = None,
+):
+    """One advection- / reaction-diffusion step on [B, L, D] (kind _lib.PDE_*).
+
+    Forward (grad_out None): returns y.  Backward: returns (dx, dcoef) with
+    dcoef = fp32 [d(alpha), d(beta)].  alpha, beta: the layer's [1] parameters,
+    read on the device."""
+    _require_cuda(x, "x")
+    if x.dim() != 3:
+        raise ValueError("x must have shape (B, L, D)")
+    x = _bld_view(x)
+    B, L, D = x.shape
+    coefs = []
+    for c in (alpha, beta):
+        c = c.detach()
+        if c.device != x.device:
+            raise ValueError(f"coefficient on {c.device}, expected {x.device}")
+        if c.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+            c = c.float()
+        coefs.append(c.contiguous())
+    if coefs[0].dtype != coefs[1].dtype:
+        coefs = [c.float() for c in coefs]
+    m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
+    lib = _lib.load()
+    code = _lib.dtype_code(x.dtype)
+    y = torch.empty((B, L, D), dtype=x.dtype, device=x.device)
+    g = None
+    dcoef = ws = None
+    ws_bytes = 0
+    if grad_out is not None:
+        g = _bld_view(grad_out)
+        if tuple(g.shape) != (B, L, D) or g.dtype != x.dtype:
+            raise ValueError("grad_out must match x in shape and dtype")
+        dcoef = torch.empty(2, dtype=torch.float32, device=x.device)
+        ws_bytes = int(lib.cta_pde_step_workspace_bytes(B, L, D))
+        ws = _workspace(x.device, ws_bytes, tag="pde_step")
+    with _lib.on_device(x):
+        rc = lib.cta_pde_step_bld(
+            _lib.ptr(x), _lib.ptr(g), _lib.ptr(y), _lib.ptr(dcoef), _lib.ptr(ws), ws_bytes, B, L, D, x.stride(0),
+            x.stride(1), g.stride(0) if g is not None else 0, g.stride(1) if g is not None else 0, y.stride(0),
+            y.stride(1), code, int(kind), int(causal), int(grad_out is not None), _lib.ptr(coefs[0]),
+            _lib.ptr(coefs[1]), _lib.dtype_code(coefs[0].dtype), _lib.ptr(m), mcode, msb, msl, _lib.stream_ptr(x),
+        )
+    _lib.check(rc)
+    return y if grad_out is None else (y, dcoef)

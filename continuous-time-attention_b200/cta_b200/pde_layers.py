@@ -16,10 +16,15 @@ Drop-in for the diffusion family of the reference's src/models/pde_layers.py:
   rounds to the input dtype after each (identical in fp32; within 2e-2 in
   bf16).
 
+* ``AdvectionDiffusionPDELayer`` / ``ReactionDiffusionPDELayer`` -- the
+  reference's other two layers (pde_layers.py:249-318, parameters ``alpha``
+  and ``beta``): one launch per step forward and one backward (dx, d(alpha),
+  d(beta)), as the reference runs them layer by layer.
+
 Arithmetic follows the reference op by op (fp32, no fused multiply-add), so a
-single fp32 or bf16 layer step is bit-identical to the reference layer.
-The reaction-diffusion and advection-diffusion layers have different update
-rules and are not served by these kernels.
+single fp32 or bf16 diffusion, wave or advection layer step is bit-identical to
+the reference layer; the reaction layer's sigmoid uses CUDA's expf, so it
+matches to fp32 rounding.
 """
 from __future__ import annotations
 
@@ -180,21 +185,95 @@ class WavePDELayer(_DiffusionFamilyLayer):
         return self.alpha.to(dtype=torch.float32) ** 2
 
 
+class _PDEStep(torch.autograd.Function):
+    """One advection- / reaction-diffusion step on [B, L, D]: forward and
+    backward are one launch each (the backward needs x: reaction is nonlinear)."""
+
+    @staticmethod
+    def forward(ctx, x, mask, kind, causal, alpha, beta):
+        y = ops.pde_step(x, kind, alpha, beta, causal=causal, mask=mask)
+        ctx.save_for_backward(x, alpha, beta)
+        ctx.mask, ctx.kind, ctx.causal = mask, kind, causal
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        x, alpha, beta = ctx.saved_tensors
+        dx, dcoef = ops.pde_step(x, ctx.kind, alpha, beta, causal=ctx.causal, mask=ctx.mask,
+                                 grad_out=g.to(x.dtype).contiguous())
+        da = dcoef[0:1].to(alpha.dtype).view_as(alpha) if ctx.needs_input_grad[4] else None
+        db = dcoef[1:2].to(beta.dtype).view_as(beta) if ctx.needs_input_grad[5] else None
+        return dx, None, None, None, da, db
+
+
+class _TwoCoefficientLayer(nn.Module):
+    """Layout/causal handling of the reference base layer (pde_layers.py:71-188)
+    for the layers with an extra ``beta`` term."""
+
+    KIND = -1
+
+    def __init__(self, hidden_size: int, alpha_init: float, beta_init: float, layout: str = "bdl",
+                 causal: bool = False):
+        super().__init__()
+        if layout not in {"bdl", "bld"}:
+            raise ValueError("layout must be 'bdl' or 'bld'")
+        self.layout = layout
+        self.causal = causal
+        self.alpha = nn.Parameter(torch.tensor([alpha_init]))
+        self.beta = nn.Parameter(torch.tensor([beta_init]))
+
+    def forward(self, x: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One refinement step (src/models/pde_layers.py:113-188)."""
+        seq_dim = 2 if self.layout == "bdl" else 1
+        if x.size(seq_dim) < 3:
+            return x
+        if x.device.type != "cuda":
+            raise ValueError("x must be on CUDA")
+        mask = attention_mask
+        if mask is not None:
+            if mask.device != x.device:
+                mask = mask.to(x.device)
+            if mask.dtype == torch.bool:
+                mask = mask.to(torch.uint8)
+        xb = x.transpose(1, 2) if self.layout == "bdl" else x
+        y = _PDEStep.apply(xb.contiguous(), mask, self.KIND, bool(self.causal), self.alpha, self.beta)
+        return y.transpose(1, 2) if self.layout == "bdl" else y
+
+
+class ReactionDiffusionPDELayer(_TwoCoefficientLayer):
+    """Reaction-diffusion ``du/dt = alpha*lap + beta*u*(1 - sigmoid(u))``
+    (src/models/pde_layers.py:249-281)."""
+
+    KIND = _lib.PDE_REACTION
+
+    def __init__(self, hidden_size: int, alpha_init: float = 0.10, beta_init: float = 0.02, layout: str = "bdl",
+                 causal: bool = False):
+        super().__init__(hidden_size, alpha_init, beta_init, layout=layout, causal=causal)
+
+
+class AdvectionDiffusionPDELayer(_TwoCoefficientLayer):
+    """Advection-diffusion ``du/dt = alpha*lap + beta*du/dx`` with a central
+    (causal: backward) difference (src/models/pde_layers.py:284-318)."""
+
+    KIND = _lib.PDE_ADVECTION
+
+    def __init__(self, hidden_size: int, alpha_init: float = 0.10, beta_init: float = 0.03, layout: str = "bdl",
+                 causal: bool = False):
+        super().__init__(hidden_size, alpha_init, beta_init, layout=layout, causal=causal)
+
+
 _PDE_REGISTRY = {
     "diffusion": DiffusionPDELayer,
     "wave": WavePDELayer,
+    "reaction-diffusion": ReactionDiffusionPDELayer,
+    "advection-diffusion": AdvectionDiffusionPDELayer,
 }
-_NOT_SERVED = ("reaction-diffusion", "advection-diffusion")
 
 
 def create_pde_layer(pde_type: str, hidden_size: int, causal: bool = False, **kwargs) -> nn.Module:
     """Factory with the reference's signature (src/models/pde_layers.py:333-357)."""
-    if pde_type in _NOT_SERVED:
-        raise NotImplementedError(f"PDE type {pde_type!r} has no fused kernel in this build")
     if pde_type not in _PDE_REGISTRY:
-        raise ValueError(
-            f"Unknown PDE type: {pde_type}. Available types: {list(_PDE_REGISTRY.keys()) + list(_NOT_SERVED)}"
-        )
+        raise ValueError(f"Unknown PDE type: {pde_type}. Available types: {list(_PDE_REGISTRY.keys())}")
     kwargs["causal"] = causal
     return _PDE_REGISTRY[pde_type](hidden_size, **kwargs)
 

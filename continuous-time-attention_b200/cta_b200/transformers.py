@@ -14,7 +14,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from .pde_layers import create_pde_layer, diffusion_pde_stack
+from .pde_layers import _DiffusionFamilyLayer, create_pde_layer, diffusion_pde_stack
 
 __all__ = ["generate_causal_mask", "PDETransformerClassifier", "PDETransformerLM"]
 
@@ -25,6 +25,12 @@ def generate_causal_mask(seq_len: int, device: torch.device) -> torch.Tensor:
 
 
 def _refine(x: torch.Tensor, pde_list: nn.ModuleList, layout: str, attention_mask: torch.Tensor) -> torch.Tensor:
+    if not all(isinstance(l, _DiffusionFamilyLayer) for l in pde_list):
+        # advection / reaction layers: one step per layer, as the reference loops
+        x_t = x.transpose(1, 2).contiguous() if layout == "bdl" else x
+        for layer in pde_list:
+            x_t = layer(x_t, attention_mask=attention_mask)
+        return x_t.transpose(1, 2).contiguous() if layout == "bdl" else x_t
     if layout == "bdl":
         x_t = x.transpose(1, 2).contiguous()
         x_t = diffusion_pde_stack(x_t, pde_list, attention_mask=attention_mask)

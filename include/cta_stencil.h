@@ -39,6 +39,7 @@ enum { CTA_F32 = 0, CTA_BF16 = 1, CTA_F16 = 2 };
 enum { CTA_MASK_U8 = 0, CTA_MASK_I32 = 1, CTA_MASK_I64 = 2, CTA_MASK_F32 = 3, CTA_MASK_BF16 = 4, CTA_MASK_F16 = 5 };
 enum { CTA_OK = 0, CTA_EINVAL = 1, CTA_EUNSUPPORTED = 2, CTA_ECUDA = 3 };
 enum { CTA_SHARD_INTERIOR = 0, CTA_SHARD_LO_EDGE = 1, CTA_SHARD_HI_EDGE = 2 };
+enum { CTA_PDE_ADVECTION = 0, CTA_PDE_REACTION = 1 };
 
 /* ABI version of the loaded library (CTA_ABI_VERSION). */
 int cta_abi_version(void);
@@ -53,7 +54,8 @@ int cta_device_error(int clear);
 
 /* Benchmark tuning hook: key 0 = target CTAs per SM used to size the [B, L, D]
  * backward tiles (default 6), key 1 = forced tile rows (0 = automatic), key 2 =
- * target CTAs per SM of the [B, L, D] forward (default 16).  Returns the
+ * target CTAs per SM of the [B, L, D] forward (default 16), key 3 = launch
+ * the [B, L, D] march kernels with programmatic dependent launch (default 0).  Returns the
  * previous value.  Process-wide, not thread-safe against concurrent launches. */
 int cta_set_tuning(int key, int value);
 
@@ -168,6 +170,23 @@ int cta_diffusion_fwd_bld_residual(const void* x, const void* residual, void* y,
                                    int64_t x_sB, int64_t x_sL, int64_t r_sB, int64_t r_sL, int64_t y_sB,
                                    int64_t y_sL, int dtype, int steps, const float* alpha, const void* mask,
                                    int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream);
+
+/* One step of the reaction-diffusion or advection-diffusion PDE layer on
+ * [B, L, D] (src/models/pde_layers.py:249-318 with the forward of :113-188):
+ *   y = x + (alpha * lap(x) + beta-term) on updated rows, x on fixed rows;
+ *   kind CTA_PDE_ADVECTION: beta * (x[i+1] - x[i-1]) / 2 (causal: beta * (x[i] - x[i-1]));
+ *   kind CTA_PDE_REACTION: (beta * x[i]) * (1 - sigmoid(x[i])).
+ * alpha_dev / beta_dev are device scalars (the layer parameters, coef_dtype).
+ * backward = 0: x -> y (grad_out, dcoef, workspace unused).
+ * backward = 1: y = dx for grad_out and the forward input x, dcoef = fp32
+ * [d(alpha), d(beta)] (reduced deterministically, two launches); workspace of
+ * cta_pde_step_workspace_bytes(B, L, D) bytes, 16-byte aligned, no zeroing. */
+int64_t cta_pde_step_workspace_bytes(int64_t B, int64_t L, int64_t D);
+int cta_pde_step_bld(const void* x, const void* grad_out, void* y, float* dcoef, void* workspace,
+                     int64_t workspace_bytes, int64_t B, int64_t L, int64_t D, int64_t x_sB, int64_t x_sL,
+                     int64_t g_sB, int64_t g_sL, int64_t y_sB, int64_t y_sL, int dtype, int kind, int causal,
+                     int backward, const void* alpha_dev, const void* beta_dev, int coef_dtype, const void* mask,
+                     int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream);
 
 /* One shard of an L-sharded sequence ([B, L_local, D], contiguous): rows
  * [pos_offset, pos_offset + L_local) of a sequence of global_len rows.

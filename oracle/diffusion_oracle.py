@@ -131,6 +131,51 @@ def layer_step(
     return y if keep_fp32 else y.to(dtype=x.dtype)
 
 
+def pde_layer_step(
+    x: torch.Tensor,
+    kind: str,
+    alpha: Alpha,
+    beta: Alpha,
+    *,
+    layout: str = "bdl",
+    causal: bool = False,
+    attention_mask: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """One AdvectionDiffusionPDELayer (kind "advection") or ReactionDiffusionPDELayer
+    (kind "reaction") step: the base forward of src/models/pde_layers.py:113-188 with
+    the updates of :309-318 and :276-281."""
+    seq_dim = 2 if layout == "bdl" else 1
+    if x.size(seq_dim) < 3:
+        return x
+    u = x.to(dtype=torch.float32)
+    if layout == "bld":
+        u = u.transpose(1, 2)
+    lap = u[:, :, 2:] - 2.0 * u[:, :, 1:-1] + u[:, :, :-2]
+    a, b = _alpha_f32(alpha), _alpha_f32(beta)
+    interior = u[:, :, 2:] if causal else u[:, :, 1:-1]
+    diffusion = a * lap
+    if kind == "advection":
+        gradient = (u[:, :, 2:] - u[:, :, 1:-1]) if causal else (u[:, :, 2:] - u[:, :, :-2]) / 2.0
+        dx = diffusion + b * gradient
+    elif kind == "reaction":
+        dx = diffusion + b * interior * (1.0 - torch.sigmoid(interior))
+    else:
+        raise ValueError(f"unknown kind {kind!r}")
+    upd = interior + dx
+    if attention_mask is not None:
+        upd = torch.where(_valid3(attention_mask, upd.size(2)), upd, interior)
+    if causal:
+        y = torch.cat([u[:, :, :2], upd], dim=2)
+    else:
+        y = torch.cat([u[:, :, :1], upd, u[:, :, -1:]], dim=2)
+    if attention_mask is not None:
+        m = attention_mask.bool().to(dtype=y.dtype).unsqueeze(1)
+        y = y * m + u * (1 - m)
+    if layout == "bld":
+        y = y.transpose(1, 2)
+    return y.to(dtype=x.dtype)
+
+
 def layer_chain(
     x: torch.Tensor,
     alphas: Sequence[Alpha],

@@ -39,7 +39,7 @@ def main() -> None:
     sys.path.insert(0, str(ref))
     from cta.ops.diffusion import diffusion_step_reference, diffusion_steps_reference
     from cta.serving_vllm import CtaConfig, CtaPostAttnMixer, _diffusion_steps_bld
-    from models.pde_layers import DiffusionPDELayer
+    from models.pde_layers import AdvectionDiffusionPDELayer, DiffusionPDELayer, ReactionDiffusionPDELayer
 
     torch.set_num_threads(1)
     G: dict = {"meta": {"generator": "tests/golden/make_golden.py", "torch": torch.__version__}}
@@ -104,6 +104,35 @@ def main() -> None:
                         "dalpha": torch.cat([l.alpha.grad.detach() for l in layers]),
                     })
     G["layer_chain"] = cases
+
+    # 4b. the advection- and reaction-diffusion layers: one layer, with gradients
+    cases = []
+    for kind, cls in (("advection", AdvectionDiffusionPDELayer), ("reaction", ReactionDiffusionPDELayer)):
+        for layout in ("bld", "bdl"):
+            for causal in (False, True):
+                for use_mask in (False, True):
+                    for dtype in (torch.float32, torch.bfloat16):
+                        torch.manual_seed(5)
+                        B, L, D = 2, 23, 6
+                        x = torch.randn(B, L, D) if layout == "bld" else torch.randn(B, D, L)
+                        x = (2.0 * x).to(dtype)
+                        mask = None
+                        if use_mask:
+                            mask = torch.ones(B, L, dtype=torch.long)
+                            mask[0, 17:] = 0
+                            mask[1, 5] = 0
+                        layer = cls(D, alpha_init=0.12, beta_init=0.07, layout=layout, causal=causal)
+                        xr = x.clone().requires_grad_(True)
+                        y = layer(xr, attention_mask=mask)
+                        torch.manual_seed(6)
+                        g = torch.randn(y.shape).to(dtype)
+                        (y.float() * g.float()).sum().backward()
+                        cases.append({
+                            "kind": kind, "layout": layout, "causal": causal, "mask": mask, "x": x, "alpha": 0.12,
+                            "beta": 0.07, "g": g, "y": y.detach(), "dx": xr.grad.detach(),
+                            "dalpha": layer.alpha.grad.detach().clone(), "dbeta": layer.beta.grad.detach().clone(),
+                        })
+    G["pde_step"] = cases
 
     # 5. packed prefill through the reference mixer's torch path
     cases = []

@@ -74,8 +74,14 @@ def test_python_errors_without_gpu():
         DiffusionPDELayer(4, layout="lbd")
     with pytest.raises(ValueError):
         create_pde_layer("heat", 4)
-    with pytest.raises(NotImplementedError):
-        create_pde_layer("reaction-diffusion", 4)
+    # the reference's four types, its parameter names and defaults (pde_layers.py:195-318)
+    rd = create_pde_layer("reaction-diffusion", 4, causal=True, layout="bld")
+    ad = create_pde_layer("advection-diffusion", 4)
+    assert sorted(n for n, _ in rd.named_parameters()) == ["alpha", "beta"] and rd.causal and rd.layout == "bld"
+    assert abs(rd.beta.item() - 0.02) < 1e-7 and abs(ad.beta.item() - 0.03) < 1e-7 and ad.layout == "bdl"
+    assert rd(torch.randn(1, 2, 4)).shape == (1, 2, 4)  # L < 3 identity before any device work
+    with pytest.raises(ValueError):
+        ad(torch.randn(1, 4, 10))  # no CPU path
     layer = DiffusionPDELayer(4, layout="bdl")
     short = torch.randn(1, 4, 2)
     assert layer(short) is short  # pde_layers.py:130-131

@@ -164,3 +164,109 @@ def test_mixer_packed_sequence_rule():
     md = SimpleNamespace(max_query_len=59, query_start_loc=qsl, num_prefill_tokens=100)
     y = mixer(x.cuda(), attn_metadata=md)
     assert torch.equal(y.cpu(), O.varlen_per_sequence(x, qsl, alpha=0.1, steps=4))
+
+
+# ---------------------------------------------------------------------------
+# advection- and reaction-diffusion layers (one kernel launch per step)
+# ---------------------------------------------------------------------------
+def _two_coef_layer(kind, D, layout, causal, alpha=0.12, beta=0.07):
+    from cta_b200.pde_layers import AdvectionDiffusionPDELayer, ReactionDiffusionPDELayer
+
+    cls = AdvectionDiffusionPDELayer if kind == "advection" else ReactionDiffusionPDELayer
+    return cls(D, alpha_init=alpha, beta_init=beta, layout=layout, causal=causal).cuda()
+
+
+def test_pde_step_layers_match_reference_golden(golden):
+    """The reference's own layer outputs: advection bit for bit, reaction (its
+    sigmoid is CUDA's expf here) to the fp32 / bf16 bar; gradients within tolerance."""
+    for c in golden["pde_step"]:
+        D = c["x"].shape[2] if c["layout"] == "bld" else c["x"].shape[1]
+        layer = _two_coef_layer(c["kind"], D, c["layout"], c["causal"], c["alpha"], c["beta"])
+        x = c["x"].cuda().requires_grad_(True)
+        mask = None if c["mask"] is None else c["mask"].cuda()
+        y = layer(x, attention_mask=mask)
+        tag = (c["kind"], c["layout"], c["causal"], c["mask"] is not None, c["x"].dtype)
+        if c["kind"] == "advection":
+            assert torch.equal(y.detach().cpu(), c["y"]), tag
+        else:
+            assert_close(y, c["y"])
+        (y.float() * c["g"].cuda().float()).sum().backward()
+        assert_close(x.grad, c["dx"])
+        scale = max(1.0, c["dalpha"].abs().max().item(), c["dbeta"].abs().max().item())
+        assert (layer.alpha.grad.cpu() - c["dalpha"]).abs().max().item() <= 1e-4 * scale, tag
+        assert (layer.beta.grad.cpu() - c["dbeta"]).abs().max().item() <= 1e-4 * scale, tag
+
+
+@pytest.mark.parametrize("kind", ["advection", "reaction"])
+@pytest.mark.parametrize("layout", ["bld", "bdl"])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", [(2, 1000, 512), (1, 77, 513), (3, 40, 6)])
+def test_pde_step_layers_match_oracle(kind, layout, causal, shape):
+    torch.manual_seed(13)
+    B, L, D = shape
+    for dtype in (torch.float32, torch.bfloat16):
+        x = (2.0 * torch.randn(B, L, D)).to(dtype)
+        if layout == "bdl":
+            x = x.transpose(1, 2).contiguous()
+        mask = torch.ones(B, L, dtype=torch.long)
+        mask[-1, L - L // 4 :] = 0
+        g = torch.randn(x.shape).to(dtype)
+        layer = _two_coef_layer(kind, D, layout, causal)
+        xg = x.cuda().requires_grad_(True)
+        y = layer(xg, attention_mask=mask.cuda())
+        kw = dict(layout=layout, causal=causal, attention_mask=mask)
+        ref = O.pde_layer_step(x, kind, 0.12, 0.07, **kw)
+        if kind == "advection":
+            assert torch.equal(y.detach().cpu(), ref), (shape, dtype)
+        else:
+            assert_close(y, ref)
+        (y.float() * g.cuda().float()).sum().backward()
+        dx_ref, (da, db) = O.grads(lambda t, a, b: O.pde_layer_step(t, kind, a, b, **kw), x.float(), g.float(),
+                                   [torch.tensor([0.12]), torch.tensor([0.07])])
+        assert_close(xg.grad, dx_ref)
+        scale = max(1.0, da.abs().max().item(), db.abs().max().item())
+        rel = 1e-4 if dtype == torch.float32 else 2e-2
+        assert (layer.alpha.grad.cpu() - da).abs().max().item() <= rel * scale, (shape, dtype, layer.alpha.grad, da)
+        assert (layer.beta.grad.cpu() - db).abs().max().item() <= rel * scale, (shape, dtype, layer.beta.grad, db)
+
+
+@pytest.mark.parametrize("pde_type", ["advection-diffusion", "reaction-diffusion"])
+def test_pde_transformer_other_pde_types(pde_type):
+    """PDETransformerLM / Classifier with the other two PDE types: the refinement
+    runs layer by layer on the kernels and matches the oracle's layers."""
+    from cta_b200 import transformers as T
+
+    torch.manual_seed(3)
+    kw = dict(vocab_size=101, embed_dim=32, num_heads=4, hidden_dim=64, num_layers=2, pde_steps=2,
+              max_length=64, dropout=0.0, pde_type=pde_type)
+    kind = pde_type.split("-")[0]
+    for model in ("classifier", "lm"):
+        net = (T.PDETransformerClassifier(num_classes=3, **kw) if model == "classifier" else T.PDETransformerLM(**kw))
+        net = net.cuda().eval()
+        ids = torch.randint(0, 101, (2, 50), device="cuda")
+        mask = torch.ones(2, 50, dtype=torch.long, device="cuda")
+        mask[1, 41:] = 0
+        out = net(ids, mask)
+        causal = model == "lm"
+        with torch.no_grad():
+            x = net.embedding(ids) + net.pos_encoder[:, :50, :]
+            if causal:
+                pad = torch.zeros_like(mask, dtype=torch.float32).masked_fill(mask == 0, float("-inf"))
+                cm = T.generate_causal_mask(50, x.device)
+            for tl, plist in zip(net.transformer_layers, net.pde_layers):
+                x = tl(x, src_mask=cm, src_key_padding_mask=pad) if causal else tl(x, src_key_padding_mask=mask == 0)
+                xc = x.cpu()
+                for p in plist:
+                    xc = O.pde_layer_step(xc, kind, p.alpha.detach().cpu(), p.beta.detach().cpu(), layout="bld",
+                                          causal=causal, attention_mask=mask.cpu())
+                x = xc.cuda()
+            if causal:
+                ref = net.fc(x)
+            else:
+                em = mask.unsqueeze(-1).expand(x.size())
+                ref = net.fc(torch.sum(x * em, 1) / torch.clamp(mask.sum(1, keepdim=True), min=1))
+        torch.testing.assert_close(out.detach(), ref, rtol=1e-4, atol=1e-4)
+        out.float().sum().backward()
+        for plist in net.pde_layers:
+            for p in plist:
+                assert torch.isfinite(p.alpha.grad).all() and torch.isfinite(p.beta.grad).all()

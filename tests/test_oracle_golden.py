@@ -112,3 +112,18 @@ def test_window_grads_oracle_matches_full(causal):
         das += da
     torch.testing.assert_close(torch.cat(dxs, 1), dx_ref, rtol=1e-6, atol=1e-6)
     torch.testing.assert_close(das.float(), da_ref, rtol=1e-5, atol=1e-5)
+
+
+def test_pde_layer_step_matches_reference(golden):
+    """Advection- and reaction-diffusion layers: forward bit for bit, gradients
+    (dx, d(alpha), d(beta)) to 1e-6, against the reference's own layers."""
+    for c in golden["pde_step"]:
+        kw = dict(layout=c["layout"], causal=c["causal"], attention_mask=c["mask"])
+        y = O.pde_layer_step(c["x"], c["kind"], c["alpha"], c["beta"], **kw)
+        assert torch.equal(y, c["y"]), (c["kind"], c["layout"], c["causal"], c["x"].dtype)
+        dx, (da, db) = O.grads(lambda t, a, b: O.pde_layer_step(t, c["kind"], a, b, **kw), c["x"], c["g"],
+                               [torch.tensor([c["alpha"]]), torch.tensor([c["beta"]])])
+        tol = 1e-6 if c["x"].dtype == torch.float32 else 1e-2
+        torch.testing.assert_close(dx.float(), c["dx"].float(), rtol=tol, atol=tol)
+        torch.testing.assert_close(da, c["dalpha"], rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(db, c["dbeta"], rtol=1e-5, atol=1e-5)
