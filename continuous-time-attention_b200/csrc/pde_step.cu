@@ -108,7 +108,8 @@ __device__ __forceinline__ bool pde_row_fixed(const PdeArgs& a, int b, int64_t i
   return false;
 }
 
-__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
+// 1 / (1 + e^-v) with the fast exponential and a correctly rounded reciprocal
+__device__ __forceinline__ float sigmoid_f(float v) { return __frcp_rn(__fadd_rn(1.0f, __expf(-v))); }
 
 // the stencil terms of row i from its three rows: (lo, mid, hi) = (x[i-1], x[i], x[i+1])
 // non-causal or (x[i-2], x[i-1], x[i]) causal.  lap, h as in the file comment,
