@@ -569,9 +569,9 @@ def run_kernels(args, rank, world, local_rank):
 
     coef = torch.tensor([0.1], device=dev)
     for name, kind in (("pde_advection", lib_.PDE_ADVECTION), ("pde_reaction", lib_.PDE_REACTION)):
-        timed(name + "_forward", 1, lambda i, kind=kind: ops.pde_step(xs[i % nb], kind, coef, coef), 2)
+        timed(name + "_forward", 1, lambda i, kind=kind: ops.pde_step(xs[i % nb], kind, coef, coef, out=ys[i % nb]), 2)
         timed(name + "_backward", 1,
-              lambda i, kind=kind: ops.pde_step(xs[i % nb], kind, coef, coef, grad_out=gs[i % nb]), 3)
+              lambda i, kind=kind: ops.pde_step(xs[i % nb], kind, coef, coef, grad_out=gs[i % nb], out=ys[i % nb]), 3)
     for S in (1, 4):
         timed("bld_adjoint_dalpha", S,
               lambda i, S=S: ops.bld_backward(gs[i % nb], [0.1] * S, S, x=xs[i % nb], need_dalpha=True,

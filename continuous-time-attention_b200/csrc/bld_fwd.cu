@@ -79,15 +79,47 @@ constexpr int march_min_ctas() {
   return S <= 3 ? (kFwdMinCtas < 16 ? kFwdMinCtas : 16) : S <= 5 ? 12 : 8;
 }
 
+// The per-pair update of one level.  KIND 0: the diffusion step (pst_c /
+// pst_nc).  KIND 1 / 2 (steps 1 only): the advection- / reaction-diffusion
+// layer step of src/models/pde_layers.py:276-281, :309-318 in the reference's
+// op order: c + (alpha*lap + beta-term), beta-term = beta * (x[i+1] - x[i-1]) / 2
+// (causal beta * (x[i] - x[i-1])) or (beta * c) * (1 - sigmoid(c)).
+// (p2, p1, x) = rows (i-1, i, i+1) non-causal, (i-2, i-1, i) causal.
+__device__ __forceinline__ float fast_sigmoid(float v) { return __frcp_rn(__fadd_rn(1.0f, __expf(-v))); }
+
+template <int KIND, bool CAUSAL>
+__device__ __forceinline__ pf2 level_update(pf2 p2, pf2 p1, pf2 x, pf2 al, pf2 be, float be_s, pf2 m2, pf2 zn) {
+  if constexpr (KIND == 0) {
+    return CAUSAL ? pst_c(p2, p1, x, al, m2, zn) : pst_nc(p2, p1, x, al, m2, zn);
+  } else {
+    const pf2 lap = plap(p2, p1, x, m2);
+    const pf2 c = CAUSAL ? x : p1;
+    pf2 bterm;
+    if constexpr (KIND == 1) {
+      const pf2 n1 = pbc(-1.f), half = pbc(0.5f);
+      const pf2 h = CAUSAL ? pfma(p1, n1, x) : pmul(pfma(p2, n1, x), half);  // x[i]-x[i-1] | (x[i+1]-x[i-1])/2
+      bterm = pmul_sep(be, h, zn);
+    } else {
+      float c0, c1;
+      upk(c, c0, c1);
+      const float t0 = __fmul_rn(__fmul_rn(be_s, c0), __fsub_rn(1.0f, fast_sigmoid(c0)));
+      const float t1 = __fmul_rn(__fmul_rn(be_s, c1), __fsub_rn(1.0f, fast_sigmoid(c1)));
+      bterm = pk(t0, t1);
+    }
+    return padd(c, padd(pmul_sep(al, lap, zn), bterm));
+  }
+}
+
 // RES (non-causal forward only): y = residual + stencil(x) in the same pass.
 // The residual rows of each full output chunk are brought by a TMA load into
 // the staging slot that chunk is about to use, issued one chunk ahead; the
 // lanes add them in place and the TMA store sends the sum out.
-template <typename T, int S, bool CAUSAL, bool ADJ, bool RES>
+template <typename T, int S, bool CAUSAL, bool ADJ, bool RES, int KIND = 0>
 __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ, RES>()))
     bld_march_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                      const __grid_constant__ CUtensorMap rmap, const BldArgs a) {
   static_assert(!RES || (!ADJ && !CAUSAL), "the residual form is the non-causal forward");
+  static_assert(KIND == 0 || (S == 1 && !ADJ && !RES), "the other PDE kinds are single forward steps");
   // every global read (cu_seqlens, mask, alphas, the streams) comes after the wait
   pdl_launch_dependents();
   pdl_wait();
@@ -169,6 +201,11 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   for (int k = 0; k < S; ++k) al[k] = pbc(alf[k]);
   const pf2 m2 = pbc(-2.f);
   const pf2 zn = pbc(a.neg_zero);
+  // KIND 1/2: beta in coefficient slot 1
+  const float be_s = KIND == 0 ? 0.f
+                               : (a.alpha_dev[1] != nullptr ? load_scalar(a.alpha_dev[1], a.alpha_dev_dtype)
+                                                            : a.alpha[1]);
+  const pf2 be = pbc(be_s);
 
   // per-level state, for both pairs.  Forward: the level's input on the two
   // previous march rows (P1, P2).  Adjoint: a = alpha*g on the two previous
@@ -266,8 +303,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       for (int k = 0; k < S; ++k) {
         pf2 na = xa, nb = xb;
         if (TCT < 0 || TCT >= 2 * k + 2) {
-          na = pst_c(P2a[k], P1a[k], xa, al[k], m2, zn);
-          nb = pst_c(P2b[k], P1b[k], xb, al[k], m2, zn);
+          na = level_update<KIND, true>(P2a[k], P1a[k], xa, al[k], be, be_s, m2, zn);
+          nb = level_update<KIND, true>(P2b[k], P1b[k], xb, al[k], be, be_s, m2, zn);
           if (SLOW) {
             na = psel(fx, xa, na);
             nb = psel(fx, xb, nb);
@@ -287,8 +324,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       for (int k = 0; k < S; ++k) {
         pf2 na = xa, nb = xb;
         if (TCT < 0 || TCT >= 2 * k + 2) {
-          na = pst_nc(P2a[k], P1a[k], xa, al[k], m2, zn);
-          nb = pst_nc(P2b[k], P1b[k], xb, al[k], m2, zn);
+          na = level_update<KIND, false>(P2a[k], P1a[k], xa, al[k], be, be_s, m2, zn);
+          nb = level_update<KIND, false>(P2b[k], P1b[k], xb, al[k], be, be_s, m2, zn);
           if (SLOW) {
             const bool fx = (fw >> (S - 1 - k)) & 1u;
             na = psel(fx, P1a[k], na);
@@ -433,18 +470,29 @@ const void* march_ptr(int steps) {
   }
 }
 
+template <typename T, int KIND>
+const void* march_ptr_kind(int steps, int causal) {
+  if (steps != 1) return nullptr;
+  return causal ? reinterpret_cast<const void*>(bld_march_kernel<T, 1, true, false, false, KIND>)
+                : reinterpret_cast<const void*>(bld_march_kernel<T, 1, false, false, false, KIND>);
+}
+
 template <typename T>
-const void* march_ptr_t(int steps, int causal, int adj, int res) {
+const void* march_ptr_t(int steps, int causal, int adj, int res, int kind) {
+  if (kind != 0) {
+    if (adj || res) return nullptr;
+    return kind == 1 ? march_ptr_kind<T, 1>(steps, causal) : kind == 2 ? march_ptr_kind<T, 2>(steps, causal) : nullptr;
+  }
   if (res) return (causal || adj) ? nullptr : march_ptr<T, false, false, true>(steps);
   if (adj) return causal ? march_ptr<T, true, true, false>(steps) : march_ptr<T, false, true, false>(steps);
   return causal ? march_ptr<T, true, false, false>(steps) : march_ptr<T, false, false, false>(steps);
 }
 
-const void* march_kernel(int dtype, int steps, int causal, int adj, int res) {
+const void* march_kernel(int dtype, int steps, int causal, int adj, int res, int kind = 0) {
   switch (dtype) {
-    case kF32: return march_ptr_t<float>(steps, causal, adj, res);
-    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, adj, res);
-    case kF16: return march_ptr_t<__half>(steps, causal, adj, res);
+    case kF32: return march_ptr_t<float>(steps, causal, adj, res, kind);
+    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, adj, res, kind);
+    case kF16: return march_ptr_t<__half>(steps, causal, adj, res, kind);
     default: return nullptr;
   }
 }
@@ -454,7 +502,7 @@ const void* march_kernel(int dtype, int steps, int causal, int adj, int res) {
 cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap,
                            const CUtensorMap* rmap, int dtype, int steps, int causal, int adjoint, dim3 grid,
                            size_t smem, cudaStream_t st) {
-  const void* kern = march_kernel(dtype, steps, causal, adjoint, a.residual != nullptr ? 1 : 0);
+  const void* kern = march_kernel(dtype, steps, causal, adjoint, a.residual != nullptr ? 1 : 0, a.pde_kind);
   if (kern == nullptr) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem_attr(kern, smem);
   if (e != cudaSuccess) return e;

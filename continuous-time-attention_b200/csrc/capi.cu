@@ -837,8 +837,40 @@ int cta_pde_step_bld(const void* x, const void* grad_out, void* y, float* dcoef,
     }
     return ok();
   }
-  const cudaError_t e = launch_pde_step(p, dtype, kind, causal ? 1 : 0, backward ? 1 : 0,
-                                        static_cast<cudaStream_t>(stream));
+  if (!backward) {
+    // forward: the one-warp TMA march kernel at steps 1 with the layer's update
+    BldArgs m = blank_bld();
+    m.x = x;
+    m.y = y;
+    m.xsB = x_sB;
+    m.xsL = x_sL;
+    m.ysB = y_sB;
+    m.ysL = y_sL;
+    m.L = L;
+    m.D = static_cast<int>(D);
+    m.nbatch = static_cast<int>(B);
+    m.global_len = L;
+    m.mask = mask;
+    m.mask_dtype = mask_dtype;
+    m.msB = mask_sB;
+    m.msL = mask_sL;
+    m.alpha_dev[0] = alpha_dev;
+    m.alpha_dev[1] = beta_dev;
+    m.alpha_dev_dtype = coef_dtype;
+    m.pde_kind = kind == CTA_PDE_ADVECTION ? 1 : 2;
+    const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
+    m.TL = pick_tl(L, ndt * B, 1, march_per_sm(dtype, 1, causal ? 1 : 0, 0));
+    m.out_begin = 0;
+    m.out_end = L;
+    m.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
+    CUtensorMap xmap, ymap;
+    std::memset(&xmap, 0, sizeof(xmap));
+    std::memset(&ymap, 0, sizeof(ymap));
+    m.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
+    m.use_tma_store = make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
+    return launch_fwd(m, dtype, 1, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), xmap, ymap);
+  }
+  const cudaError_t e = launch_pde_step(p, dtype, kind, causal ? 1 : 0, 1, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "pde step launch");
   return ok();
 }

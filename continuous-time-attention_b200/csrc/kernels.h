@@ -94,6 +94,9 @@ struct BldArgs {
   // with element strides (rsB, rsL), added as an elementwise add of type T
   const void* residual;
   int64_t rsB, rsL;
+  // 0: diffusion.  1 / 2: advection- / reaction-diffusion layer step (steps 1,
+  // beta in coefficient slot 1)
+  int pde_kind;
   // L-shard halos of the gradient stream for the d(alpha) kernel (lo_ext/hi_ext
   // above hold the x stream's): [nbatch, g_hext_lo|hi, D]
   const void* g_lo_ext;

@@ -1,5 +1,6 @@
 // One step of the non-diffusion PDE layers on [B, L, D] hidden states
-// (src/models/pde_layers.py:249-318), forward and backward:
+// (src/models/pde_layers.py:249-318).  The forward runs on the march kernel
+// (bld_fwd.cu, level_update KIND 1/2); this file holds the backward:
 //
 //   y[i] = x[i] + (alpha * lap[i] + beta * h[i])    on updated rows, x[i] on fixed rows
 //   lap[i] = (x[i+1] - 2 x[i]) + x[i-1]              (causal: (x[i] - 2 x[i-1]) + x[i-2])
@@ -136,41 +137,6 @@ __device__ __forceinline__ void terms(float lo, float mid, float hi, float al, f
 }  // namespace
 
 template <typename T, int KIND, bool CAUSAL>
-__global__ void __launch_bounds__(kPdeThreads) pde_step_fwd_kernel(const PdeArgs a) {
-  const int b = blockIdx.z;
-  const int col = (blockIdx.y * kPdeThreads + threadIdx.x) * kPdeVec;
-  if (col >= a.D) return;
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kPdeRows;
-  const int64_t r1 = r0 + kPdeRows < a.L ? r0 + kPdeRows : a.L;
-  const bool vx = a.x_vec && col + kPdeVec <= a.D;
-  const bool vy = a.y_vec && col + kPdeVec <= a.D;
-  const float al = load_scalar(a.alpha_dev, a.coef_dtype);
-  const float be = load_scalar(a.beta_dev, a.coef_dtype);
-  const T* X = static_cast<const T*>(a.x);
-  T* Y = static_cast<T*>(a.y);
-  // window: w0, w1 = the two rows before the one being read
-  F4 w0 = load4<T>(a, X, a.xsB, a.xsL, b, CAUSAL ? r0 - 2 : r0 - 1, col, vx);
-  F4 w1 = load4<T>(a, X, a.xsB, a.xsL, b, CAUSAL ? r0 - 1 : r0, col, vx);
-#pragma unroll 4
-  for (int64_t i = r0; i < r1; ++i) {
-    const F4 w2 = load4<T>(a, X, a.xsB, a.xsL, b, CAUSAL ? i : i + 1, col, vx);
-    const bool fixed = pde_row_fixed<CAUSAL>(a, b, i);
-    F4 out;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float c = CAUSAL ? w2.v[j] : w1.v[j];
-      float lap, h, dx;
-      terms<KIND, CAUSAL>(w0.v[j], w1.v[j], w2.v[j], al, be, lap, h, dx);
-      // pde_layers.py:145-146 / :160-161: interior + (alpha*lap + beta-term)
-      out.v[j] = fixed ? c : __fadd_rn(c, dx);
-    }
-    store4<T>(a, Y, a.ysB, a.ysL, b, i, col, vy, out);
-    w0 = w1;
-    w1 = w2;
-  }
-}
-
-template <typename T, int KIND, bool CAUSAL>
 __global__ void __launch_bounds__(kPdeThreads) pde_step_bwd_kernel(const PdeArgs a) {
   __shared__ float red[kPdeThreads / 32][2];
   const int b = blockIdx.z;
@@ -291,11 +257,7 @@ dim3 pde_grid(const PdeArgs& a) {
 template <typename T, int KIND>
 cudaError_t launch_t(const PdeArgs& a, int causal, int backward, cudaStream_t st) {
   const dim3 grid = pde_grid(a);
-  if (!backward) {
-    if (causal) pde_step_fwd_kernel<T, KIND, true><<<grid, kPdeThreads, 0, st>>>(a);
-    else pde_step_fwd_kernel<T, KIND, false><<<grid, kPdeThreads, 0, st>>>(a);
-    return cudaGetLastError();
-  }
+  if (!backward) return cudaErrorInvalidValue;  // the forward runs on the march kernel
   if (causal) pde_step_bwd_kernel<T, KIND, true><<<grid, kPdeThreads, 0, st>>>(a);
   else pde_step_bwd_kernel<T, KIND, false><<<grid, kPdeThreads, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();

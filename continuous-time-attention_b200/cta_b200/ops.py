@@ -385,6 +385,7 @@ def pde_step(
     causal: bool = False,
     mask: Optional[torch.Tensor] = None,
     grad_out: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
 ):
     """One advection- / reaction-diffusion step on [B, L, D] (kind _lib.PDE_*).
 
@@ -409,7 +410,7 @@ def pde_step(
     m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
     lib = _lib.load()
     code = _lib.dtype_code(x.dtype)
-    y = torch.empty((B, L, D), dtype=x.dtype, device=x.device)
+    y = _out(out, (B, L, D), x)
     g = None
     dcoef = ws = None
     ws_bytes = 0
