@@ -108,10 +108,34 @@ constexpr int da_min_ctas() {
   return S <= 2 ? 16 : (S == 3 && !(CAUSAL && sizeof(T) == 4)) ? 12 : 8;
 }
 
-template <typename T, int S, bool CAUSAL>
+// KIND 1 / 2 (steps 1 only): the backward of one advection- / reaction-
+// diffusion layer step (src/models/pde_layers.py:276-281, :309-318), with q the
+// output gradient on updated rows (0 on fixed rows) and h the layer's beta term:
+//   dx[i] += beta * (q[i-1] - q[i+1]) / 2  (causal beta * (q[i] - q[i+1]))      advection
+//   dx[i] += beta * q[i] * (1 - s) * (1 - x[i] s), s = sigmoid(x[i])             reaction
+//   d(beta) = sum over updated rows of g[i] * h(x)[i], next to d(alpha)
+// At steps 1 the adjoint and the recomputed stencil of a row meet in the same
+// march step (delay 0), so no delay line is needed.
+__device__ __forceinline__ float da_sigmoid(float v) { return __frcp_rn(__fadd_rn(1.0f, __expf(-v))); }
+
+// per element of a pair: f(v) = v * (1 - s) or f'(v) = (1 - s) * (1 - v s)
+template <bool DERIV>
+__device__ __forceinline__ pf2 reaction_fn(pf2 v) {
+  float v0, v1;
+  upk(v, v0, v1);
+  const float s0 = da_sigmoid(v0), s1 = da_sigmoid(v1);
+  if (DERIV)
+    return pk(__fmul_rn(__fsub_rn(1.0f, s0), __fsub_rn(1.0f, __fmul_rn(v0, s0))),
+              __fmul_rn(__fsub_rn(1.0f, s1), __fsub_rn(1.0f, __fmul_rn(v1, s1))));
+  return pk(__fmul_rn(v0, __fsub_rn(1.0f, s0)), __fmul_rn(v1, __fsub_rn(1.0f, s1)));
+}
+
+template <typename T, int S, bool CAUSAL, int KIND = 0>
 __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     bld_dalpha_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
                       const __grid_constant__ CUtensorMap ymap, const BldArgs a) {
+  static_assert(KIND == 0 || S == 1, "the other PDE kinds are single steps");
+  constexpr int NV = S + (KIND != 0 ? 1 : 0);  // reduced values: d(alpha_k) [, d(beta)]
   using Q = ColVec<T, kFwdVec>;
   using V = typename Q::V;
   using G = DaGeom<S, CAUSAL>;
@@ -149,9 +173,9 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
   const bool use_tma = a.use_tma != 0;
   const bool tstore = a.use_tma_store != 0;
 
-  pf2 acc[S];
+  pf2 acc[NV];
 #pragma unroll
-  for (int k = 0; k < S; ++k) acc[k] = 0ull;
+  for (int k = 0; k < NV; ++k) acc[k] = 0ull;
   int err = 0;
 
   if (active) {
@@ -188,6 +212,12 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     for (int k = 0; k < S; ++k) al[k] = pbc(alf[k]);
     const pf2 m2 = pbc(-2.f);
     const pf2 zn = pbc(a.neg_zero);
+    const pf2 n1 = pbc(-1.f), half = pbc(0.5f);
+    // KIND 1/2: beta in coefficient slot 1; q history (output gradient on updated rows)
+    const pf2 be = pbc(KIND == 0 ? 0.f
+                                 : (a.alpha_dev[1] != nullptr ? load_scalar(a.alpha_dev[1], a.alpha_dev_dtype)
+                                                              : a.alpha[1]));
+    pf2 Q1a = 0ull, Q1b = 0ull, Q2a = 0ull, Q2b = 0ull;
 
     // adjoint state per level m (forward step k = S - m): a = alpha*g on the two
     // previous rows (P1, P2), g on the one or two previous rows (G1, G2)
@@ -237,6 +267,18 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
         if (rb.zero(jg)) ga = gb = 0ull;
         if (rb.zero(jx)) xa = xb = 0ull;
       }
+      // ---- KIND 1/2: the beta term h(x) of the paired row and, for reaction,
+      // f'(x) of the row the adjoint finishes (from the window before its shift) ----
+      pf2 ha = 0ull, hb = 0ull, fpa = 0ull, fpb = 0ull;
+      if constexpr (KIND == 1) {
+        ha = CAUSAL ? pfma(F1a[0], n1, xa) : pmul(pfma(F2a[0], n1, xa), half);
+        hb = CAUSAL ? pfma(F1b[0], n1, xb) : pmul(pfma(F2b[0], n1, xb), half);
+      } else if constexpr (KIND == 2) {
+        ha = reaction_fn<false>(CAUSAL ? xa : F1a[0]);
+        hb = reaction_fn<false>(CAUSAL ? xb : F1b[0]);
+        fpa = reaction_fn<true>(F2a[0]);
+        fpb = reaction_fn<true>(F2b[0]);
+      }
       // ---- forward recomputation: lap(u_q) of this march row, q = 0..S-1 ----
       pf2 la[S], lb[S];
       {
@@ -278,6 +320,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
       const uint32_t fw = SLOW ? (CAUSAL ? rb.window16_fixed(jg - 2 * S) : rb.window8_fixed(jg - S)) : 0u;
       pf2 ca = pmul_sep(al[S - 1], ga, zn), cb2 = pmul_sep(al[S - 1], gb, zn);
       if (SLOW && f0) ca = cb2 = 0ull;
+      const pf2 qa = (SLOW && f0) ? 0ull : ga, qb = (SLOW && f0) ? 0ull : gb;  // q at row jg
       static_for<S>([&](auto M) {
         constexpr int m = decltype(M)::value;
         constexpr int k = S - m;
@@ -307,6 +350,10 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
           if (take) {
             acc[k - 1] = pfma(pga, pla, acc[k - 1]);
             acc[k - 1] = pfma(pgb, plb, acc[k - 1]);
+            if constexpr (KIND != 0) {
+              acc[S] = pfma(pga, ha, acc[S]);
+              acc[S] = pfma(pgb, hb, acc[S]);
+            }
           }
         }
         pf2 na = ga, nb = gb;
@@ -318,6 +365,26 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
             na = padd(G1a[m], plap(P2a[m], P1a[m], ca, m2));
             nb = padd(G1b[m], plap(P2b[m], P1b[m], cb2, m2));
           }
+          if constexpr (KIND != 0) {
+            // finished row i = jg-1 (causal jg-2): q[i-1], q[i], q[i+1] are
+            // (Q2, Q1, q) non-causal, q[i], q[i+1] are (Q2, Q1) causal
+            pf2 hta, htb;
+            if constexpr (KIND == 1) {
+              hta = CAUSAL ? pfma(Q1a, n1, Q2a) : pmul(pfma(qa, n1, Q2a), half);
+              htb = CAUSAL ? pfma(Q1b, n1, Q2b) : pmul(pfma(qb, n1, Q2b), half);
+            } else {
+              hta = pmul(fpa, CAUSAL ? Q2a : Q1a);
+              htb = pmul(fpb, CAUSAL ? Q2b : Q1b);
+            }
+            na = padd(na, pmul_sep(be, hta, zn));
+            nb = padd(nb, pmul_sep(be, htb, zn));
+          }
+        }
+        if constexpr (KIND != 0) {
+          Q2a = Q1a;
+          Q2b = Q1b;
+          Q1a = qa;
+          Q1b = qb;
         }
         P2a[m] = P1a[m];
         P1a[m] = ca;
@@ -429,9 +496,9 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
   // ---------------- deterministic d(alpha) reduction ----------------
   // a CTA that gave up after a timed-out wait contributes zeros, so the
   // completion protocol (and the counters) stay consistent
-  float part[S];
+  float part[NV];
 #pragma unroll
-  for (int k = 0; k < S; ++k) {
+  for (int k = 0; k < NV; ++k) {
     float lo, hi;
     upk(acc[k], lo, hi);
     float v = err ? 0.f : lo + hi;
@@ -445,11 +512,11 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
   const int gsz = a.dalpha_group;  // CTAs per group, a multiple of 32
   const int ngroups = (a.num_ctas + gsz - 1) / gsz;
   unsigned int* gcount = a.counter + 1;
-  double* gsum = reinterpret_cast<double*>(a.dalpha_partial + static_cast<int64_t>(a.num_ctas) * S +
-                                           ((static_cast<int64_t>(a.num_ctas) * S) & 1));
+  double* gsum = reinterpret_cast<double*>(a.dalpha_partial + static_cast<int64_t>(a.num_ctas) * NV +
+                                           ((static_cast<int64_t>(a.num_ctas) * NV) & 1));
   if (tid == 0) {
 #pragma unroll
-    for (int k = 0; k < S; ++k) a.dalpha_partial[static_cast<int64_t>(cta_id) * S + k] = part[k];
+    for (int k = 0; k < NV; ++k) a.dalpha_partial[static_cast<int64_t>(cta_id) * NV + k] = part[k];
   }
   __threadfence();
   __syncwarp();
@@ -463,13 +530,13 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
   // then a fixed shuffle tree over the lanes
   __threadfence();
 #pragma unroll
-  for (int k = 0; k < S; ++k) {
+  for (int k = 0; k < NV; ++k) {
     double v = 0.0;
     for (int j = tid; j < gsize; j += 32)
-      v += static_cast<double>(__ldcg(a.dalpha_partial + static_cast<int64_t>(grp * gsz + j) * S + k));
+      v += static_cast<double>(__ldcg(a.dalpha_partial + static_cast<int64_t>(grp * gsz + j) * NV + k));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (tid == 0) gsum[static_cast<int64_t>(grp) * S + k] = v;
+    if (tid == 0) gsum[static_cast<int64_t>(grp) * NV + k] = v;
   }
   if (tid == 0) gcount[grp] = 0u;
   __threadfence();
@@ -480,9 +547,9 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
   // last group: lanes stride over the group sums in order, then the same tree
   __threadfence();
 #pragma unroll
-  for (int k = 0; k < S; ++k) {
+  for (int k = 0; k < NV; ++k) {
     double v = 0.0;
-    for (int g = tid; g < ngroups; g += 32) v += __ldcg(gsum + static_cast<int64_t>(g) * S + k);
+    for (int g = tid; g < ngroups; g += 32) v += __ldcg(gsum + static_cast<int64_t>(g) * NV + k);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if (tid == 0) a.dalpha[k] = static_cast<float>(a.dalpha_accumulate ? static_cast<double>(a.dalpha[k]) + v : v);
@@ -493,6 +560,20 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
 size_t dalpha_smem_bytes(int dtype) { return dtype == kF32 ? da_smem<float>() : da_smem<__nv_bfloat16>(); }
 
 namespace {
+
+template <typename T, int KIND>
+const void* da_ptr_kind(int steps, int causal) {
+  if (steps != 1) return nullptr;
+  return causal ? reinterpret_cast<const void*>(bld_dalpha_kernel<T, 1, true, KIND>)
+                : reinterpret_cast<const void*>(bld_dalpha_kernel<T, 1, false, KIND>);
+}
+
+template <typename T>
+const void* da_ptr_any(int steps, int causal, int kind) {
+  if (kind == 1) return da_ptr_kind<T, 1>(steps, causal);
+  if (kind == 2) return da_ptr_kind<T, 2>(steps, causal);
+  return nullptr;
+}
 
 template <typename T, bool CAUSAL>
 const void* da_ptr(int steps) {
@@ -505,7 +586,15 @@ const void* da_ptr(int steps) {
   }
 }
 
-const void* da_kernel(int dtype, int steps, int causal) {
+const void* da_kernel(int dtype, int steps, int causal, int kind = 0) {
+  if (kind != 0) {
+    switch (dtype) {
+      case kF32: return da_ptr_any<float>(steps, causal, kind);
+      case kBF16: return da_ptr_any<__nv_bfloat16>(steps, causal, kind);
+      case kF16: return da_ptr_any<__half>(steps, causal, kind);
+      default: return nullptr;
+    }
+  }
   switch (dtype) {
     case kF32: return causal ? da_ptr<float, true>(steps) : da_ptr<float, false>(steps);
     case kBF16: return causal ? da_ptr<__nv_bfloat16, true>(steps) : da_ptr<__nv_bfloat16, false>(steps);
@@ -518,7 +607,7 @@ const void* da_kernel(int dtype, int steps, int causal) {
 
 cudaError_t launch_bld_dalpha(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap,
                               const CUtensorMap* ymap, int dtype, int steps, int causal, dim3 grid, cudaStream_t st) {
-  const void* kern = da_kernel(dtype, steps, causal);
+  const void* kern = da_kernel(dtype, steps, causal, a.pde_kind);
   if (kern == nullptr) return cudaErrorInvalidValue;
   const size_t smem = dalpha_smem_bytes(dtype);
   cudaError_t e = ensure_smem_attr(kern, smem);

@@ -769,13 +769,8 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
 }
 
 int64_t cta_pde_step_workspace_bytes(int64_t B, int64_t L, int64_t D) {
-  if (B <= 0 || L <= 0 || D <= 0) return 256;
-  PdeArgs p;
-  std::memset(&p, 0, sizeof(p));
-  p.L = L;
-  p.D = static_cast<int>(D);
-  p.nbatch = static_cast<int>(B);
-  return std::max<int64_t>(256, pde_step_num_ctas(p) * 2 * static_cast<int64_t>(sizeof(float)));
+  // the d(alpha) march layout with two reduced values (d(alpha), d(beta))
+  return cta_diffusion_bwd_bld_workspace_bytes(B, L, D, CTA_F32, 2, 0);
 }
 
 int cta_pde_step_bld(const void* x, const void* grad_out, void* y, float* dcoef, void* workspace,
@@ -796,39 +791,13 @@ int cta_pde_step_bld(const void* x, const void* grad_out, void* y, float* dcoef,
     return fail(CTA_EINVAL, "null tensor pointer");
   if (x_sL < D || y_sL < D || (backward && g_sL < D)) return fail(CTA_EINVAL, "row stride smaller than D");
   if (mask != nullptr && !valid_mask_dtype(mask_dtype)) return fail(CTA_EINVAL, "bad mask dtype %d", mask_dtype);
-  PdeArgs p;
-  std::memset(&p, 0, sizeof(p));
-  p.x = x;
-  p.g = grad_out;
-  p.y = y;
-  p.xsB = x_sB;
-  p.xsL = x_sL;
-  p.gsB = g_sB;
-  p.gsL = g_sL;
-  p.ysB = y_sB;
-  p.ysL = y_sL;
-  p.L = L;
-  p.D = static_cast<int>(D);
-  p.nbatch = static_cast<int>(B);
-  p.mask = mask;
-  p.mask_dtype = mask_dtype;
-  p.msB = mask_sB;
-  p.msL = mask_sL;
-  p.alpha_dev = alpha_dev;
-  p.beta_dev = beta_dev;
-  p.coef_dtype = coef_dtype;
-  p.x_vec = quad_ok(x, dtype, B, D, x_sB, x_sL) ? 1 : 0;
-  p.g_vec = (backward && quad_ok(grad_out, dtype, B, D, g_sB, g_sL)) ? 1 : 0;
-  p.y_vec = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
   if (backward) {
     if (dcoef == nullptr) return fail(CTA_EINVAL, "backward needs dcoef (fp32 [2])");
-    if (workspace == nullptr || reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
-      return fail(CTA_EINVAL, "backward needs a 16-byte aligned workspace");
+    if (workspace == nullptr || reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+      return fail(CTA_EINVAL, "backward needs a 256-byte aligned workspace");
     const int64_t need = cta_pde_step_workspace_bytes(B, L, D);
     if (workspace_bytes < need)
       return fail(CTA_EINVAL, "workspace too small: %lld < %lld bytes", (long long)workspace_bytes, (long long)need);
-    p.partial = static_cast<float*>(workspace);
-    p.dcoef = dcoef;
   }
   if (B == 0 || L == 0 || D == 0) {
     if (backward) {
@@ -837,42 +806,46 @@ int cta_pde_step_bld(const void* x, const void* grad_out, void* y, float* dcoef,
     }
     return ok();
   }
-  if (!backward) {
-    // forward: the one-warp TMA march kernel at steps 1 with the layer's update
-    BldArgs m = blank_bld();
-    m.x = x;
-    m.y = y;
-    m.xsB = x_sB;
-    m.xsL = x_sL;
-    m.ysB = y_sB;
-    m.ysL = y_sL;
-    m.L = L;
-    m.D = static_cast<int>(D);
-    m.nbatch = static_cast<int>(B);
-    m.global_len = L;
-    m.mask = mask;
-    m.mask_dtype = mask_dtype;
-    m.msB = mask_sB;
-    m.msL = mask_sL;
-    m.alpha_dev[0] = alpha_dev;
-    m.alpha_dev[1] = beta_dev;
-    m.alpha_dev_dtype = coef_dtype;
-    m.pde_kind = kind == CTA_PDE_ADVECTION ? 1 : 2;
-    const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-    m.TL = pick_tl(L, ndt * B, 1, march_per_sm(dtype, 1, causal ? 1 : 0, 0));
-    m.out_begin = 0;
-    m.out_end = L;
-    m.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
-    CUtensorMap xmap, ymap;
-    std::memset(&xmap, 0, sizeof(xmap));
-    std::memset(&ymap, 0, sizeof(ymap));
-    m.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
-    m.use_tma_store = make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
-    return launch_fwd(m, dtype, 1, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), xmap, ymap);
+  // both directions run on the one-warp TMA march kernels at steps 1 with the
+  // layer's update: the forward march, and the d(alpha) march (backward, which
+  // also reduces d(beta))
+  BldArgs m = blank_bld();
+  m.x = x;
+  m.y = y;
+  m.xsB = x_sB;
+  m.xsL = x_sL;
+  m.ysB = y_sB;
+  m.ysL = y_sL;
+  m.L = L;
+  m.D = static_cast<int>(D);
+  m.nbatch = static_cast<int>(B);
+  m.global_len = L;
+  m.mask = mask;
+  m.mask_dtype = mask_dtype;
+  m.msB = mask_sB;
+  m.msL = mask_sL;
+  m.alpha_dev[0] = alpha_dev;
+  m.alpha_dev[1] = beta_dev;
+  m.alpha_dev_dtype = coef_dtype;
+  m.pde_kind = kind == CTA_PDE_ADVECTION ? 1 : 2;
+  m.out_begin = 0;
+  m.out_end = L;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (backward) {
+    m.g = grad_out;
+    m.gsB = g_sB;
+    m.gsL = g_sL;
+    return launch_dalpha_march(m, dtype, 1, causal ? 1 : 0, B, L, D, workspace, dcoef, false, true, st);
   }
-  const cudaError_t e = launch_pde_step(p, dtype, kind, causal ? 1 : 0, 1, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "pde step launch");
-  return ok();
+  const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
+  m.TL = pick_tl(L, ndt * B, 1, march_per_sm(dtype, 1, causal ? 1 : 0, 0));
+  m.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
+  CUtensorMap xmap, ymap;
+  std::memset(&xmap, 0, sizeof(xmap));
+  std::memset(&ymap, 0, sizeof(ymap));
+  m.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
+  m.use_tma_store = make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
+  return launch_fwd(m, dtype, 1, causal ? 1 : 0, B, L, st, xmap, ymap);
 }
 
 int cta_diffusion_shard_bld_dalpha(const void* grad_out, const void* x, void* grad_in, float* dalpha,

@@ -138,29 +138,6 @@ struct BdlArgs {
   int tw, nseg;
 };
 
-// One step of the advection- / reaction-diffusion layers on [B, L, D]
-enum : int { kPdeAdvection = 0, kPdeReaction = 1 };
-struct PdeArgs {
-  const void* x;  // forward input (both directions)
-  const void* g;  // backward: gradient of the output
-  void* y;        // forward: output.  backward: gradient of the input
-  int64_t xsB, xsL, gsB, gsL, ysB, ysL;
-  int64_t L;
-  int D;
-  int nbatch;
-  const void* mask;
-  int mask_dtype;
-  int64_t msB, msL;
-  const void* alpha_dev;  // device scalars (the layer parameters)
-  const void* beta_dev;
-  int coef_dtype;
-  int x_vec, g_vec, y_vec;  // 4-column vector access is legal for every row
-  float* partial;           // backward: [num_ctas][2] partial sums (caller scratch)
-  float* dcoef;             // backward: [2] d(alpha), d(beta)
-};
-cudaError_t launch_pde_step(const PdeArgs& a, int dtype, int kind, int causal, int backward, cudaStream_t st);
-int64_t pde_step_num_ctas(const PdeArgs& a);
-
 // launch march kernels with programmatic dependent launch (tuning key 3)
 int pdl_enabled();
 

@@ -26,7 +26,7 @@ BUILD_DIR = SRC_ROOT / "_build"
 LIB_NAME = "libcta_stencil.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["capi.cu", "bld_fwd.cu", "bld_bwd.cu", "bld_dalpha.cu", "stencil_bdl.cu", "pde_step.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "bld_fwd.cu", "bld_bwd.cu", "bld_dalpha.cu", "stencil_bdl.cu", "noalloc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = [
     "-O3",

@@ -179,8 +179,10 @@ int cta_diffusion_fwd_bld_residual(const void* x, const void* residual, void* y,
  * alpha_dev / beta_dev are device scalars (the layer parameters, coef_dtype).
  * backward = 0: x -> y (grad_out, dcoef, workspace unused).
  * backward = 1: y = dx for grad_out and the forward input x, dcoef = fp32
- * [d(alpha), d(beta)] (reduced deterministically, two launches); workspace of
- * cta_pde_step_workspace_bytes(B, L, D) bytes, 16-byte aligned, no zeroing. */
+ * [d(alpha), d(beta)] (reduced deterministically in the same launch);
+ * workspace of cta_pde_step_workspace_bytes(B, L, D) bytes, 256-byte aligned,
+ * zeroed once before its first use (the kernel leaves its counters at zero;
+ * the d(alpha) workspace layout of cta_diffusion_bwd_bld). */
 int64_t cta_pde_step_workspace_bytes(int64_t B, int64_t L, int64_t D);
 int cta_pde_step_bld(const void* x, const void* grad_out, void* y, float* dcoef, void* workspace,
                      int64_t workspace_bytes, int64_t B, int64_t L, int64_t D, int64_t x_sB, int64_t x_sL,
