@@ -118,16 +118,24 @@ constexpr int da_min_ctas() {
 // march step (delay 0), so no delay line is needed.
 __device__ __forceinline__ float da_sigmoid(float v) { return __frcp_rn(__fadd_rn(1.0f, __expf(-v))); }
 
-// per element of a pair: f(v) = v * (1 - s) or f'(v) = (1 - s) * (1 - v s)
-template <bool DERIV>
-__device__ __forceinline__ pf2 reaction_fn(pf2 v) {
+// per element of a pair: s = sigmoid(v); f(v) = v * (1 - s); f'(v) = (1 - s) * (1 - v s)
+__device__ __forceinline__ pf2 psigmoid(pf2 v) {
   float v0, v1;
   upk(v, v0, v1);
-  const float s0 = da_sigmoid(v0), s1 = da_sigmoid(v1);
-  if (DERIV)
-    return pk(__fmul_rn(__fsub_rn(1.0f, s0), __fsub_rn(1.0f, __fmul_rn(v0, s0))),
-              __fmul_rn(__fsub_rn(1.0f, s1), __fsub_rn(1.0f, __fmul_rn(v1, s1))));
+  return pk(da_sigmoid(v0), da_sigmoid(v1));
+}
+__device__ __forceinline__ pf2 reaction_f(pf2 v, pf2 s) {
+  float v0, v1, s0, s1;
+  upk(v, v0, v1);
+  upk(s, s0, s1);
   return pk(__fmul_rn(v0, __fsub_rn(1.0f, s0)), __fmul_rn(v1, __fsub_rn(1.0f, s1)));
+}
+__device__ __forceinline__ pf2 reaction_df(pf2 v, pf2 s) {
+  float v0, v1, s0, s1;
+  upk(v, v0, v1);
+  upk(s, s0, s1);
+  return pk(__fmul_rn(__fsub_rn(1.0f, s0), __fsub_rn(1.0f, __fmul_rn(v0, s0))),
+            __fmul_rn(__fsub_rn(1.0f, s1), __fsub_rn(1.0f, __fmul_rn(v1, s1))));
 }
 
 template <typename T, int S, bool CAUSAL, int KIND = 0>
@@ -218,6 +226,8 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
                                  : (a.alpha_dev[1] != nullptr ? load_scalar(a.alpha_dev[1], a.alpha_dev_dtype)
                                                               : a.alpha[1]));
     pf2 Q1a = 0ull, Q1b = 0ull, Q2a = 0ull, Q2b = 0ull;
+    // reaction: sigmoid of the paired row, kept for the rows the adjoint finishes later
+    pf2 S1a = 0ull, S1b = 0ull, S2a = 0ull, S2b = 0ull;
 
     // adjoint state per level m (forward step k = S - m): a = alpha*g on the two
     // previous rows (P1, P2), g on the one or two previous rows (G1, G2)
@@ -274,10 +284,18 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
         ha = CAUSAL ? pfma(F1a[0], n1, xa) : pmul(pfma(F2a[0], n1, xa), half);
         hb = CAUSAL ? pfma(F1b[0], n1, xb) : pmul(pfma(F2b[0], n1, xb), half);
       } else if constexpr (KIND == 2) {
-        ha = reaction_fn<false>(CAUSAL ? xa : F1a[0]);
-        hb = reaction_fn<false>(CAUSAL ? xb : F1b[0]);
-        fpa = reaction_fn<true>(F2a[0]);
-        fpb = reaction_fn<true>(F2b[0]);
+        // the paired row is jg; the finished row jg-1 (causal jg-2), whose x is
+        // F2 and whose sigmoid was taken one (two) march steps ago
+        const pf2 ca_ = CAUSAL ? xa : F1a[0], cb_ = CAUSAL ? xb : F1b[0];
+        const pf2 sa = psigmoid(ca_), sb = psigmoid(cb_);
+        ha = reaction_f(ca_, sa);
+        hb = reaction_f(cb_, sb);
+        fpa = reaction_df(F2a[0], CAUSAL ? S2a : S1a);
+        fpb = reaction_df(F2b[0], CAUSAL ? S2b : S1b);
+        S2a = S1a;
+        S2b = S1b;
+        S1a = sa;
+        S1b = sb;
       }
       // ---- forward recomputation: lap(u_q) of this march row, q = 0..S-1 ----
       pf2 la[S], lb[S];
