@@ -111,7 +111,10 @@ constexpr int kBdlThreads = 256;  // 8 warps, each owns two 256-wide windows
 constexpr int kBdlElems = 8;      // positions per lane
 constexpr int kBdlOut = 240;      // output positions per window (30 lanes)
 constexpr int kBdlWin = 256;      // loaded positions per window (32 lanes x 8)
-constexpr int kBdlRows = 2;       // rows per one-warp CTA of the TMA form (pair halves)
+#ifndef CTA_BDL_ROWS
+#define CTA_BDL_ROWS 2
+#endif
+constexpr int kBdlRows = CTA_BDL_ROWS;  // rows per one-warp CTA of the TMA form (pairs of pair halves)
 constexpr int kBdlStages = 4;     // input windows in flight per CTA (TMA form)
 // staging slot of the TMA form: kBdlRows x kBdlOut elements, rounded up to 128 bytes
 template <typename T>

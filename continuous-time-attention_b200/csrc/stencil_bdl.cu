@@ -317,6 +317,8 @@ __global__ void __launch_bounds__(32, 16)
   constexpr int NST = kBdlStages;
   constexpr int IN_CHUNK = kBdlRows * kBdlWin;                    // elements per input slot
   constexpr int OUT_SLOT = bdl_out_slot_elems<T>();               // elements per staging slot (128-B multiple)
+  constexpr int NP = kBdlRows / 2;                                // row pairs (register pair sets) per CTA
+  static_assert(kBdlRows % 2 == 0, "rows come in pairs");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   T* ring = reinterpret_cast<T*>(smem_raw);
   T* stage = ring + NST * IN_CHUNK;
@@ -329,8 +331,7 @@ __global__ void __launch_bounds__(32, 16)
   const int64_t w1 = w0 + a.tw < nwin ? w0 + a.tw : nwin;
   if (w0 >= w1) return;
   const int nw = static_cast<int>(w1 - w0);
-  const int64_t r0 = 2 * rp;
-  const bool vb = r0 + 1 < a.rows;
+  const int64_t r0 = static_cast<int64_t>(kBdlRows) * rp;
 
   if (lane == 0) {
     prefetch_tmap(&imap);
@@ -363,21 +364,24 @@ __global__ void __launch_bounds__(32, 16)
     const int64_t p = ws + lane * E8;
     if (!err) {
       const T* buf = ring + slot * IN_CHUNK + lane * E8;
-      pf2 e[E8];
-      bdl_smem_pairs<T>(buf, buf + kBdlWin, e);
       const bool interior = a.mask == nullptr && ws > lo_fixed && ws + kBdlWin - 1 < hi_fixed;
-      uint32_t fa = 0u, fb = 0u;
-      if (!interior) {
-        fa = fixed_bits<CAUSAL>(a, r0, p, true);
-        fb = fixed_bits<CAUSAL>(a, r0 + 1, p, vb);
-      }
-      if (!interior && __any_sync(0xffffffffu, (fa | fb) != 0u))
-        window_levels<S, CAUSAL, BWD, true>(e, fa, fb, al, m2, zn);
-      else
-        window_levels<S, CAUSAL, BWD, false>(e, fa, fb, al, m2, zn);
-      if (lane >= HLN && lane < 32 - HRN) {
-        T* st = stage + (i & 1) * OUT_SLOT + (lane - HLN) * E8;
-        bdl_smem_store_pairs<T>(st, st + kBdlOut, e);
+#pragma unroll
+      for (int q = 0; q < NP; ++q) {
+        pf2 e[E8];
+        bdl_smem_pairs<T>(buf + (2 * q) * kBdlWin, buf + (2 * q + 1) * kBdlWin, e);
+        uint32_t fa = 0u, fb = 0u;
+        if (!interior) {
+          fa = fixed_bits<CAUSAL>(a, r0 + 2 * q, p, r0 + 2 * q < a.rows);
+          fb = fixed_bits<CAUSAL>(a, r0 + 2 * q + 1, p, r0 + 2 * q + 1 < a.rows);
+        }
+        if (!interior && __any_sync(0xffffffffu, (fa | fb) != 0u))
+          window_levels<S, CAUSAL, BWD, true>(e, fa, fb, al, m2, zn);
+        else
+          window_levels<S, CAUSAL, BWD, false>(e, fa, fb, al, m2, zn);
+        if (lane >= HLN && lane < 32 - HRN) {
+          T* st = stage + (i & 1) * OUT_SLOT + (2 * q) * kBdlOut + (lane - HLN) * E8;
+          bdl_smem_store_pairs<T>(st, st + kBdlOut, e);
+        }
       }
       fence_proxy_async_smem();
     }
