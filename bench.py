@@ -608,6 +608,18 @@ def run_kernels(args, rank, world, local_rank):
         timed(name + "_forward", 1, lambda i, kind=kind: ops.pde_step(xs[i % nb], kind, coef, coef, out=ys[i % nb]), 2)
         timed(name + "_backward", 1,
               lambda i, kind=kind: ops.pde_step(xs[i % nb], kind, coef, coef, grad_out=gs[i % nb], out=ys[i % nb]), 3)
+    # the classifier's last refinement + masked mean pool: fused (x read once,
+    # nothing written but [B, D]) against the stack followed by torch's pooling
+    pmask = torch.ones(1, L, dtype=torch.long, device=dev)
+    pmask[:, L - L // 8 :] = 0
+
+    def stack_then_pool(i):
+        y = ops.bld_forward(xs[i % nb], [0.1] * 4, 4, mask=pmask, out=ys[i % nb])
+        torch.sum(y * pmask.unsqueeze(-1), dim=1) / torch.clamp(pmask.sum(dim=1, keepdim=True), min=1)
+
+    timed("bld_forward_masked", 4, lambda i: ops.bld_forward(xs[i % nb], [0.1] * 4, 4, mask=pmask, out=ys[i % nb]), 2)
+    timed("bld_forward_pool", 4, lambda i: ops.bld_forward_pool(xs[i % nb], [0.1] * 4, 4, pmask), 1)
+    timed("bld_forward_then_torch_pool", 4, stack_then_pool, 1)
     for S in (1, 4):
         timed("bld_adjoint_dalpha", S,
               lambda i, S=S: ops.bld_backward(gs[i % nb], [0.1] * S, S, x=xs[i % nb], need_dalpha=True,

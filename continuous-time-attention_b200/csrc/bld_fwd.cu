@@ -114,10 +114,17 @@ __device__ __forceinline__ pf2 level_update(pf2 p2, pf2 p1, pf2 x, pf2 al, pf2 b
 // The residual rows of each full output chunk are brought by a TMA load into
 // the staging slot that chunk is about to use, issued one chunk ahead; the
 // lanes add them in place and the TMA store sends the sum out.
-template <typename T, int S, bool CAUSAL, bool ADJ, bool RES, int KIND = 0>
+// POOL (non-causal forward, masked): the classifier's masked mean pool
+// (src/models/transformers.py:135-139) fused into the last refinement: the
+// output rows are not stored; each lane sums mask[row] * y[row] (y rounded to
+// T, as the stored tensor would hold it) over its rows, and the CTA writes its
+// column sums to a.pool_partial[(batch * row tiles + row tile) * D + col], for
+// pool_finish_kernel to reduce in a fixed order.
+template <typename T, int S, bool CAUSAL, bool ADJ, bool RES, int KIND = 0, bool POOL = false>
 __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ, RES>()))
     bld_march_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                      const __grid_constant__ CUtensorMap rmap, const BldArgs a) {
+  static_assert(!POOL || (!ADJ && !RES && KIND == 0 && !CAUSAL), "the pooled form is the non-causal forward");
   static_assert(!RES || (!ADJ && !CAUSAL), "the residual form is the non-causal forward");
   static_assert(KIND == 0 || (S == 1 && !ADJ && !RES), "the other PDE kinds are single forward steps");
   // every global read (cu_seqlens, mask, alphas, the streams) comes after the wait
@@ -141,6 +148,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   T* stage = ring + kFwdStages * CHUNK;  // output staging for the TMA stores
   __shared__ __align__(8) uint64_t full_bar[kFwdStages];
   __shared__ __align__(8) uint64_t res_bar[RES ? 2 : 1];
+  __shared__ uint32_t pbits[POOL ? kBldMaxWords : 1];  // POOL: mask bits of the tile's output rows
   __shared__ uint32_t fbits[kBldMaxWords + 2];
   __shared__ uint32_t zbits[kBldMaxWords + 2];
 
@@ -193,6 +201,16 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   }
   RowBits rb{fbits, zbits, jb};
   const bool slow = build_row_bits<CAUSAL, 1>(a, sg, rb, (nch * kFwdRC + 31) / 32);
+  if constexpr (POOL) {
+    // bit r of word w: mask of output row l0 + 32 w + r (read once per tile)
+    for (int w = 0; w < (nout + 31) / 32; ++w) {
+      const int64_t r = l0 + 32 * w + tid;
+      const bool v = r < oend && mask_valid(a.mask, a.mask_dtype, static_cast<int64_t>(sg.bcoord) * a.msB + r * a.msL);
+      const uint32_t m = __ballot_sync(0xffffffffu, v);
+      if (tid == 0) pbits[w] = m;
+    }
+    __syncwarp();
+  }
 
   float alf[kMaxSteps];
   load_alphas(a, alf, S);
@@ -225,7 +243,18 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
           : nullptr;
   const int soff = cb;  // element offset of this lane in a slot row
 
+  pf2 pool_a = 0ull, pool_b = 0ull;  // POOL: masked column sums of this lane
   auto store_row = [&](int64_t orow, pf2 pa, pf2 pb) {
+    if constexpr (POOL) {
+      const int64_t rr = orow - l0;
+      if (col_ok && ((pbits[rr >> 5] >> (rr & 31)) & 1u)) {
+        pf2 ra, rb2;
+        Q::split(Q::join(pa, pb), ra, rb2);  // the values the stored tensor would hold
+        pool_a = padd(pool_a, ra);
+        pool_b = padd(pool_b, rb2);
+      }
+      return;
+    }
     T* yp = ybase + orow * a.ysL;
     if (quad_ok) {
       V y = Q::join(pa, pb);
@@ -446,6 +475,68 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   };
   const bool ok = slow ? run(std::true_type{}) : run(std::false_type{});
   if (ok && tstore && tid == 0) bulk_wait_all();
+  if constexpr (POOL) {
+    const int64_t ntl = gridDim.x / ndt;
+    float* pp = a.pool_partial + ((static_cast<int64_t>(sg.bcoord) * ntl + blockIdx.x / ndt) * a.D);
+    float v[4];
+    upk(pool_a, v[0], v[1]);
+    upk(pool_b, v[2], v[3]);
+#pragma unroll
+    for (int j = 0; j < kFwdVec; ++j)
+      if (col + j < a.D) pp[col + j] = ok ? v[j] : 0.f;
+    if (dtile == 0 && tid == 0) {
+      // valid rows of this tile, after the nbatch * ntl * D partials (exact in fp32)
+      int n = 0;
+      for (int w = 0; w < (nout + 31) / 32; ++w) n += __popc(pbits[w]);
+      a.pool_partial[(static_cast<int64_t>(a.nbatch) * ntl) * a.D + static_cast<int64_t>(sg.bcoord) * ntl +
+                     blockIdx.x / ndt] = static_cast<float>(n);
+    }
+  }
+}
+
+// pooled[b, d] = round_T(round_T(sum_t partial[b][t][d]) / max(sum_t count[b][t], 1)):
+// the reference's half-precision sum and division (transformers.py:135-139).
+// A CTA owns 32 columns of one batch row; warp w sums tiles w, w + 32, ... of
+// its lane's column with four interleaved accumulators, the per-tile valid-row
+// counts are summed by a fixed tree, and warp 0 adds the 32 warp sums in order.
+// Every order depends on the shape alone, so the result is deterministic.
+template <typename T>
+__global__ void __launch_bounds__(kPoolThreads) pool_finish_kernel(const BldArgs a, int64_t ntl, void* pooled) {
+  constexpr int NW = kPoolThreads / 32;
+  __shared__ double part[NW][33];
+  __shared__ double cnt[NW];
+  const int b = blockIdx.y;
+  const int cl = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const float* counts = a.pool_partial + static_cast<int64_t>(a.nbatch) * ntl * a.D + static_cast<int64_t>(b) * ntl;
+  double c = 0.0;
+  for (int64_t t = threadIdx.x; t < ntl; t += kPoolThreads) c += static_cast<double>(counts[t]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if (cl == 0) cnt[w] = c;
+  const int d = blockIdx.x * 32 + cl;
+  double s[4] = {0.0, 0.0, 0.0, 0.0};
+  if (d < a.D) {
+    const float* col = a.pool_partial + static_cast<int64_t>(b) * ntl * a.D + d;
+    int64_t t = w;
+    for (; t + 3 * NW < ntl; t += 4 * NW) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) s[k] += static_cast<double>(col[(t + k * NW) * a.D]);
+    }
+    for (int k = 0; t < ntl; t += NW, ++k) s[k] += static_cast<double>(col[t * a.D]);
+  }
+  part[w][cl] = (s[0] + s[1]) + (s[2] + s[3]);
+  __syncthreads();
+  if (w == 0 && d < a.D) {
+    double sum = 0.0, n = 0.0;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+      sum += part[k][cl];
+      n += cnt[k];
+    }
+    const float count = n < 1.0 ? 1.f : static_cast<float>(n);
+    const float s_t = Elem<T>::to_f(Elem<T>::from_f(static_cast<float>(sum)));
+    static_cast<T*>(pooled)[static_cast<int64_t>(b) * a.D + d] = Elem<T>::from_f(__fdiv_rn(s_t, count));
+  }
 }
 
 size_t fwd_smem_bytes(int dtype) {
@@ -488,7 +579,31 @@ const void* march_ptr_t(int steps, int causal, int adj, int res, int kind) {
   return causal ? march_ptr<T, true, false, false>(steps) : march_ptr<T, false, false, false>(steps);
 }
 
-const void* march_kernel(int dtype, int steps, int causal, int adj, int res, int kind = 0) {
+template <typename T>
+const void* march_ptr_pool(int steps) {
+  switch (steps) {
+    case 1: return reinterpret_cast<const void*>(bld_march_kernel<T, 1, false, false, false, 0, true>);
+    case 2: return reinterpret_cast<const void*>(bld_march_kernel<T, 2, false, false, false, 0, true>);
+    case 3: return reinterpret_cast<const void*>(bld_march_kernel<T, 3, false, false, false, 0, true>);
+    case 4: return reinterpret_cast<const void*>(bld_march_kernel<T, 4, false, false, false, 0, true>);
+    case 5: return reinterpret_cast<const void*>(bld_march_kernel<T, 5, false, false, false, 0, true>);
+    case 6: return reinterpret_cast<const void*>(bld_march_kernel<T, 6, false, false, false, 0, true>);
+    case 7: return reinterpret_cast<const void*>(bld_march_kernel<T, 7, false, false, false, 0, true>);
+    case 8: return reinterpret_cast<const void*>(bld_march_kernel<T, 8, false, false, false, 0, true>);
+    default: return nullptr;
+  }
+}
+
+const void* march_kernel(int dtype, int steps, int causal, int adj, int res, int kind = 0, int pool = 0) {
+  if (pool) {
+    if (causal || adj || res || kind) return nullptr;
+    switch (dtype) {
+      case kF32: return march_ptr_pool<float>(steps);
+      case kBF16: return march_ptr_pool<__nv_bfloat16>(steps);
+      case kF16: return march_ptr_pool<__half>(steps);
+      default: return nullptr;
+    }
+  }
   switch (dtype) {
     case kF32: return march_ptr_t<float>(steps, causal, adj, res, kind);
     case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, adj, res, kind);
@@ -502,7 +617,8 @@ const void* march_kernel(int dtype, int steps, int causal, int adj, int res, int
 cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap,
                            const CUtensorMap* rmap, int dtype, int steps, int causal, int adjoint, dim3 grid,
                            size_t smem, cudaStream_t st) {
-  const void* kern = march_kernel(dtype, steps, causal, adjoint, a.residual != nullptr ? 1 : 0, a.pde_kind);
+  const void* kern = march_kernel(dtype, steps, causal, adjoint, a.residual != nullptr ? 1 : 0, a.pde_kind,
+                                  a.pool_partial != nullptr ? 1 : 0);
   if (kern == nullptr) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem_attr(kern, smem);
   if (e != cudaSuccess) return e;
@@ -520,6 +636,17 @@ cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUte
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelExC(&cfg, kern, args);
+}
+
+cudaError_t launch_pool_finish(const BldArgs& a, int dtype, int64_t ntl, void* pooled, cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>((a.D + 31) / 32), static_cast<unsigned>(a.nbatch));
+  switch (dtype) {
+    case kF32: pool_finish_kernel<float><<<grid, kPoolThreads, 0, st>>>(a, ntl, pooled); break;
+    case kBF16: pool_finish_kernel<__nv_bfloat16><<<grid, kPoolThreads, 0, st>>>(a, ntl, pooled); break;
+    case kF16: pool_finish_kernel<__half><<<grid, kPoolThreads, 0, st>>>(a, ntl, pooled); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
 }
 
 int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual) {

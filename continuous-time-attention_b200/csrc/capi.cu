@@ -472,6 +472,68 @@ int cta_diffusion_fwd_bld(const void* x, void* y, int64_t B, int64_t L, int64_t 
                       alpha_dev_dtype, mask, mask_dtype, mask_sB, mask_sL, stream);
 }
 
+int64_t cta_diffusion_fwd_bld_pool_workspace_bytes(int64_t B, int64_t L, int64_t D) {
+  if (B <= 0 || L <= 0 || D <= 0) return 256;
+  // per row tile (at least 32 rows): D column sums and one valid-row count
+  return std::max<int64_t>(256, ((L + 31) / 32) * B * (D + 1) * static_cast<int64_t>(sizeof(float)));
+}
+
+int cta_diffusion_fwd_bld_pool(const void* x, void* pooled, void* workspace, int64_t workspace_bytes, int64_t B,
+                               int64_t L, int64_t D, int64_t x_sB, int64_t x_sL, int dtype, int steps,
+                               const float* alpha, const void* const* alpha_dev, int alpha_dev_dtype,
+                               const void* mask, int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream) {
+  int rc = check_common(dtype, steps);
+  if (rc) return rc;
+  rc = check_alpha(steps, alpha, alpha_dev, alpha_dev_dtype);
+  if (rc) return rc;
+  if (B < 0 || L < 0 || D < 0) return fail(CTA_EINVAL, "negative shape");
+  if (B == 0 || D == 0) return ok();
+  if (L < 3) return fail(CTA_EINVAL, "L < 3 is the identity; handled by the caller");
+  if (B > 65535) return fail(CTA_EUNSUPPORTED, "at most 65535 batch rows");
+  if (x == nullptr || pooled == nullptr) return fail(CTA_EINVAL, "null tensor pointer");
+  if (x_sL < D) return fail(CTA_EINVAL, "row stride smaller than D");
+  if (mask == nullptr || !valid_mask_dtype(mask_dtype)) return fail(CTA_EINVAL, "the masked pool needs a mask");
+  if (workspace == nullptr || reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+    return fail(CTA_EINVAL, "the masked pool needs a 16-byte aligned workspace");
+  const int64_t need = cta_diffusion_fwd_bld_pool_workspace_bytes(B, L, D);
+  if (workspace_bytes < need)
+    return fail(CTA_EINVAL, "workspace too small: %lld < %lld bytes", (long long)workspace_bytes, (long long)need);
+  BldArgs a = blank_bld();
+  a.x = x;
+  a.y = workspace;  // never written: the pooled form stores no rows
+  a.xsB = x_sB;
+  a.xsL = x_sL;
+  a.L = L;
+  a.D = static_cast<int>(D);
+  a.nbatch = static_cast<int>(B);
+  a.global_len = L;
+  a.mask = mask;
+  a.mask_dtype = mask_dtype;
+  a.msB = mask_sB;
+  a.msL = mask_sL;
+  a.pool_partial = static_cast<float*>(workspace);
+  fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
+  const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
+  a.TL = pick_tl(L, ndt * B, steps, march_per_sm(dtype, steps, 0, 0));
+  // a row-tile override below 32 rows needs more partials than the size query reports
+  const int64_t ntl = (L + a.TL - 1) / a.TL;
+  if (ntl * B * (D + 1) * static_cast<int64_t>(sizeof(float)) > workspace_bytes)
+    return fail(CTA_EINVAL, "workspace too small for %lld row tiles", (long long)ntl);
+  a.out_begin = 0;
+  a.out_end = L;
+  CUtensorMap xmap, ymap;
+  std::memset(&xmap, 0, sizeof(xmap));
+  std::memset(&ymap, 0, sizeof(ymap));
+  a.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
+  a.use_tma_store = 0;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = launch_fwd(a, dtype, steps, 0, B, L, st, xmap, ymap);
+  if (rc) return rc;
+  const cudaError_t e = launch_pool_finish(a, dtype, ntl, pooled, st);
+  if (e != cudaSuccess) return cuda_fail(e, "masked pool reduction launch");
+  return ok();
+}
+
 int cta_diffusion_fwd_bld_residual(const void* x, const void* residual, void* y, int64_t B, int64_t L, int64_t D,
                                    int64_t x_sB, int64_t x_sL, int64_t r_sB, int64_t r_sL, int64_t y_sB,
                                    int64_t y_sL, int dtype, int steps, const float* alpha, const void* mask,

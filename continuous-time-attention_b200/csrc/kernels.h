@@ -48,6 +48,7 @@ constexpr int64_t kWsHeaderBytes = 8192;
 constexpr int kWsMaxGroups = static_cast<int>(kWsHeaderBytes / 4) - 1;
 constexpr int kDaMaxSteps = 4;  // steps handled by the march d(alpha) kernel
 constexpr int kBldMaxWords = (kBldMaxTL + 2 * 2 * kMaxSteps + kBldRC + 31) / 32 + 1;
+constexpr int kPoolThreads = 1024;  // masked-pool finish: 32 columns x 32 tile strides
 
 struct BldArgs {
   // streams (element pointers); columns are contiguous
@@ -97,6 +98,9 @@ struct BldArgs {
   // 0: diffusion.  1 / 2: advection- / reaction-diffusion layer step (steps 1,
   // beta in coefficient slot 1)
   int pde_kind;
+  // forward only: masked mean pool of the output instead of storing it,
+  // per-CTA column sums [nbatch][row tiles][D] (fp32, caller scratch)
+  float* pool_partial;
   // L-shard halos of the gradient stream for the d(alpha) kernel (lo_ext/hi_ext
   // above hold the x stream's): [nbatch, g_hext_lo|hi, D]
   const void* g_lo_ext;
@@ -148,6 +152,9 @@ int pdl_enabled();
 // resident one-warp CTAs per SM of a march kernel variant on the current device
 // (occupancy query, cached), or -1
 int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual = 0);
+// reduces the pooled partials of a POOL march launch with `ntl` row tiles into
+// pooled [nbatch, D] of the tensor dtype
+cudaError_t launch_pool_finish(const BldArgs& a, int dtype, int64_t ntl, void* pooled, cudaStream_t st);
 // march kernel: forward (adjoint = 0) or the adjoint without d(alpha) (adjoint = 1)
 // rmap: residual map (box as ymap), read only when a.residual is set (non-causal forward)
 cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap,

@@ -76,6 +76,10 @@ _SIGNATURES = {
     "cta_pde_step_bld": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                                  c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_int, c_int,
                                  c_void_p, c_void_p, c_int, c_void_p, c_int, c_int64, c_int64, c_void_p]),
+    "cta_diffusion_fwd_bld_pool_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "cta_diffusion_fwd_bld_pool": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
+                                           c_int64, c_int, c_int, POINTER(c_float), POINTER(c_void_p), c_int,
+                                           c_void_p, c_int, c_int64, c_int64, c_void_p]),
     "cta_diffusion_shard_bld_dalpha": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                                                c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                                                c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,

@@ -430,3 +430,31 @@ def pde_step(
         )
     _lib.check(rc)
     return y if grad_out is None else (y, dcoef)
+
+
+def bld_forward_pool(
+    x: torch.Tensor, alphas: Sequence[AlphaLike], steps: int, mask: torch.Tensor
+) -> torch.Tensor:
+    """`steps` fused non-causal steps on [B, L, D] under `mask`, followed by the
+    masked mean pool over L, without writing the stepped tensor: [B, D]."""
+    _require_cuda(x, "x")
+    if x.dim() != 3:
+        raise ValueError("x must have shape (B, L, D)")
+    x = _bld_view(x)
+    B, L, D = x.shape
+    fa, pa, pcode, keep = _alpha_args(alphas, steps, x.device)
+    m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
+    if m is None:
+        raise ValueError("the masked pool needs an attention mask")
+    lib = _lib.load()
+    pooled = torch.empty((B, D), dtype=x.dtype, device=x.device)
+    ws_bytes = int(lib.cta_diffusion_fwd_bld_pool_workspace_bytes(B, L, D))
+    ws = _workspace(x.device, ws_bytes, tag="pool")
+    with _lib.on_device(x):
+        rc = lib.cta_diffusion_fwd_bld_pool(
+            _lib.ptr(x), _lib.ptr(pooled), _lib.ptr(ws), ws_bytes, B, L, D, x.stride(0), x.stride(1),
+            _lib.dtype_code(x.dtype), steps, fa, pa, pcode, _lib.ptr(m), mcode, msb, msl, _lib.stream_ptr(x),
+        )
+    del keep
+    _lib.check(rc)
+    return pooled

@@ -41,6 +41,7 @@ __all__ = [
     "create_pde_layer",
     "diffusion_pde_stack",
     "diffusion_stack_function",
+    "diffusion_stack_pool",
 ]
 
 
@@ -107,6 +108,45 @@ class _StackBDL(torch.autograd.Function):
             else:
                 dalphas.append(None)
         return (dx if ctx.needs_input_grad[0] else None), None, None, *dalphas
+
+
+class _StackPoolBLD(torch.autograd.Function):
+    """The last refinement of the classifier and its masked mean pool
+    (src/models/transformers.py:120-139) in one forward pass over [B, L, D]."""
+
+    @staticmethod
+    def forward(ctx, x, mask, *alphas):
+        steps = len(alphas)
+        pooled = ops.bld_forward_pool(x, list(alphas), steps, mask)
+        ctx.steps = steps
+        ctx.save_for_backward(x, mask, *alphas)
+        return pooled
+
+    @staticmethod
+    def backward(ctx, gp):
+        x, mask, *alphas = ctx.saved_tensors
+        # the pool's gradient, in x's dtype as the reference's autograd forms it:
+        # d(sum) = gp / count, then d(y) = d(sum) * mask
+        count = torch.clamp(mask.sum(dim=1, keepdim=True), min=1)
+        g = ((gp.to(x.dtype) / count).unsqueeze(1) * mask.unsqueeze(-1)).to(x.dtype)
+        need_da = any(ctx.needs_input_grad[2:])
+        dx, da = ops.bld_backward(g, alphas, ctx.steps, x=x, causal=False, mask=mask, need_dalpha=need_da)
+        dalphas = [da[k : k + 1].reshape(a.shape).to(a.dtype) if ctx.needs_input_grad[2 + k] else None
+                   for k, a in enumerate(alphas)]
+        return (dx if ctx.needs_input_grad[0] else None), None, *dalphas
+
+
+def diffusion_stack_pool(x: torch.Tensor, layers: Sequence[nn.Module], attention_mask: torch.Tensor) -> torch.Tensor:
+    """``diffusion_pde_stack`` on [B, L, D] followed by the classifier's masked mean
+    pool, with the last up-to-8 steps and the pool fused into one pass (the
+    stepped tensor of those steps is never written).  Returns [B, D]."""
+    layers = list(layers)
+    mask = attention_mask.to(x.device) if attention_mask.device != x.device else attention_mask
+    alphas = [l.effective_alpha() for l in layers]
+    head = len(alphas) - ((len(alphas) - 1) % _lib.MAX_STEPS + 1)
+    if head > 0:
+        x = diffusion_stack_function(x, alphas[:head], layout="bld", causal=False, attention_mask=mask)
+    return _StackPoolBLD.apply(x, mask, *alphas[head:])
 
 
 def diffusion_stack_function(

@@ -14,7 +14,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from .pde_layers import _DiffusionFamilyLayer, create_pde_layer, diffusion_pde_stack
+from .pde_layers import _DiffusionFamilyLayer, create_pde_layer, diffusion_pde_stack, diffusion_stack_pool
 
 __all__ = ["generate_causal_mask", "PDETransformerClassifier", "PDETransformerLM"]
 
@@ -85,8 +85,13 @@ class PDETransformerClassifier(nn.Module):
         x = x + self.pos_encoder[:, :seq_len, :]
         x = self.dropout(x)
         padding_mask = attention_mask == 0
-        for transformer_layer, pde_list in zip(self.transformer_layers, self.pde_layers):
+        n = len(self.transformer_layers)
+        for i, (transformer_layer, pde_list) in enumerate(zip(self.transformer_layers, self.pde_layers)):
             x = transformer_layer(x, src_key_padding_mask=padding_mask)
+            if (i == n - 1 and self.pde_layout == "bld" and len(pde_list) > 0 and x.size(1) >= 3
+                    and all(isinstance(l, _DiffusionFamilyLayer) and not l.causal for l in pde_list)):
+                # the last refinement and the masked mean pool in one pass
+                return self.fc(diffusion_stack_pool(x, pde_list, attention_mask))
             x = _refine(x, pde_list, self.pde_layout, attention_mask)
         expanded_mask = attention_mask.unsqueeze(-1).expand(x.size())
         sum_embeddings = torch.sum(x * expanded_mask, dim=1)

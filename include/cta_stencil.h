@@ -164,6 +164,21 @@ int cta_diffusion_fwd_varlen_residual(const void* x, const void* residual, void*
                                       int64_t nseq, int64_t max_len, int pad_to_max, int dtype, int steps,
                                       float alpha, void* stream);
 
+/* The classifier's last refinement and its masked mean pool in one pass
+ * (src/models/transformers.py:120-139; no single counterpart in the
+ * reference): pooled[b, :] = sum_l mask[b, l] * y[b, l, :] / max(sum_l mask, 1)
+ * with y = `steps` fused non-causal steps of x under the same mask, y rounded to
+ * the tensor dtype as the stored tensor would hold it, and the sum and the
+ * division rounded to that dtype as the reference's half-precision ops do.  y
+ * is never written.  pooled: [B, D] contiguous, x's dtype.  workspace: fp32
+ * scratch of cta_diffusion_fwd_bld_pool_workspace_bytes(B, L, D) bytes (16-byte
+ * aligned, no zeroing).  Two launches. */
+int64_t cta_diffusion_fwd_bld_pool_workspace_bytes(int64_t B, int64_t L, int64_t D);
+int cta_diffusion_fwd_bld_pool(const void* x, void* pooled, void* workspace, int64_t workspace_bytes, int64_t B,
+                               int64_t L, int64_t D, int64_t x_sB, int64_t x_sL, int dtype, int steps,
+                               const float* alpha, const void* const* alpha_dev, int alpha_dev_dtype,
+                               const void* mask, int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream);
+
 /* The dense [B, L, D] form of cta_diffusion_fwd_varlen_residual (mask allowed,
  * host alphas, non-causal). */
 int cta_diffusion_fwd_bld_residual(const void* x, const void* residual, void* y, int64_t B, int64_t L, int64_t D,

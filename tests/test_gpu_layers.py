@@ -270,3 +270,44 @@ def test_pde_transformer_other_pde_types(pde_type):
         for plist in net.pde_layers:
             for p in plist:
                 assert torch.isfinite(p.alpha.grad).all() and torch.isfinite(p.beta.grad).all()
+
+
+# ---------------------------------------------------------------------------
+# the classifier's last refinement fused with its masked mean pool
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("steps", [1, 4, 8, 11])
+@pytest.mark.parametrize("shape", [(3, 1000, 512), (2, 77, 264), (4, 40, 6)])
+def test_stack_pool_matches_stack_then_pool(dtype, steps, shape):
+    """pooled = masked mean of the stepped tensor (never written), against the
+    stack followed by the reference's pooling; gradients through both paths."""
+    from cta_b200 import ops
+    from cta_b200.pde_layers import DiffusionPDELayer, diffusion_pde_stack, diffusion_stack_pool
+
+    torch.manual_seed(30 + steps)
+    B, L, D = shape
+    x = torch.randn(B, L, D, device="cuda").to(dtype)
+    mask = torch.ones(B, L, dtype=torch.long, device="cuda")
+    mask[0, L - L // 3 :] = 0
+    mask[-1, : L // 5] = 0
+    layers = [DiffusionPDELayer(D, alpha_init=0.1 - 0.005 * k, layout="bld").cuda() for k in range(steps)]
+
+    def reference(t):
+        y = diffusion_pde_stack(t, layers, attention_mask=mask)
+        s = torch.sum(y * mask.unsqueeze(-1).expand(y.size()), dim=1)
+        return s / torch.clamp(mask.sum(dim=1, keepdim=True), min=1)
+
+    xa = x.clone().requires_grad_(True)
+    xb = x.clone().requires_grad_(True)
+    pa = diffusion_stack_pool(xa, layers, mask)
+    pb = reference(xb)
+    assert pa.dtype == pb.dtype and pa.shape == (B, D)
+    assert_close(pa, pb)
+    g = torch.randn(B, D, device="cuda").to(dtype)
+    da = torch.autograd.grad((pa.float() * g.float()).sum(), [xa] + [l.alpha for l in layers])
+    db = torch.autograd.grad((pb.float() * g.float()).sum(), [xb] + [l.alpha for l in layers])
+    assert torch.equal(da[0], db[0])  # the same pooled gradient through the same backward kernels
+    for u, v in zip(da[1:], db[1:]):
+        assert torch.equal(u, v)
+    with pytest.raises(ValueError):
+        ops.bld_forward_pool(x, [0.1], 1, None)
