@@ -566,7 +566,10 @@ def run_kernels(args, rank, world, local_rank):
                                                              need_dalpha=True, out=ys[i % 2]),
             "bdl_forward": lambda i: ops.bdl_simple(xt[i % 2], 0.1, S, out=yt[i % 2]),
             "bdl_adjoint": lambda i: ops.bdl_simple(xt[i % 2], 0.1, S, backward=True, out=yt[i % 2]),
+            "bld_forward_pool": lambda i: ops.bld_forward_pool(xs[i % 2], [0.1] * S, S, pmask),
         }
+        pmask = torch.ones(1, L, dtype=torch.long, device=dev)
+        pmask[:, L - L // 8 :] = 0
         fn = calls[args.kernel]
         for i in range(args.warmup):
             fn(i)
@@ -644,7 +647,8 @@ def main() -> None:
                          "block: PDE-Transformer LM fwd+bwd; sharded: L=1M x 4096 split over the ranks; "
                          "kernels: per-kernel timing table")
     ap.add_argument("--kernel", default="bld_forward",
-                    choices=["bld_forward", "bld_adjoint", "bld_adjoint_dalpha", "bdl_forward", "bdl_adjoint"],
+                    choices=["bld_forward", "bld_adjoint", "bld_adjoint_dalpha", "bdl_forward", "bdl_adjoint",
+                             "bld_forward_pool"],
                     help="with --workload kernels --mode kernel: the one kernel to launch")
     ap.add_argument("--mode", choices=["full", "kernel"], default="full",
                     help="kernel: only warmup + timed launches of the fused kernel (for ncu)")

@@ -123,8 +123,11 @@ struct RowBits {
   }
 };
 
+// pool_bits (optional, same word layout as fbits): bit set where row j is inside
+// the segment and its mask entry is valid
 template <bool CAUSAL, int NWARPS = kBldThreads / 32>
-__device__ __forceinline__ bool build_row_bits(const BldArgs& a, const Seg& sg, RowBits rb, int nwords) {
+__device__ __forceinline__ bool build_row_bits(const BldArgs& a, const Seg& sg, RowBits rb, int nwords,
+                                               uint32_t* pool_bits = nullptr) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t any = 0;
   if (threadIdx.x == 0) {
@@ -138,6 +141,12 @@ __device__ __forceinline__ bool build_row_bits(const BldArgs& a, const Seg& sg, 
     if (lane == 0) {
       rb.fbits[w + 1] = fm;
       rb.zbits[w + 1] = zm;
+    }
+    if (pool_bits != nullptr) {
+      const bool pv = j >= 0 && j < sg.n &&
+                      mask_valid(a.mask, a.mask_dtype, static_cast<int64_t>(sg.bcoord) * a.msB + j * a.msL);
+      const uint32_t pm = __ballot_sync(0xffffffffu, pv);
+      if (lane == 0) pool_bits[w + 1] = pm;
     }
     any |= fm | zm;
   }

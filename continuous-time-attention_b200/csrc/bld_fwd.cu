@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   T* stage = ring + kFwdStages * CHUNK;  // output staging for the TMA stores
   __shared__ __align__(8) uint64_t full_bar[kFwdStages];
   __shared__ __align__(8) uint64_t res_bar[RES ? 2 : 1];
-  __shared__ uint32_t pbits[POOL ? kBldMaxWords : 1];  // POOL: mask bits of the tile's output rows
+  __shared__ uint32_t pbits[POOL ? kBldMaxWords + 2 : 1];  // POOL: mask bits of the march rows
   __shared__ uint32_t fbits[kBldMaxWords + 2];
   __shared__ uint32_t zbits[kBldMaxWords + 2];
 
@@ -200,17 +200,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
     for (int c = 0; c < nch && c < kFwdStages; ++c) issue(c);
   }
   RowBits rb{fbits, zbits, jb};
-  const bool slow = build_row_bits<CAUSAL, 1>(a, sg, rb, (nch * kFwdRC + 31) / 32);
-  if constexpr (POOL) {
-    // bit r of word w: mask of output row l0 + 32 w + r (read once per tile)
-    for (int w = 0; w < (nout + 31) / 32; ++w) {
-      const int64_t r = l0 + 32 * w + tid;
-      const bool v = r < oend && mask_valid(a.mask, a.mask_dtype, static_cast<int64_t>(sg.bcoord) * a.msB + r * a.msL);
-      const uint32_t m = __ballot_sync(0xffffffffu, v);
-      if (tid == 0) pbits[w] = m;
-    }
-    __syncwarp();
-  }
+  const bool slow = build_row_bits<CAUSAL, 1>(a, sg, rb, (nch * kFwdRC + 31) / 32, POOL ? pbits : nullptr);
 
   float alf[kMaxSteps];
   load_alphas(a, alf, S);
@@ -246,8 +236,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   pf2 pool_a = 0ull, pool_b = 0ull;  // POOL: masked column sums of this lane
   auto store_row = [&](int64_t orow, pf2 pa, pf2 pb) {
     if constexpr (POOL) {
-      const int64_t rr = orow - l0;
-      if (col_ok && ((pbits[rr >> 5] >> (rr & 31)) & 1u)) {
+      const int64_t p = orow - jb + 32;  // fbits layout: word 0 is the guard word
+      if (col_ok && ((pbits[p >> 5] >> (p & 31)) & 1u)) {
         pf2 ra, rb2;
         Q::split(Q::join(pa, pb), ra, rb2);  // the values the stored tensor would hold
         pool_a = padd(pool_a, ra);
@@ -484,12 +474,17 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
 #pragma unroll
     for (int j = 0; j < kFwdVec; ++j)
       if (col + j < a.D) pp[col + j] = ok ? v[j] : 0.f;
-    if (dtile == 0 && tid == 0) {
+    if (dtile == 0) {
       // valid rows of this tile, after the nbatch * ntl * D partials (exact in fp32)
       int n = 0;
-      for (int w = 0; w < (nout + 31) / 32; ++w) n += __popc(pbits[w]);
-      a.pool_partial[(static_cast<int64_t>(a.nbatch) * ntl) * a.D + static_cast<int64_t>(sg.bcoord) * ntl +
-                     blockIdx.x / ndt] = static_cast<float>(n);
+      for (int r0 = 0; r0 < nout; r0 += 32) {
+        const int64_t p = l0 + r0 + tid - jb + 32;
+        const bool v = r0 + tid < nout && ((pbits[p >> 5] >> (p & 31)) & 1u);
+        n += __popc(__ballot_sync(0xffffffffu, v));
+      }
+      if (tid == 0)
+        a.pool_partial[(static_cast<int64_t>(a.nbatch) * ntl) * a.D + static_cast<int64_t>(sg.bcoord) * ntl +
+                       blockIdx.x / ndt] = static_cast<float>(n);
     }
   }
 }
@@ -502,6 +497,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
 // Every order depends on the shape alone, so the result is deterministic.
 template <typename T>
 __global__ void __launch_bounds__(kPoolThreads) pool_finish_kernel(const BldArgs a, int64_t ntl, void* pooled) {
+  // launched as a programmatic dependent of the march: wait for its partials
+  pdl_wait();
   constexpr int NW = kPoolThreads / 32;
   __shared__ double part[NW][33];
   __shared__ double cnt[NW];
@@ -639,14 +636,25 @@ cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUte
 }
 
 cudaError_t launch_pool_finish(const BldArgs& a, int dtype, int64_t ntl, void* pooled, cudaStream_t st) {
-  const dim3 grid(static_cast<unsigned>((a.D + 31) / 32), static_cast<unsigned>(a.nbatch));
-  switch (dtype) {
-    case kF32: pool_finish_kernel<float><<<grid, kPoolThreads, 0, st>>>(a, ntl, pooled); break;
-    case kBF16: pool_finish_kernel<__nv_bfloat16><<<grid, kPoolThreads, 0, st>>>(a, ntl, pooled); break;
-    case kF16: pool_finish_kernel<__half><<<grid, kPoolThreads, 0, st>>>(a, ntl, pooled); break;
-    default: return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  const void* kern = dtype == kF32    ? reinterpret_cast<const void*>(&pool_finish_kernel<float>)
+                     : dtype == kBF16 ? reinterpret_cast<const void*>(&pool_finish_kernel<__nv_bfloat16>)
+                     : dtype == kF16  ? reinterpret_cast<const void*>(&pool_finish_kernel<__half>)
+                                      : nullptr;
+  if (kern == nullptr) return cudaErrorInvalidValue;
+  // programmatic dependent launch: the launch overlaps the march's tail and the
+  // kernel's griddepcontrol.wait holds it until the march's partials are visible
+  void* args[] = {const_cast<BldArgs*>(&a), &ntl, &pooled};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((a.D + 31) / 32), static_cast<unsigned>(a.nbatch));
+  cfg.blockDim = dim3(kPoolThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
 int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual) {

@@ -58,6 +58,18 @@ def test_invalid_arguments_fail_before_launch():
                                      7, 0, 2, 0, 0, ctypes.c_float(0.1), null)
     assert rc == _lib.CTA_EINVAL
     assert lib.cta_diffusion_bwd_bld_workspace_bytes(1, 16384, 512, 1, 4, 0) >= 256 + 4 * 4 * 512
+    # the pooled classifier form: per row tile (>= 32 rows) D column sums + one count
+    assert lib.cta_diffusion_fwd_bld_pool_workspace_bytes(2, 1000, 64) >= 4 * 32 * 2 * 65
+    assert lib.cta_diffusion_fwd_bld_pool_workspace_bytes(0, 1000, 64) == 256
+    x16 = ctypes.c_void_p(16)
+    # no mask: the pooled form is the masked mean
+    rc = lib.cta_diffusion_fwd_bld_pool(x16, x16, x16, 1 << 20, 1, 100, 8, 800, 8, 1, 2, one, None, 0, null, 0,
+                                        0, 0, null)
+    assert rc == _lib.CTA_EINVAL and b"mask" in lib.cta_last_error()
+    # workspace below the size query
+    rc = lib.cta_diffusion_fwd_bld_pool(x16, x16, x16, 64, 1, 100, 8, 800, 8, 1, 2, one, None, 0, x16, 2, 100, 1,
+                                        null)
+    assert rc == _lib.CTA_EINVAL and b"workspace" in lib.cta_last_error()
 
 
 def test_python_errors_without_gpu():
