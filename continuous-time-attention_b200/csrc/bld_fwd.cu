@@ -201,6 +201,31 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   }
   RowBits rb{fbits, zbits, jb};
   const bool slow = build_row_bits<CAUSAL, 1>(a, sg, rb, (nch * kFwdRC + 31) / 32, POOL ? pbits : nullptr);
+  if constexpr (POOL) {
+    // a tile whose output rows are all masked out adds nothing to the pool:
+    // zero partials and count, drain the loads already issued, and leave
+    uint32_t anyv = 0u;
+    for (int r0 = 0; r0 < nout; r0 += 32) {
+      const int64_t p = l0 + r0 + tid - jb + 32;
+      anyv |= __ballot_sync(0xffffffffu, r0 + tid < nout && ((pbits[p >> 5] >> (p & 31)) & 1u));
+    }
+    if (anyv == 0u) {
+      if (use_tma && tid == 0)
+        for (int c = 0; c < nch && c < kFwdStages; ++c)
+          if (!mbar_wait_bounded(&full_bar[c], 0)) atomicExch(&g_bld_fwd_error, kDevTimeout);
+      const int64_t ntl = gridDim.x / ndt;
+      float* pp = a.pool_partial + ((static_cast<int64_t>(sg.bcoord) * ntl + blockIdx.x / ndt) * a.D);
+      const int col0 = d0 + tid * kFwdVec;
+#pragma unroll
+      for (int j = 0; j < kFwdVec; ++j)
+        if (col0 + j < a.D) pp[col0 + j] = 0.f;
+      if (dtile == 0 && tid == 0)
+        a.pool_partial[(static_cast<int64_t>(a.nbatch) * ntl) * a.D + static_cast<int64_t>(sg.bcoord) * ntl +
+                       blockIdx.x / ndt] = 0.f;
+      __syncwarp();
+      return;
+    }
+  }
 
   float alf[kMaxSteps];
   load_alphas(a, alf, S);
