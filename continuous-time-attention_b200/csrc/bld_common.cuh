@@ -64,35 +64,6 @@ __device__ __forceinline__ bool row_zero(const BldArgs& a, const Seg& s, int64_t
   return a.pad_to_max && j >= s.n && j < s.gdom;
 }
 
-// Fill one pipeline chunk with plain loads (any alignment / stride, halo rows
-// from neighbour shards).  Used when TMA cannot address the tensor.
-template <typename T>
-__device__ void fill_chunk_generic(const BldArgs& a, const void* src, int64_t sB, int64_t sL, const Seg& s,
-                                   int64_t jrow0, int d0, T* dst) {
-  const T zero = Elem<T>::from_f(0.f);
-  for (int idx = threadIdx.x; idx < kBldRC * (kBldDT / 2); idx += kBldThreads) {
-    const int i = idx / (kBldDT / 2);
-    const int cp = (idx - i * (kBldDT / 2)) * 2;
-    const int64_t tr = s.row0 + jrow0 + i;
-    const int col = d0 + cp;
-    const T* rowp = nullptr;
-    if (tr >= 0 && tr < a.L) {
-      rowp = static_cast<const T*>(src) + static_cast<int64_t>(s.bcoord) * sB + tr * sL;
-    } else if (tr < 0 && a.lo_ext != nullptr && tr >= -a.hext_lo) {
-      rowp = static_cast<const T*>(a.lo_ext) + (static_cast<int64_t>(s.bcoord) * a.hext_lo + (a.hext_lo + tr)) * a.D;
-    } else if (tr >= a.L && a.hi_ext != nullptr && tr - a.L < a.hext_hi) {
-      rowp = static_cast<const T*>(a.hi_ext) + (static_cast<int64_t>(s.bcoord) * a.hext_hi + (tr - a.L)) * a.D;
-    }
-    T v0 = zero, v1 = zero;
-    if (rowp != nullptr) {
-      if (col < a.D) v0 = rowp[col];
-      if (col + 1 < a.D) v1 = rowp[col + 1];
-    }
-    dst[i * kBldDT + cp] = v0;
-    dst[i * kBldDT + cp + 1] = v1;
-  }
-}
-
 // Bitmap of fixed / zero rows for rows [jbits, jbits + 32*nwords).  Word 0 is
 // a guard word of ones so that "row - 1 .. row - 8" never indexes below it.
 struct RowBits {
@@ -125,7 +96,7 @@ struct RowBits {
 
 // pool_bits (optional, same word layout as fbits): bit set where row j is inside
 // the segment and its mask entry is valid
-template <bool CAUSAL, int NWARPS = kBldThreads / 32>
+template <bool CAUSAL, int NWARPS = 1>
 __device__ __forceinline__ bool build_row_bits(const BldArgs& a, const Seg& sg, RowBits rb, int nwords,
                                                uint32_t* pool_bits = nullptr) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

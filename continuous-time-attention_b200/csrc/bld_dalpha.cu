@@ -1,4 +1,4 @@
-// Fused backward WITH d(alpha) on [B, L, D] hidden states, steps 1..4: the
+// Fused backward WITH d(alpha) on [B, L, D] hidden states, steps 1..8: the
 // one-warp march of bld_fwd.cu carrying two wavefronts at once.
 //
 // Gradient of one step u_k = A_k u_{k-1} (copy boundary, mask, per-step
@@ -9,18 +9,22 @@
 //     causal      g_{k-1}[i] = g_k[i] + (a[i] - 2 a[i+1]) + a[i+2]
 //   d(alpha_k) = sum over updated rows i of g_k[i] * lap(u_{k-1})[i]
 //
-// Work decomposition.  A CTA is one warp owning TL output rows x 128 columns;
-// each lane owns 4 columns (two packed fp32 pairs).  Two input streams arrive
+// Work decomposition.  A CTA is one warp owning TL output rows x kDaDT columns;
+// each lane owns kDaPairs packed fp32 column pairs (one by default: 64-column
+// tiles, so that the two wavefronts of a lane fit in half the registers of two
+// pairs and twice as many warps stay resident).  Two input streams arrive
 // through their own TMA rings, 8 rows per chunk: the gradient g (entering the
 // adjoint wavefront as level S) and the forward input x (entering a
 // recomputation of the forward levels u_0 .. u_{S-1}).  One march step
 // advances both wavefronts by one row.  The adjoint of level k meets
 // lap(u_{k-1}) of the same row a fixed number of march steps earlier or later
 // (the forward wavefront lags one row per level, the adjoint one leads), so
-// the earlier factor waits in a register delay line.  The x stream starts
-// DX rows after the g stream, with DX chosen so that every delay length is 0,
-// 1, 2 or 4: a delay line is then a circular buffer whose slot is the row's
-// position in the 8-row chunk, known at compile time, and costs no moves.
+// the earlier factor waits in a delay line.  The x stream starts DX rows after
+// the g stream, which keeps every delay within 8 march steps.  A delay of 1, 2
+// or 4 is a register ring whose slot is the row's position in the 8-row chunk,
+// known at compile time, so it costs no moves; the other delays (3, 5, 6, 7 or
+// 8, at steps 6..8) use an 8-slot ring per lane in shared memory, written at
+// slot I and read at slot (I - delay) mod 8, again known at compile time.
 //
 // d(alpha) is reduced deterministically: lane sums -> warp shuffle tree (fixed
 // order) -> one partial per CTA -> the last CTA of each group (32 CTAs, or a
@@ -49,15 +53,27 @@ struct DaGeom {
   // march steps by which lap(u_{k-1}) of a row arrives before g_k of that row
   // (negative: g_k arrives first)
   static constexpr int delay(int k) { return CAUSAL ? DX + 2 * (S - k) : DX + S - 2 * k; }
+  static constexpr int adelay(int k) { return delay(k) < 0 ? -delay(k) : delay(k); }
   // the pair (g_k, lap(u_{k-1})) completed at march step t belongs to output row
   // l0 + t - PRO + e(k)
   static constexpr int e(int k) {
     return CAUSAL ? (2 * k < 2 * S + DX ? 2 * k : 2 * S + DX) : (k < S + DX - k ? k : S + DX - k);
   }
+  // delays of 1, 2 or 4 march steps divide the 8-row chunk: the delay line is a
+  // register ring indexed by the row's place in the chunk (no moves).  Longer
+  // or odd delays (3..8) use an 8-slot ring in shared memory, written at slot I
+  // and read at slot (I - delay) mod 8, both known at compile time.
+  static constexpr bool reg_ring(int k) { return adelay(k) == 1 || adelay(k) == 2 || adelay(k) == 4; }
+  static constexpr bool smem_ring(int k) { return adelay(k) != 0 && !reg_ring(k); }
+  static constexpr int smem_index(int k) {
+    int n = 0;
+    for (int j = 1; j < k; ++j) n += smem_ring(j) ? 1 : 0;
+    return n;
+  }
+  static constexpr int n_smem_rings() { return smem_index(S + 1); }
   static constexpr bool delays_ok() {
     for (int k = 1; k <= S; ++k) {
-      const int d = delay(k) < 0 ? -delay(k) : delay(k);
-      if (!(d == 0 || d == 1 || d == 2 || d == 4)) return false;
+      if (adelay(k) > kFwdRC) return false;
       if (e(k) < 0) return false;
     }
     return true;
@@ -66,24 +82,28 @@ struct DaGeom {
 
 template <typename T>
 constexpr int da_stages() {
-  return sizeof(T) == 4 ? 2 : 3;
+  return sizeof(T) == 4 ? 3 : 4;
 }
 
-template <typename T>
+constexpr int kDaChunk = kFwdRC * kDaDT;  // elements per stream and pipeline slot
+constexpr int kDaRingBytes = kFwdRC * kDaPairs * 32 * 8;  // one 8-slot shared-memory delay ring
+
+template <typename T, int S, bool CAUSAL>
 constexpr size_t da_smem() {
-  return static_cast<size_t>(2 * da_stages<T>() + kFwdOutSlots) * kFwdRC * kFwdDT * sizeof(T);
+  return static_cast<size_t>(2 * da_stages<T>() + kFwdOutSlots) * kDaChunk * sizeof(T) +
+         static_cast<size_t>(DaGeom<S, CAUSAL>::n_smem_rings()) * kDaRingBytes;
 }
 
-// Plain-load fill of one chunk ([8][128]) of a [B, L, D] stream, for tensors
+// Plain-load fill of one chunk ([8][kDaDT]) of a [B, L, D] stream, for tensors
 // TMA cannot address and for L-shard edges: rows before / after the local
 // shard come from the halo buffers lo / hi ([nbatch, nlo|nhi, D]), if given.
 template <typename T>
 __device__ void fill_da_chunk(const BldArgs& a, const void* src, int64_t sB, int64_t sL, const void* lo, int nlo,
                               const void* hi, int nhi, const Seg& s, int64_t jrow0, int d0, T* dst) {
   const T zero = Elem<T>::from_f(0.f);
-  for (int idx = threadIdx.x; idx < kFwdRC * kFwdDT; idx += kFwdThreads) {
-    const int i = idx / kFwdDT;
-    const int cc = idx - i * kFwdDT;
+  for (int idx = threadIdx.x; idx < kDaChunk; idx += kFwdThreads) {
+    const int i = idx / kDaDT;
+    const int cc = idx - i * kDaDT;
     const int64_t tr = s.row0 + jrow0 + i;
     const int col = d0 + cc;
     const T* rowp = nullptr;
@@ -94,18 +114,21 @@ __device__ void fill_da_chunk(const BldArgs& a, const void* src, int64_t sB, int
     } else if (tr >= a.L && hi != nullptr && tr - a.L < nhi) {
       rowp = static_cast<const T*>(hi) + (static_cast<int64_t>(s.bcoord) * nhi + (tr - a.L)) * a.D;
     }
-    dst[i * kFwdDT + cc] = (rowp != nullptr && col < a.D) ? rowp[col] : zero;
+    dst[i * kDaDT + cc] = (rowp != nullptr && col < a.D) ? rowp[col] : zero;
   }
 }
 
 }  // namespace
 
-// Register budget: two wavefronts, the delay lines and the S laps of a row in
-// flight need up to ~200 registers at steps 4 (resident CTAs per SM from
-// ptxas -v without spills: 16 up to steps 2, 12 at steps 3, 8 beyond)
+// Register budget (one packed pair per lane): forward and adjoint state of S
+// levels, the register delay rings and the S laps of a row in flight.  The
+// minimum resident one-warp CTAs per SM handed to __launch_bounds__ is the
+// largest at which ptxas -v shows no spills for every dtype and direction.
 template <typename T, int S, bool CAUSAL>
 constexpr int da_min_ctas() {
-  return S <= 2 ? 16 : (S == 3 && !(CAUSAL && sizeof(T) == 4)) ? 12 : 8;
+  // ptxas budgets registers per SM sub-partition (16384 each, warps spread over
+  // 4), so 10 or 12 CTAs both cap a lane at 168 registers and 8 at 255
+  return S <= 2 ? 24 : S == 3 ? 16 : S == 4 ? (CAUSAL ? 12 : 16) : S == 5 ? 12 : (S == 6 && !CAUSAL) ? 12 : 8;
 }
 
 // KIND 1 / 2 (steps 1 only): the backward of one advection- / reaction-
@@ -144,42 +167,45 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
                       const __grid_constant__ CUtensorMap ymap, const BldArgs a) {
   static_assert(KIND == 0 || S == 1, "the other PDE kinds are single steps");
   constexpr int NV = S + (KIND != 0 ? 1 : 0);  // reduced values: d(alpha_k) [, d(beta)]
-  using Q = ColVec<T, kFwdVec>;
+  constexpr int NP = kDaPairs;                 // packed column pairs per lane
+  using Q = ColVec<T, 2 * NP>;
   using V = typename Q::V;
   using G = DaGeom<S, CAUSAL>;
   constexpr int NST = da_stages<T>();
-  constexpr int CHUNK = kFwdRC * kFwdDT;
+  constexpr int CHUNK = kDaChunk;
   constexpr int PRO = G::PRO;
   constexpr int NPRO = G::NPRO;
-  static_assert(kFwdVec == 4, "two packed pairs per lane");
-  static_assert(NPRO >= 1 && NPRO <= 2, "prologue spans one or two chunks");
-  static_assert(G::delays_ok(), "delay lines must divide the chunk");
+  constexpr int NSR = G::n_smem_rings();
+  static_assert(NP == 1 || NP == 2, "one or two packed pairs per lane");
+  static_assert(NPRO >= 1 && NPRO <= 3, "prologue spans one to three chunks");
+  static_assert(G::delays_ok(), "delays must fit an 8-slot ring");
   static_assert(CAUSAL || G::DX <= G::PAD, "x stream must start S rows above the tile");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   T* gring = reinterpret_cast<T*>(smem_raw);
   T* xring = gring + NST * CHUNK;
   T* stage = xring + NST * CHUNK;
+  pf2* dring = reinterpret_cast<pf2*>(stage + kFwdOutSlots * CHUNK);  // [NSR][8][NP][32]
   __shared__ __align__(8) uint64_t full_bar[NST];
   __shared__ uint32_t fbits[kBldMaxWords + 2];
   __shared__ uint32_t zbits[kBldMaxWords + 2];
 
   const Seg sg = resolve_seg(a, blockIdx.z);
-  const int ndt = (a.D + kFwdDT - 1) / kFwdDT;
+  const int ndt = (a.D + kDaDT - 1) / kDaDT;
   const int dtile = static_cast<int>(blockIdx.x % ndt);
   const int64_t l0 = a.out_begin + static_cast<int64_t>(blockIdx.x / ndt) * a.TL;
   const int64_t oend = a.out_end < sg.n ? a.out_end : sg.n;
   const int cta_id = blockIdx.x + gridDim.x * blockIdx.z;
   const int tid = threadIdx.x;
   const bool active = l0 < oend;
-  const int d0 = dtile * kFwdDT;
+  const int d0 = dtile * kDaDT;
   const int64_t jbg = l0 - G::HLG - G::PAD;  // first g row of the march
   const int64_t jbx = jbg + G::DX;           // first x row of the march
   const int nout = active ? static_cast<int>(oend - l0 < a.TL ? oend - l0 : a.TL) : 0;
   const int nrows = PRO + nout;
   const int nch = active ? (nrows + kFwdRC - 1) / kFwdRC : 0;
   const bool use_tma = a.use_tma != 0;
-  const bool tstore = a.use_tma_store != 0;
+  const bool tstore = a.use_tma_store != 0 && kFwdOutSlots > 0;
 
   pf2 acc[NV];
 #pragma unroll
@@ -208,6 +234,8 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     if (use_tma && tid == 0) {
       for (int c = 0; c < nch && c < NST; ++c) issue(c);
     }
+    // the shared-memory delay rings start at zero, as the register ones do
+    for (int i = tid; i < NSR * kFwdRC * NP * 32; i += 32) dring[i] = 0ull;
     const int64_t jbits = jbg < jbx ? jbg : jbx;
     const int span = (G::DX < 0 ? -G::DX : G::DX) + nch * kFwdRC;
     RowBits rb{fbits, zbits, jbits};
@@ -225,203 +253,191 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     const pf2 be = pbc(KIND == 0 ? 0.f
                                  : (a.alpha_dev[1] != nullptr ? load_scalar(a.alpha_dev[1], a.alpha_dev_dtype)
                                                               : a.alpha[1]));
-    pf2 Q1a = 0ull, Q1b = 0ull, Q2a = 0ull, Q2b = 0ull;
+    pf2 Q1[NP], Q2[NP];
     // reaction: sigmoid of the paired row, kept for the rows the adjoint finishes later
-    pf2 S1a = 0ull, S1b = 0ull, S2a = 0ull, S2b = 0ull;
-
+    pf2 S1[NP], S2[NP];
     // adjoint state per level m (forward step k = S - m): a = alpha*g on the two
     // previous rows (P1, P2), g on the one or two previous rows (G1, G2)
-    pf2 P1a[S], P2a[S], P1b[S], P2b[S], G1a[S], G1b[S], G2a[S], G2b[S];
+    pf2 P1[S][NP], P2[S][NP], G1[S][NP], G2[S][NP];
     // forward recomputation, level q: u_q on the two previous rows
-    pf2 F1a[S], F2a[S], F1b[S], F2b[S];
-    // delay lines, one per step k (the earlier of its two factors)
-    pf2 DLa[S][4], DLb[S][4];
+    pf2 F1[S][NP], F2[S][NP];
+    // register delay rings, one per step k whose delay is 1, 2 or 4 (the earlier of its two factors)
+    pf2 DL[S][4][NP];
 #pragma unroll
-    for (int k = 0; k < S; ++k) {
-      P1a[k] = P2a[k] = P1b[k] = P2b[k] = G1a[k] = G1b[k] = G2a[k] = G2b[k] = 0ull;
-      F1a[k] = F2a[k] = F1b[k] = F2b[k] = 0ull;
+    for (int p = 0; p < NP; ++p) {
+      Q1[p] = Q2[p] = S1[p] = S2[p] = 0ull;
 #pragma unroll
-      for (int d = 0; d < 4; ++d) DLa[k][d] = DLb[k][d] = 0ull;
+      for (int k = 0; k < S; ++k) {
+        P1[k][p] = P2[k][p] = G1[k][p] = G2[k][p] = F1[k][p] = F2[k][p] = 0ull;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) DL[k][d][p] = 0ull;
+      }
     }
 
-    const int cb = tid * kFwdVec;
+    const int cb = tid * 2 * NP;
     const int col = d0 + cb;
     const bool col_ok = col < a.D;
-    const bool quad_ok = a.y_quad_ok != 0 && col + kFwdVec - 1 < a.D;
+    const bool vec_ok = a.y_quad_ok != 0 && col + 2 * NP - 1 < a.D;
     T* const ybase = static_cast<T*>(a.y) + static_cast<int64_t>(sg.bcoord) * a.ysB + sg.row0 * a.ysL + col;
 
-    auto store_row = [&](int64_t orow, pf2 pa, pf2 pb) {
+    auto store_row = [&](int64_t orow, const pf2* v) {
       T* yp = ybase + orow * a.ysL;
-      if (quad_ok) {
-        *reinterpret_cast<V*>(yp) = Q::join(pa, pb);
+      if (vec_ok) {
+        *reinterpret_cast<V*>(yp) = Q::join(v[0], NP > 1 ? v[NP - 1] : 0ull);
       } else if (col_ok) {
-        float v[4];
-        upk(pa, v[0], v[1]);
-        upk(pb, v[2], v[3]);
+        float f[4];
+        upk(v[0], f[0], f[1]);
+        if (NP > 1) upk(v[NP - 1], f[2], f[3]);
 #pragma unroll
-        for (int j = 0; j < kFwdVec; ++j)
-          if (col + j < a.D) yp[j] = Elem<T>::from_f(v[j]);
+        for (int j = 0; j < 2 * NP; ++j)
+          if (col + j < a.D) yp[j] = Elem<T>::from_f(f[j]);
       }
     };
 
     // One march row: TCT >= 0 is the compile-time march row of a prologue row
     // (start-up triangles of both wavefronts skipped); I the row in its chunk;
     // lim = nout + PRO - (first march row of the chunk).
-    auto step_row = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, pf2& ga, pf2& gb, pf2 xa,
-                        pf2 xb) {
+    auto step_row = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, pf2* g, pf2* x) {
       constexpr bool SLOW = decltype(slow_tag)::value;
       constexpr int TCT = decltype(tct_tag)::value;
       constexpr int I = decltype(i_tag)::value;
       const int64_t jg = jbg + t, jx = jbx + t;
       if (SLOW) {
-        if (rb.zero(jg)) ga = gb = 0ull;
-        if (rb.zero(jx)) xa = xb = 0ull;
+        if (rb.zero(jg))
+#pragma unroll
+          for (int p = 0; p < NP; ++p) g[p] = 0ull;
+        if (rb.zero(jx))
+#pragma unroll
+          for (int p = 0; p < NP; ++p) x[p] = 0ull;
       }
       // ---- KIND 1/2: the beta term h(x) of the paired row and, for reaction,
       // f'(x) of the row the adjoint finishes (from the window before its shift) ----
-      pf2 ha = 0ull, hb = 0ull, fpa = 0ull, fpb = 0ull;
-      if constexpr (KIND == 1) {
-        ha = CAUSAL ? pfma(F1a[0], n1, xa) : pmul(pfma(F2a[0], n1, xa), half);
-        hb = CAUSAL ? pfma(F1b[0], n1, xb) : pmul(pfma(F2b[0], n1, xb), half);
-      } else if constexpr (KIND == 2) {
-        // the paired row is jg; the finished row jg-1 (causal jg-2), whose x is
-        // F2 and whose sigmoid was taken one (two) march steps ago
-        const pf2 ca_ = CAUSAL ? xa : F1a[0], cb_ = CAUSAL ? xb : F1b[0];
-        const pf2 sa = psigmoid(ca_), sb = psigmoid(cb_);
-        ha = reaction_f(ca_, sa);
-        hb = reaction_f(cb_, sb);
-        fpa = reaction_df(F2a[0], CAUSAL ? S2a : S1a);
-        fpb = reaction_df(F2b[0], CAUSAL ? S2b : S1b);
-        S2a = S1a;
-        S2b = S1b;
-        S1a = sa;
-        S1b = sb;
+      pf2 h[NP], fp[NP];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        h[p] = fp[p] = 0ull;
+        if constexpr (KIND == 1) {
+          h[p] = CAUSAL ? pfma(F1[0][p], n1, x[p]) : pmul(pfma(F2[0][p], n1, x[p]), half);
+        } else if constexpr (KIND == 2) {
+          // the paired row is jg; the finished row jg-1 (causal jg-2), whose x is
+          // F2 and whose sigmoid was taken one (two) march steps ago
+          const pf2 c_ = CAUSAL ? x[p] : F1[0][p];
+          const pf2 sv = psigmoid(c_);
+          h[p] = reaction_f(c_, sv);
+          fp[p] = reaction_df(F2[0][p], CAUSAL ? S2[p] : S1[p]);
+          S2[p] = S1[p];
+          S1[p] = sv;
+        }
       }
       // ---- forward recomputation: lap(u_q) of this march row, q = 0..S-1 ----
-      pf2 la[S], lb[S];
+      pf2 la[S][NP];
       {
         const bool fxc = SLOW && CAUSAL && rb.fixed(jx);
         const uint32_t fwx = (SLOW && !CAUSAL) ? rb.window8_fixed(jx - S) : 0u;
 #pragma unroll
         for (int q = 0; q < S; ++q) {
-          la[q] = lb[q] = 0ull;
-          pf2 na = xa, nb = xb;
-          if (TCT < 0 || TCT >= 2 * q + 2) {
-            la[q] = plap(F2a[q], F1a[q], xa, m2);
-            lb[q] = plap(F2b[q], F1b[q], xb, m2);
-            if (CAUSAL) {
-              na = padd(xa, pmul_sep(al[q], la[q], zn));
-              nb = padd(xb, pmul_sep(al[q], lb[q], zn));
-              if (SLOW && fxc) {
-                na = xa;
-                nb = xb;
-              }
-            } else {
-              na = padd(F1a[q], pmul_sep(al[q], la[q], zn));
-              nb = padd(F1b[q], pmul_sep(al[q], lb[q], zn));
-              if (SLOW && ((fwx >> (S - 1 - q)) & 1u)) {
-                na = F1a[q];
-                nb = F1b[q];
+#pragma unroll
+          for (int p = 0; p < NP; ++p) {
+            la[q][p] = 0ull;
+            pf2 n = x[p];
+            if (TCT < 0 || TCT >= 2 * q + 2) {
+              la[q][p] = plap(F2[q][p], F1[q][p], x[p], m2);
+              if (CAUSAL) {
+                n = padd(x[p], pmul_sep(al[q], la[q][p], zn));
+                if (SLOW && fxc) n = x[p];
+              } else {
+                n = padd(F1[q][p], pmul_sep(al[q], la[q][p], zn));
+                if (SLOW && ((fwx >> (S - 1 - q)) & 1u)) n = F1[q][p];
               }
             }
+            F2[q][p] = F1[q][p];
+            F1[q][p] = x[p];
+            x[p] = n;
           }
-          F2a[q] = F1a[q];
-          F1a[q] = xa;
-          F2b[q] = F1b[q];
-          F1b[q] = xb;
-          xa = na;
-          xb = nb;
         }
       }
       // ---- adjoint march, pairing g_k with lap(u_{k-1}) ----
       const bool f0 = SLOW && rb.fixed(jg);
       const uint32_t fw = SLOW ? (CAUSAL ? rb.window16_fixed(jg - 2 * S) : rb.window8_fixed(jg - S)) : 0u;
-      pf2 ca = pmul_sep(al[S - 1], ga, zn), cb2 = pmul_sep(al[S - 1], gb, zn);
-      if (SLOW && f0) ca = cb2 = 0ull;
-      const pf2 qa = (SLOW && f0) ? 0ull : ga, qb = (SLOW && f0) ? 0ull : gb;  // q at row jg
+      pf2 c[NP], q[NP];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        c[p] = pmul_sep(al[S - 1], g[p], zn);
+        if (SLOW && f0) c[p] = 0ull;
+        q[p] = (SLOW && f0) ? 0ull : g[p];  // q at row jg
+      }
       static_for<S>([&](auto M) {
         constexpr int m = decltype(M)::value;
         constexpr int k = S - m;
         constexpr int d = G::delay(k);
         constexpr int e = G::e(k);
-        // d(alpha_k): g_k is (ga, gb), lap(u_{k-1}) is (la[k-1], lb[k-1])
-        {
-          pf2 pga = ga, pgb = gb, pla = la[k - 1], plb = lb[k - 1];
-          if constexpr (d > 0) {
-            constexpr int slot = I % d;
-            const pf2 oa = DLa[k - 1][slot], ob = DLb[k - 1][slot];
-            DLa[k - 1][slot] = pla;
-            DLb[k - 1][slot] = plb;
-            pla = oa;
-            plb = ob;
-          } else if constexpr (d < 0) {
-            constexpr int slot = I % (-d);
-            const pf2 oa = DLa[k - 1][slot], ob = DLb[k - 1][slot];
-            DLa[k - 1][slot] = pga;
-            DLb[k - 1][slot] = pgb;
-            pga = oa;
-            pgb = ob;
-          }
-          // paired row - l0 = t - PRO + e, in [0, nout); only updated rows count
-          bool take = (TCT < 0 || TCT + e >= PRO) && (I + e < lim);
-          if (SLOW) take = take && !rb.fixed(l0 + t - PRO + e);
-          if (take) {
-            acc[k - 1] = pfma(pga, pla, acc[k - 1]);
-            acc[k - 1] = pfma(pgb, plb, acc[k - 1]);
-            if constexpr (KIND != 0) {
-              acc[S] = pfma(pga, ha, acc[S]);
-              acc[S] = pfma(pgb, hb, acc[S]);
+        // d(alpha_k): g_k is g, lap(u_{k-1}) is la[k-1]
+        // paired row - l0 = t - PRO + e, in [0, nout); only updated rows count
+        bool take = (TCT < 0 || TCT + e >= PRO) && (I + e < lim);
+        if (SLOW) take = take && !rb.fixed(l0 + t - PRO + e);
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+          pf2 pg = g[p], pl = la[k - 1][p];
+          if constexpr (G::reg_ring(k)) {
+            constexpr int slot = I % G::adelay(k);
+            pf2& cell = DL[k - 1][slot][p];
+            const pf2 old = cell;
+            if constexpr (d > 0) {
+              cell = pl;
+              pl = old;
+            } else {
+              cell = pg;
+              pg = old;
             }
+          } else if constexpr (G::smem_ring(k)) {
+            constexpr int r = G::smem_index(k);
+            pf2* ring = dring + (r * kFwdRC * NP + p) * 32 + tid;
+            constexpr int rd = (I - G::adelay(k) + kFwdRC) % kFwdRC;
+            const pf2 old = ring[rd * NP * 32];
+            ring[I * NP * 32] = d > 0 ? pl : pg;
+            if constexpr (d > 0) pl = old;
+            else pg = old;
+          }
+          if (take) {
+            acc[k - 1] = pfma(pg, pl, acc[k - 1]);
+            if constexpr (KIND != 0) acc[S] = pfma(pg, h[p], acc[S]);
           }
         }
-        pf2 na = ga, nb = gb;
-        if (TCT < 0 || TCT >= 2 * m + 2) {
-          if (CAUSAL) {
-            na = padd(G2a[m], plap(ca, P1a[m], P2a[m], m2));
-            nb = padd(G2b[m], plap(cb2, P1b[m], P2b[m], m2));
-          } else {
-            na = padd(G1a[m], plap(P2a[m], P1a[m], ca, m2));
-            nb = padd(G1b[m], plap(P2b[m], P1b[m], cb2, m2));
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+          pf2 n = g[p];
+          if (TCT < 0 || TCT >= 2 * m + 2) {
+            if (CAUSAL) n = padd(G2[m][p], plap(c[p], P1[m][p], P2[m][p], m2));
+            else n = padd(G1[m][p], plap(P2[m][p], P1[m][p], c[p], m2));
+            if constexpr (KIND != 0) {
+              // finished row i = jg-1 (causal jg-2): q[i-1], q[i], q[i+1] are
+              // (Q2, Q1, q) non-causal, q[i], q[i+1] are (Q2, Q1) causal
+              pf2 ht;
+              if constexpr (KIND == 1) {
+                ht = CAUSAL ? pfma(Q1[p], n1, Q2[p]) : pmul(pfma(q[p], n1, Q2[p]), half);
+              } else {
+                ht = pmul(fp[p], CAUSAL ? Q2[p] : Q1[p]);
+              }
+              n = padd(n, pmul_sep(be, ht, zn));
+            }
           }
           if constexpr (KIND != 0) {
-            // finished row i = jg-1 (causal jg-2): q[i-1], q[i], q[i+1] are
-            // (Q2, Q1, q) non-causal, q[i], q[i+1] are (Q2, Q1) causal
-            pf2 hta, htb;
-            if constexpr (KIND == 1) {
-              hta = CAUSAL ? pfma(Q1a, n1, Q2a) : pmul(pfma(qa, n1, Q2a), half);
-              htb = CAUSAL ? pfma(Q1b, n1, Q2b) : pmul(pfma(qb, n1, Q2b), half);
-            } else {
-              hta = pmul(fpa, CAUSAL ? Q2a : Q1a);
-              htb = pmul(fpb, CAUSAL ? Q2b : Q1b);
-            }
-            na = padd(na, pmul_sep(be, hta, zn));
-            nb = padd(nb, pmul_sep(be, htb, zn));
+            Q2[p] = Q1[p];
+            Q1[p] = q[p];
           }
+          P2[m][p] = P1[m][p];
+          P1[m][p] = c[p];
+          if (CAUSAL) G2[m][p] = G1[m][p];
+          G1[m][p] = g[p];
+          g[p] = n;
         }
-        if constexpr (KIND != 0) {
-          Q2a = Q1a;
-          Q2b = Q1b;
-          Q1a = qa;
-          Q1b = qb;
-        }
-        P2a[m] = P1a[m];
-        P1a[m] = ca;
-        P2b[m] = P1b[m];
-        P1b[m] = cb2;
-        if (CAUSAL) {
-          G2a[m] = G1a[m];
-          G2b[m] = G1b[m];
-        }
-        G1a[m] = ga;
-        G1b[m] = gb;
-        ga = na;
-        gb = nb;
         if constexpr (m < S - 1) {
-          ca = pmul_sep(al[S - 2 - m], ga, zn);
-          cb2 = pmul_sep(al[S - 2 - m], gb, zn);
-          if (SLOW) {
-            const bool f = CAUSAL ? ((fw >> (2 * S - 2 * m - 2)) & 1u) : ((fw >> (S - 1 - m)) & 1u);
-            if (f) ca = cb2 = 0ull;
+          bool f = false;
+          if (SLOW) f = CAUSAL ? ((fw >> (2 * S - 2 * m - 2)) & 1u) : ((fw >> (S - 1 - m)) & 1u);
+#pragma unroll
+          for (int p = 0; p < NP; ++p) {
+            c[p] = pmul_sep(al[S - 2 - m], g[p], zn);
+            if (SLOW && f) c[p] = 0ull;
           }
         }
       });
@@ -429,33 +445,33 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
 
     // kind: 0..NPRO-1 = prologue chunk, NPRO = full output chunk, NPRO+1 = partial last chunk
     auto march_chunk = [&](auto slow_tag, auto kind_tag, int c, const T* gbuf, const T* xbuf) {
-      constexpr int KIND = decltype(kind_tag)::value;
+      constexpr int CK = decltype(kind_tag)::value;
       const int t0 = c * kFwdRC;
       const int lim = nrows - t0;
       T* st = stage + ((c - NPRO) & 1) * CHUNK + cb;
       static_for<kFwdRC>([&](auto II) {
         constexpr int i = decltype(II)::value;
-        pf2 ga, gb, xa, xb;
-        Q::split(*reinterpret_cast<const V*>(gbuf + cb + i * kFwdDT), ga, gb);
-        Q::split(*reinterpret_cast<const V*>(xbuf + cb + i * kFwdDT), xa, xb);
-        if constexpr (KIND < NPRO) {
-          step_row(slow_tag, std::integral_constant<int, KIND * kFwdRC + i>{}, II, t0 + i, lim, ga, gb, xa, xb);
+        pf2 g[NP], x[NP], hi_;
+        Q::split(*reinterpret_cast<const V*>(gbuf + cb + i * kDaDT), g[0], NP > 1 ? g[NP - 1] : hi_);
+        Q::split(*reinterpret_cast<const V*>(xbuf + cb + i * kDaDT), x[0], NP > 1 ? x[NP - 1] : hi_);
+        if constexpr (CK < NPRO) {
+          step_row(slow_tag, std::integral_constant<int, CK * kFwdRC + i>{}, II, t0 + i, lim, g, x);
         } else {
-          step_row(slow_tag, std::integral_constant<int, -1>{}, II, t0 + i, lim, ga, gb, xa, xb);
+          step_row(slow_tag, std::integral_constant<int, -1>{}, II, t0 + i, lim, g, x);
           const int64_t orow = l0 + t0 + i - PRO;
-          if constexpr (KIND == NPRO) {
-            if (tstore) *reinterpret_cast<V*>(st + i * kFwdDT) = Q::join(ga, gb);
-            else store_row(orow, ga, gb);
+          if constexpr (CK == NPRO) {
+            if (tstore) *reinterpret_cast<V*>(st + i * kDaDT) = Q::join(g[0], NP > 1 ? g[NP - 1] : 0ull);
+            else store_row(orow, g);
           } else {
-            if (t0 + i < nrows) store_row(orow, ga, gb);
+            if (t0 + i < nrows) store_row(orow, g);
           }
         }
       });
     };
 
     auto do_chunk = [&](auto slow_tag, auto kind_tag, int c) -> bool {
-      constexpr int KIND = decltype(kind_tag)::value;
-      constexpr bool FULL = KIND == NPRO;
+      constexpr int CK = decltype(kind_tag)::value;
+      constexpr bool FULL = CK == NPRO;
       const int slot = c % NST;
       T* gbuf = gring + slot * CHUNK;
       T* xbuf = xring + slot * CHUNK;
@@ -499,6 +515,9 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
       if (!do_chunk(slow_tag, std::integral_constant<int, 0>{}, 0)) return false;
       if constexpr (NPRO > 1) {
         if (!do_chunk(slow_tag, std::integral_constant<int, 1>{}, 1)) return false;
+      }
+      if constexpr (NPRO > 2) {
+        if (!do_chunk(slow_tag, std::integral_constant<int, 2>{}, 2)) return false;
       }
       for (int c = NPRO; c < nfull_end; ++c)
         if (!do_chunk(slow_tag, std::integral_constant<int, NPRO>{}, c)) return false;
@@ -575,7 +594,28 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
   if (tid == 0) *a.counter = 0u;
 }
 
-size_t dalpha_smem_bytes(int dtype) { return dtype == kF32 ? da_smem<float>() : da_smem<__nv_bfloat16>(); }
+namespace {
+
+template <typename T, bool CAUSAL>
+size_t da_smem_s(int steps) {
+  switch (steps) {
+    case 1: return da_smem<T, 1, CAUSAL>();
+    case 2: return da_smem<T, 2, CAUSAL>();
+    case 3: return da_smem<T, 3, CAUSAL>();
+    case 4: return da_smem<T, 4, CAUSAL>();
+    case 5: return da_smem<T, 5, CAUSAL>();
+    case 6: return da_smem<T, 6, CAUSAL>();
+    case 7: return da_smem<T, 7, CAUSAL>();
+    default: return da_smem<T, 8, CAUSAL>();
+  }
+}
+
+}  // namespace
+
+size_t dalpha_smem_bytes(int dtype, int steps, int causal) {
+  if (dtype == kF32) return causal ? da_smem_s<float, true>(steps) : da_smem_s<float, false>(steps);
+  return causal ? da_smem_s<__nv_bfloat16, true>(steps) : da_smem_s<__nv_bfloat16, false>(steps);
+}
 
 namespace {
 
@@ -600,6 +640,10 @@ const void* da_ptr(int steps) {
     case 2: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 2, CAUSAL>);
     case 3: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 3, CAUSAL>);
     case 4: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 4, CAUSAL>);
+    case 5: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 5, CAUSAL>);
+    case 6: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 6, CAUSAL>);
+    case 7: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 7, CAUSAL>);
+    case 8: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 8, CAUSAL>);
     default: return nullptr;
   }
 }
@@ -627,7 +671,7 @@ cudaError_t launch_bld_dalpha(const BldArgs& a, const CUtensorMap* gmap, const C
                               const CUtensorMap* ymap, int dtype, int steps, int causal, dim3 grid, cudaStream_t st) {
   const void* kern = da_kernel(dtype, steps, causal, a.pde_kind);
   if (kern == nullptr) return cudaErrorInvalidValue;
-  const size_t smem = dalpha_smem_bytes(dtype);
+  const size_t smem = dalpha_smem_bytes(dtype, steps, causal);
   cudaError_t e = ensure_smem_attr(kern, smem);
   if (e != cudaSuccess) return e;
   void* args[] = {const_cast<CUtensorMap*>(gmap), const_cast<CUtensorMap*>(xmap), const_cast<CUtensorMap*>(ymap),
@@ -641,7 +685,7 @@ int bld_dalpha_ctas_per_sm(int dtype, int steps, int causal) {
     int dev;
     int n;
   };
-  static Entry table[64];
+  static Entry table[256];
   static int used = 0;
   static std::mutex mu;
   const void* kern = da_kernel(dtype, steps, causal);
@@ -651,11 +695,11 @@ int bld_dalpha_ctas_per_sm(int dtype, int steps, int causal) {
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; ++i)
     if (table[i].kern == kern && table[i].dev == dev) return table[i].n;
-  const size_t smem = dalpha_smem_bytes(dtype);
+  const size_t smem = dalpha_smem_bytes(dtype, steps, causal);
   if (ensure_smem_attr(kern, smem) != cudaSuccess) return -1;
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kFwdThreads, smem) != cudaSuccess || n <= 0) return -1;
-  if (used < 64) table[used++] = Entry{kern, dev, n};
+  if (used < 256) table[used++] = Entry{kern, dev, n};
   return n;
 }
 

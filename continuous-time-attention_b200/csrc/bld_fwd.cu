@@ -87,10 +87,10 @@ constexpr int march_min_ctas() {
 // (p2, p1, x) = rows (i-1, i, i+1) non-causal, (i-2, i-1, i) causal.
 __device__ __forceinline__ float fast_sigmoid(float v) { return __frcp_rn(__fadd_rn(1.0f, __expf(-v))); }
 
-template <int KIND, bool CAUSAL>
+template <int KIND, bool CAUSAL, bool FM = false>
 __device__ __forceinline__ pf2 level_update(pf2 p2, pf2 p1, pf2 x, pf2 al, pf2 be, float be_s, pf2 m2, pf2 zn) {
   if constexpr (KIND == 0) {
-    return CAUSAL ? pst_c(p2, p1, x, al, m2, zn) : pst_nc(p2, p1, x, al, m2, zn);
+    return CAUSAL ? pst_c<FM>(p2, p1, x, al, m2, zn) : pst_nc<FM>(p2, p1, x, al, m2, zn);
   } else {
     const pf2 lap = plap(p2, p1, x, m2);
     const pf2 c = CAUSAL ? x : p1;
@@ -120,13 +120,16 @@ __device__ __forceinline__ pf2 level_update(pf2 p2, pf2 p1, pf2 x, pf2 al, pf2 b
 // T, as the stored tensor would hold it) over its rows, and the CTA writes its
 // column sums to a.pool_partial[(batch * row tiles + row tile) * D + col], for
 // pool_finish_kernel to reduce in a fixed order.
-template <typename T, int S, bool CAUSAL, bool ADJ, bool RES, int KIND = 0, bool POOL = false>
+// FM: the contracted update (pst_nc / pst_c), forward diffusion only.
+template <typename T, int S, bool CAUSAL, bool ADJ, bool RES, int KIND = 0, bool POOL = false, bool FM = false>
 __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ, RES>()))
     bld_march_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                      const __grid_constant__ CUtensorMap rmap, const BldArgs a) {
+  static_assert(!FM || (!ADJ && KIND == 0 && !POOL), "the contracted update is the diffusion forward");
   static_assert(!POOL || (!ADJ && !RES && KIND == 0 && !CAUSAL), "the pooled form is the non-causal forward");
   static_assert(!RES || (!ADJ && !CAUSAL), "the residual form is the non-causal forward");
   static_assert(KIND == 0 || (S == 1 && !ADJ && !RES), "the other PDE kinds are single forward steps");
+  constexpr int PKIND = KIND;  // the update kind (the chunk lambdas below name their chunk kind KIND)
   // every global read (cu_seqlens, mask, alphas, the streams) comes after the wait
   pdl_launch_dependents();
   pdl_wait();
@@ -148,6 +151,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   T* stage = ring + kFwdStages * CHUNK;  // output staging for the TMA stores
   __shared__ __align__(8) uint64_t full_bar[kFwdStages];
   __shared__ __align__(8) uint64_t res_bar[RES ? 2 : 1];
+  __shared__ __align__(8) uint64_t stall_bar;  // test hook: a phase nothing completes
   __shared__ uint32_t pbits[POOL ? kBldMaxWords + 2 : 1];  // POOL: mask bits of the march rows
   __shared__ uint32_t fbits[kBldMaxWords + 2];
   __shared__ uint32_t zbits[kBldMaxWords + 2];
@@ -180,6 +184,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       mbar_init(&res_bar[0], 1);
       mbar_init(&res_bar[1], 1);
     }
+    if (a.debug_stall_us > 0) mbar_init(&stall_bar, 1);
     fence_mbar_init();
   }
   // full output chunk c's residual rows into its staging slot
@@ -201,6 +206,20 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   }
   RowBits rb{fbits, zbits, jb};
   const bool slow = build_row_bits<CAUSAL, 1>(a, sg, rb, (nch * kFwdRC + 31) / 32, POOL ? pbits : nullptr);
+  if (a.debug_stall_us > 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+    // the timeout path of every pipeline wait, on demand: a bounded wait that
+    // runs out, the error word, a bounded drain of the loads in flight, exit
+    __syncwarp();
+    if (!mbar_wait_bounded_ns(&stall_bar, 0, static_cast<uint64_t>(a.debug_stall_us) * 1000ull)) {
+      if (tid == 0) {
+        atomicExch(&g_bld_fwd_error, kDevTimeout);
+        if (use_tma)
+          for (int c = 0; c < nch && c < kFwdStages; ++c) mbar_wait_bounded(&full_bar[c], 0);
+      }
+      __syncwarp();
+      return;
+    }
+  }
   if constexpr (POOL) {
     // a tile whose output rows are all masked out adds nothing to the pool:
     // zero partials and count, drain the loads already issued, and leave
@@ -347,8 +366,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       for (int k = 0; k < S; ++k) {
         pf2 na = xa, nb = xb;
         if (TCT < 0 || TCT >= 2 * k + 2) {
-          na = level_update<KIND, true>(P2a[k], P1a[k], xa, al[k], be, be_s, m2, zn);
-          nb = level_update<KIND, true>(P2b[k], P1b[k], xb, al[k], be, be_s, m2, zn);
+          na = level_update<KIND, true, FM>(P2a[k], P1a[k], xa, al[k], be, be_s, m2, zn);
+          nb = level_update<KIND, true, FM>(P2b[k], P1b[k], xb, al[k], be, be_s, m2, zn);
           if (SLOW) {
             na = psel(fx, xa, na);
             nb = psel(fx, xb, nb);
@@ -368,8 +387,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       for (int k = 0; k < S; ++k) {
         pf2 na = xa, nb = xb;
         if (TCT < 0 || TCT >= 2 * k + 2) {
-          na = level_update<KIND, false>(P2a[k], P1a[k], xa, al[k], be, be_s, m2, zn);
-          nb = level_update<KIND, false>(P2b[k], P1b[k], xb, al[k], be, be_s, m2, zn);
+          na = level_update<KIND, false, FM>(P2a[k], P1a[k], xa, al[k], be, be_s, m2, zn);
+          nb = level_update<KIND, false, FM>(P2b[k], P1b[k], xb, al[k], be, be_s, m2, zn);
           if (SLOW) {
             const bool fx = (fw >> (S - 1 - k)) & 1u;
             na = psel(fx, P1a[k], na);
@@ -397,6 +416,89 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
     if constexpr (CTA_FWD_PRELOAD) {
 #pragma unroll
       for (int i = 0; i < kFwdRC; ++i) in[i] = *reinterpret_cast<const V*>(buf + soff + i * kFwdDT);
+      if constexpr (CTA_FWD_EARLY_REFILL) {
+        // the whole chunk is in registers: refill its slot before marching it.
+        // Folding every loaded word into `dep` and handing it to the (volatile)
+        // issue below orders the shared-memory reads before the TMA overwrite.
+        uint32_t dep = 0;
+#pragma unroll
+        for (int i = 0; i < kFwdRC; ++i) {
+          if constexpr (sizeof(V) == 16) {
+            const uint4 w = *reinterpret_cast<const uint4*>(&in[i]);
+            dep ^= w.x ^ w.y ^ w.z ^ w.w;
+          } else if constexpr (sizeof(V) == 8) {
+            const uint2 w = *reinterpret_cast<const uint2*>(&in[i]);
+            dep ^= w.x ^ w.y;
+          } else {
+            dep ^= *reinterpret_cast<const uint32_t*>(&in[i]);
+          }
+        }
+        asm volatile("" ::"r"(dep) : "memory");
+        __syncwarp();
+        if (use_tma && tid == 0 && c + kFwdStages < nch) issue(c + kFwdStages);
+      }
+    }
+    // Full chunks of tiles without fixed rows: the S levels of the chunk's 8
+    // rows in anti-diagonal order (row i of level k on diagonal i + k).  Every
+    // level still sees its rows in order, so the arithmetic is unchanged, but
+    // consecutive instructions come from up to min(S, 8) independent
+    // (row, level) cells, which hides the FP32 latency of the dependent chain
+    // of one row.
+    if constexpr (CTA_FWD_DIAG && KIND == NPRO && !decltype(slow_tag)::value && CTA_FWD_PRELOAD) {
+      pf2 ua[kFwdRC], ub[kFwdRC];
+#pragma unroll
+      for (int i = 0; i < kFwdRC; ++i) Q::split(in[i], ua[i], ub[i]);
+      static_for<kFwdRC + S - 1>([&](auto Dg) {
+        constexpr int dg = decltype(Dg)::value;
+        static_for<S>([&](auto M) {
+          constexpr int m = decltype(M)::value;
+          constexpr int i = dg - m;
+          if constexpr (i >= 0 && i < kFwdRC) {
+            if constexpr (ADJ) {
+              // adjoint level m (forward step S-m) at march row i; see step_row
+              const pf2 ca = pmul_sep(al[S - 1 - m], ua[i], zn), cb = pmul_sep(al[S - 1 - m], ub[i], zn);
+              pf2 na, nb;
+              if (CAUSAL) {
+                na = padd(G2a[m], plap(ca, P1a[m], P2a[m], m2));
+                nb = padd(G2b[m], plap(cb, P1b[m], P2b[m], m2));
+                G2a[m] = G1a[m];
+                G2b[m] = G1b[m];
+              } else {
+                na = padd(G1a[m], plap(P2a[m], P1a[m], ca, m2));
+                nb = padd(G1b[m], plap(P2b[m], P1b[m], cb, m2));
+              }
+              P2a[m] = P1a[m];
+              P1a[m] = ca;
+              P2b[m] = P1b[m];
+              P1b[m] = cb;
+              G1a[m] = ua[i];
+              G1b[m] = ub[i];
+              ua[i] = na;
+              ub[i] = nb;
+            } else {
+              const pf2 na = level_update<PKIND, CAUSAL, FM>(P2a[m], P1a[m], ua[i], al[m], be, be_s, m2, zn);
+              const pf2 nb = level_update<PKIND, CAUSAL, FM>(P2b[m], P1b[m], ub[i], al[m], be, be_s, m2, zn);
+              P2a[m] = P1a[m];
+              P1a[m] = ua[i];
+              ua[i] = na;
+              P2b[m] = P1b[m];
+              P1b[m] = ub[i];
+              ub[i] = nb;
+            }
+          }
+        });
+      });
+#pragma unroll
+      for (int i = 0; i < kFwdRC; ++i) {
+        if (tstore) {
+          V y = Q::join(ua[i], ub[i]);
+          if constexpr (RES) y = vec_add_round<Q>(y, *reinterpret_cast<const V*>(st + i * kFwdDT));
+          *reinterpret_cast<V*>(st + i * kFwdDT) = y;
+        } else {
+          store_row(l0 + t0 + i - PRO, ua[i], ub[i]);
+        }
+      }
+      return;
     }
     static_for<kFwdRC>([&](auto I) {
       constexpr int i = decltype(I)::value;
@@ -470,7 +572,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       // the next full chunk's staging slot was last read by the store of chunk
       // c-1, which bulk_wait_read_all above has seen complete
       if (RES && tstore && c + 1 >= NPRO && c + 1 < nfull_end) issue_res(c + 1);
-      if (use_tma && c + kFwdStages < nch) issue(c + kFwdStages);
+      if (!(CTA_FWD_PRELOAD && CTA_FWD_EARLY_REFILL) && use_tma && c + kFwdStages < nch) issue(c + kFwdStages);
     }
     return true;
   };
@@ -568,17 +670,17 @@ size_t fwd_smem_bytes(int dtype) {
 
 namespace {
 
-template <typename T, bool CAUSAL, bool ADJ, bool RES>
+template <typename T, bool CAUSAL, bool ADJ, bool RES, bool FM = false>
 const void* march_ptr(int steps) {
   switch (steps) {
-    case 1: return reinterpret_cast<const void*>(bld_march_kernel<T, 1, CAUSAL, ADJ, RES>);
-    case 2: return reinterpret_cast<const void*>(bld_march_kernel<T, 2, CAUSAL, ADJ, RES>);
-    case 3: return reinterpret_cast<const void*>(bld_march_kernel<T, 3, CAUSAL, ADJ, RES>);
-    case 4: return reinterpret_cast<const void*>(bld_march_kernel<T, 4, CAUSAL, ADJ, RES>);
-    case 5: return reinterpret_cast<const void*>(bld_march_kernel<T, 5, CAUSAL, ADJ, RES>);
-    case 6: return reinterpret_cast<const void*>(bld_march_kernel<T, 6, CAUSAL, ADJ, RES>);
-    case 7: return reinterpret_cast<const void*>(bld_march_kernel<T, 7, CAUSAL, ADJ, RES>);
-    case 8: return reinterpret_cast<const void*>(bld_march_kernel<T, 8, CAUSAL, ADJ, RES>);
+    case 1: return reinterpret_cast<const void*>(bld_march_kernel<T, 1, CAUSAL, ADJ, RES, 0, false, FM>);
+    case 2: return reinterpret_cast<const void*>(bld_march_kernel<T, 2, CAUSAL, ADJ, RES, 0, false, FM>);
+    case 3: return reinterpret_cast<const void*>(bld_march_kernel<T, 3, CAUSAL, ADJ, RES, 0, false, FM>);
+    case 4: return reinterpret_cast<const void*>(bld_march_kernel<T, 4, CAUSAL, ADJ, RES, 0, false, FM>);
+    case 5: return reinterpret_cast<const void*>(bld_march_kernel<T, 5, CAUSAL, ADJ, RES, 0, false, FM>);
+    case 6: return reinterpret_cast<const void*>(bld_march_kernel<T, 6, CAUSAL, ADJ, RES, 0, false, FM>);
+    case 7: return reinterpret_cast<const void*>(bld_march_kernel<T, 7, CAUSAL, ADJ, RES, 0, false, FM>);
+    case 8: return reinterpret_cast<const void*>(bld_march_kernel<T, 8, CAUSAL, ADJ, RES, 0, false, FM>);
     default: return nullptr;
   }
 }
@@ -591,10 +693,19 @@ const void* march_ptr_kind(int steps, int causal) {
 }
 
 template <typename T>
-const void* march_ptr_t(int steps, int causal, int adj, int res, int kind) {
+const void* march_ptr_t(int steps, int causal, int adj, int res, int kind, int fm) {
   if (kind != 0) {
     if (adj || res) return nullptr;
     return kind == 1 ? march_ptr_kind<T, 1>(steps, causal) : kind == 2 ? march_ptr_kind<T, 2>(steps, causal) : nullptr;
+  }
+  if (fm) {
+    // the contracted forward is built for 16-bit I/O only
+    if constexpr (sizeof(T) == 2) {
+      if (adj) return nullptr;
+      if (res) return causal ? nullptr : march_ptr<T, false, false, true, true>(steps);
+      return causal ? march_ptr<T, true, false, false, true>(steps) : march_ptr<T, false, false, false, true>(steps);
+    }
+    return nullptr;
   }
   if (res) return (causal || adj) ? nullptr : march_ptr<T, false, false, true>(steps);
   if (adj) return causal ? march_ptr<T, true, true, false>(steps) : march_ptr<T, false, true, false>(steps);
@@ -616,9 +727,15 @@ const void* march_ptr_pool(int steps) {
   }
 }
 
-const void* march_kernel(int dtype, int steps, int causal, int adj, int res, int kind = 0, int pool = 0) {
+const void* march_kernel(int dtype, int steps, int causal, int adj, int res, int kind = 0, int pool = 0, int fm = 0) {
+#if defined(CTA_EXPERIMENT_BF16_FWD_ONLY)
+  // reduced build for timing experiments on the forward march only
+  if (dtype != kBF16 || causal || adj || res || kind || pool) return nullptr;
+  return fm ? march_ptr<__nv_bfloat16, false, false, false, true>(steps)
+            : march_ptr<__nv_bfloat16, false, false, false>(steps);
+#else
   if (pool) {
-    if (causal || adj || res || kind) return nullptr;
+    if (causal || adj || res || kind || fm) return nullptr;
     switch (dtype) {
       case kF32: return march_ptr_pool<float>(steps);
       case kBF16: return march_ptr_pool<__nv_bfloat16>(steps);
@@ -627,11 +744,12 @@ const void* march_kernel(int dtype, int steps, int causal, int adj, int res, int
     }
   }
   switch (dtype) {
-    case kF32: return march_ptr_t<float>(steps, causal, adj, res, kind);
-    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, adj, res, kind);
-    case kF16: return march_ptr_t<__half>(steps, causal, adj, res, kind);
+    case kF32: return march_ptr_t<float>(steps, causal, adj, res, kind, fm);
+    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, adj, res, kind, fm);
+    case kF16: return march_ptr_t<__half>(steps, causal, adj, res, kind, fm);
     default: return nullptr;
   }
+#endif
 }
 
 }  // namespace
@@ -640,12 +758,14 @@ cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUte
                            const CUtensorMap* rmap, int dtype, int steps, int causal, int adjoint, dim3 grid,
                            size_t smem, cudaStream_t st) {
   const void* kern = march_kernel(dtype, steps, causal, adjoint, a.residual != nullptr ? 1 : 0, a.pde_kind,
-                                  a.pool_partial != nullptr ? 1 : 0);
+                                  a.pool_partial != nullptr ? 1 : 0, a.contract);
   if (kern == nullptr) return cudaErrorInvalidValue;
   cudaError_t e = ensure_smem_attr(kern, smem);
   if (e != cudaSuccess) return e;
+  BldArgs la = a;
+  if (kFwdOutSlots == 0) la.use_tma_store = 0;  // no staging slots: plain stores
   void* args[] = {const_cast<CUtensorMap*>(xmap), const_cast<CUtensorMap*>(ymap), const_cast<CUtensorMap*>(rmap),
-                  const_cast<BldArgs*>(&a)};
+                  &la};
   if (!pdl_enabled()) return cudaLaunchKernel(kern, grid, dim3(kFwdThreads), args, smem, st);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -682,7 +802,7 @@ cudaError_t launch_pool_finish(const BldArgs& a, int dtype, int64_t ntl, void* p
   return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
-int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual) {
+int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual, int contract) {
   struct Entry {
     const void* kern;
     int dev;
@@ -691,7 +811,7 @@ int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int res
   static Entry table[256];
   static int used = 0;
   static std::mutex mu;
-  const void* kern = march_kernel(dtype, steps, causal, adjoint, residual);
+  const void* kern = march_kernel(dtype, steps, causal, adjoint, residual, 0, 0, contract);
   if (kern == nullptr) return -1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;

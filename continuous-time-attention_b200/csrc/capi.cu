@@ -4,6 +4,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -147,12 +148,24 @@ bool encode_map(CUtensorMap* m, const void* base, int dtype, int64_t nb, int64_t
 // that the 2*steps halo rows stay a small overhead
 // ---------------------------------------------------------------------------
 struct Tuning {
-  int ctas_per_sm = 6;       // backward kernels (128-thread CTAs)
   int tl_override = 0;
   int fwd_ctas_per_sm = 16;  // forward kernels (one-warp CTAs): one full wave
   int pdl = 0;               // march kernels launched with programmatic dependent launch
+  int no_tma_store = 0;      // forward march: plain vector stores instead of staged TMA stores
+  int debug_stall_us = 0;    // test hook of the forward march's timeout path (microseconds, 0 = off)
 };
 Tuning g_tuning;
+
+// Arithmetic of the forward update with 16-bit I/O: process default (set by
+// cta_set_arithmetic) and a per-thread override (cta_set_thread_arithmetic, -1
+// = follow the process default).  fp32 I/O always uses the exact update.
+std::atomic<int> g_arith{CTA_ARITH_CONTRACTED};
+thread_local int t_arith = -1;
+
+int contract_for(int dtype) {
+  const int mode = t_arith >= 0 ? t_arith : g_arith.load(std::memory_order_relaxed);
+  return (mode == CTA_ARITH_CONTRACTED && dtype != CTA_F32) ? 1 : 0;
+}
 
 int pick_tl(int64_t rows, int64_t parallel_ctas, int steps, int per_sm) {
   if (g_tuning.tl_override > 0) return std::min(kBldMaxTL, ((g_tuning.tl_override + kBldRC - 1) / kBldRC) * kBldRC);
@@ -167,8 +180,8 @@ int pick_tl(int64_t rows, int64_t parallel_ctas, int steps, int per_sm) {
 
 // target resident CTAs per SM of a march kernel: the tuning value, capped by
 // the occupancy the variant gets (deep variants hold more registers)
-int march_per_sm(int dtype, int steps, int causal, int adjoint, int residual = 0) {
-  const int occ = bld_march_ctas_per_sm(dtype, steps, causal, adjoint, residual);
+int march_per_sm(int dtype, int steps, int causal, int adjoint, int residual = 0, int contract = 0) {
+  const int occ = bld_march_ctas_per_sm(dtype, steps, causal, adjoint, residual, contract);
   return occ > 0 ? std::min(g_tuning.fwd_ctas_per_sm, occ) : g_tuning.fwd_ctas_per_sm;
 }
 
@@ -202,13 +215,17 @@ BldArgs blank_bld() {
   BldArgs a;
   std::memset(&a, 0, sizeof(a));
   a.neg_zero = -0.0f;
+  a.debug_stall_us = g_tuning.debug_stall_us;
   return a;
 }
 
-bool quad_ok(const void* y, int dtype, int64_t nb, int64_t D, int64_t sB, int64_t sL) {
+// rows of y allow aligned stores of v consecutive elements per lane
+bool vec_ok(const void* y, int dtype, int64_t nb, int64_t D, int64_t sB, int64_t sL, int64_t v) {
   const int64_t es = static_cast<int64_t>(dtype_size(dtype));
-  const int64_t v = kFwdVec;
   return reinterpret_cast<uintptr_t>(y) % (v * es) == 0 && D % v == 0 && sL % v == 0 && (nb == 1 || sB % v == 0);
+}
+bool quad_ok(const void* y, int dtype, int64_t nb, int64_t D, int64_t sB, int64_t sL) {
+  return vec_ok(y, dtype, nb, D, sB, sL, kFwdVec);
 }
 
 int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int64_t tile_rows, cudaStream_t st,
@@ -235,11 +252,12 @@ int launch_fwd(BldArgs& a, int dtype, int steps, int causal, int64_t nbatch, int
 // = TMA may address the three tensors (dense, whole-tensor rows).
 int launch_dalpha_march(BldArgs& m, int dtype, int steps, int causal, int64_t B, int64_t L, int64_t D,
                         void* workspace, float* dalpha, bool accumulate, bool tiled, cudaStream_t st) {
-  const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
+  const int64_t ndt = (D + kDaDT - 1) / kDaDT;
   const int64_t rows = m.out_end - m.out_begin;
   if (rows <= 0) return ok();
   const int occ = bld_dalpha_ctas_per_sm(dtype, steps, causal);
-  m.TL = pick_tl(rows, ndt * B, steps, occ > 0 ? std::min(g_tuning.fwd_ctas_per_sm, occ) : 8);
+  // one wave at the occupancy the variant gets (up to 24 one-warp CTAs per SM)
+  m.TL = pick_tl(rows, ndt * B, steps, occ > 0 ? occ : 8);
   const int64_t ntl = (rows + m.TL - 1) / m.TL;
   if (ntl * ndt > 0x7fffffffLL || B > 65535 || ntl * ndt * B > 0x7fffffffLL)
     return fail(CTA_EUNSUPPORTED, "grid too large (tiles %lld, D tiles %lld, batch %lld)", (long long)ntl,
@@ -250,25 +268,19 @@ int launch_dalpha_march(BldArgs& m, int dtype, int steps, int causal, int64_t B,
   m.counter = static_cast<unsigned int*>(workspace);
   m.dalpha_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeaderBytes);
   m.dalpha = dalpha;
-  m.y_quad_ok = quad_ok(m.y, dtype, B, D, m.ysB, m.ysL) ? 1 : 0;
+  m.y_quad_ok = vec_ok(m.y, dtype, B, D, m.ysB, m.ysL, 2 * kDaPairs) ? 1 : 0;
   CUtensorMap gm, xm, dm;
   std::memset(&gm, 0, sizeof(gm));
   std::memset(&xm, 0, sizeof(xm));
   std::memset(&dm, 0, sizeof(dm));
-  const bool tg = tiled && make_map(&gm, m.g, dtype, B, L, D, m.gsB, m.gsL, kFwdRC, kFwdDT);
-  const bool tx = tiled && make_map(&xm, m.x, dtype, B, L, D, m.xsB, m.xsL, kFwdRC, kFwdDT);
+  const bool tg = tiled && make_map(&gm, m.g, dtype, B, L, D, m.gsB, m.gsL, kFwdRC, kDaDT);
+  const bool tx = tiled && make_map(&xm, m.x, dtype, B, L, D, m.xsB, m.xsL, kFwdRC, kDaDT);
   m.use_tma = (tg && tx) ? 1 : 0;
-  m.use_tma_store = make_map(&dm, m.y, dtype, B, L, D, m.ysB, m.ysL, kFwdRC, kFwdDT) ? 1 : 0;
+  m.use_tma_store = make_map(&dm, m.y, dtype, B, L, D, m.ysB, m.ysL, kFwdRC, kDaDT) ? 1 : 0;
   dim3 grid(static_cast<unsigned>(ntl * ndt), 1u, static_cast<unsigned>(B));
   const cudaError_t e = launch_bld_dalpha(m, &gm, &xm, &dm, dtype, steps, causal, grid, st);
   if (e != cudaSuccess) return cuda_fail(e, "bld backward (d(alpha)) launch");
   return ok();
-}
-
-int64_t dalpha_max_ctas(int64_t B, int64_t L, int64_t D) {
-  const int64_t ntl = (L + 31) / 32;  // pick_tl never goes below 32 rows
-  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
-  return ntl * ndt * B;
 }
 
 }  // namespace
@@ -292,21 +304,30 @@ const char* cta_last_error(void) { return t_last_error.c_str(); }
 
 int cta_device_error(int clear) {
   const int a = read_device_error_bld_fwd(clear);
-  const int b = read_device_error_bld_bwd(clear);
   const int c = read_device_error_bdl(clear);
   const int d = read_device_error_bld_dalpha(clear);
-  if (a < 0 || b < 0 || c < 0 || d < 0) return -1;
-  return a != 0 ? a : (b != 0 ? b : (c != 0 ? c : d));
+  if (a < 0 || c < 0 || d < 0) return -1;
+  return a != 0 ? a : (c != 0 ? c : d);
 }
 
-// Tuning hook used by the benchmark sweeps (key 0: CTAs per SM target,
-// key 1: forced tile rows, 0 = automatic).  Returns the previous value.
+int cta_set_arithmetic(int mode) {
+  if (mode != CTA_ARITH_EXACT && mode != CTA_ARITH_CONTRACTED) return fail(-1, "unknown arithmetic mode %d", mode);
+  return g_arith.exchange(mode);
+}
+
+int cta_set_thread_arithmetic(int mode) {
+  if (mode != -1 && mode != CTA_ARITH_EXACT && mode != CTA_ARITH_CONTRACTED)
+    return fail(-2, "unknown arithmetic mode %d", mode);
+  const int prev = t_arith;
+  t_arith = mode;
+  return prev;
+}
+
+// Benchmark and test hook; the keys are listed with the declaration in
+// include/cta_stencil.h.  Returns the previous value.
 int cta_set_tuning(int key, int value) {
   int prev = 0;
-  if (key == 0) {
-    prev = g_tuning.ctas_per_sm;
-    g_tuning.ctas_per_sm = value > 0 ? value : 6;
-  } else if (key == 1) {
+  if (key == 1) {
     prev = g_tuning.tl_override;
     g_tuning.tl_override = value > 0 ? value : 0;
   } else if (key == 2) {
@@ -315,6 +336,12 @@ int cta_set_tuning(int key, int value) {
   } else if (key == 3) {
     prev = g_tuning.pdl;
     g_tuning.pdl = value != 0 ? 1 : 0;
+  } else if (key == 4) {
+    prev = g_tuning.no_tma_store;
+    g_tuning.no_tma_store = value != 0 ? 1 : 0;
+  } else if (key == 5) {
+    prev = g_tuning.debug_stall_us;
+    g_tuning.debug_stall_us = value > 0 ? std::min(value, 100000) : 0;
   }
   return prev;
 }
@@ -359,6 +386,7 @@ int cta_diffusion_bdl_ex(const void* in, void* out, int64_t B, int64_t D, int64_
     a.alpha_dev[k] = (alpha_dev != nullptr && k < steps) ? alpha_dev[k] : nullptr;
   }
   a.alpha_dev_dtype = alpha_dev_dtype;
+  a.contract = backward ? 0 : contract_for(dtype);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   // TMA form when both tensors are addressable: [B*D rows, L] maps, boxes of two
   // rows x 256 positions (loads) and two rows x 240 positions (stores)
@@ -370,7 +398,7 @@ int cta_diffusion_bdl_ex(const void* in, void* out, int64_t B, int64_t D, int64_
       make_map(&omap, out, dtype, 1, rows, L, rows * out_row_stride, out_row_stride, kBdlRows, kBdlOut)) {
     const int64_t nwin = (L + kBdlOut - 1) / kBdlOut;
     const int64_t pairs = (rows + kBdlRows - 1) / kBdlRows;
-    const int occ = bdl_march_ctas_per_sm(dtype, steps, causal ? 1 : 0, backward ? 1 : 0);
+    const int occ = bdl_march_ctas_per_sm(dtype, steps, causal ? 1 : 0, backward ? 1 : 0, a.contract);
     const int per_sm = occ > 0 ? std::min(g_tuning.fwd_ctas_per_sm, occ) : g_tuning.fwd_ctas_per_sm;
     const int64_t target = static_cast<int64_t>(num_sms()) * per_sm;
     const int64_t tw = std::max<int64_t>(1, (pairs * nwin + target - 1) / target);
@@ -440,7 +468,9 @@ static int fwd_bld_impl(const void* x, const void* residual, void* y, int64_t B,
   a.msL = mask_sL;
   fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-  a.TL = pick_tl(L, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, 0, residual != nullptr ? 1 : 0));
+  a.contract = contract_for(dtype);
+  a.TL = pick_tl(L, ndt * B, steps,
+                 march_per_sm(dtype, steps, causal ? 1 : 0, 0, residual != nullptr ? 1 : 0, a.contract));
   a.out_begin = 0;
   a.out_end = L;
   a.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
@@ -448,7 +478,7 @@ static int fwd_bld_impl(const void* x, const void* residual, void* y, int64_t B,
   std::memset(&xmap, 0, sizeof(xmap));
   std::memset(&ymap, 0, sizeof(ymap));
   a.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
-  a.use_tma_store = make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
+  a.use_tma_store = !g_tuning.no_tma_store && make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
   CUtensorMap rmap;
   std::memset(&rmap, 0, sizeof(rmap));
   if (residual != nullptr) {
@@ -548,13 +578,13 @@ int64_t cta_diffusion_bwd_bld_workspace_bytes(int64_t B, int64_t L, int64_t D, i
   (void)causal;
   if (B <= 0 || L <= 0 || D <= 0 || steps < 1 || steps > kMaxSteps) return kWsHeaderBytes;
   if (steps <= kDaMaxSteps) {
-    // march kernel: partials of up to ceil(L/32) x ceil(D/128) x B CTAs, then the
+    // march kernel: partials of up to ceil(L/32) x ceil(D/kDaDT) x B CTAs, then the
     // group sums (f64, 8-byte aligned)
-    const int64_t ctas = ((L + 31) / 32) * ((D + kFwdDT - 1) / kFwdDT) * B;
+    const int64_t ctas = ((L + 31) / 32) * ((D + kDaDT - 1) / kDaDT) * B;
     const int64_t ngroups = std::min<int64_t>(kWsMaxGroups, (ctas + 31) / 32);
     return kWsHeaderBytes + ctas * steps * 4 + 4 + ngroups * steps * 8;
   }
-  return kWsHeaderBytes + dalpha_max_ctas(B, L, D) * steps * static_cast<int64_t>(sizeof(float));
+  return kWsHeaderBytes;
 }
 
 int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, float* dalpha, void* workspace,
@@ -618,75 +648,30 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
     m.use_tma_store = make_map(&dm, grad_in, dtype, B, L, D, d_sB, d_sL, kFwdRC, kFwdDT) ? 1 : 0;
     return launch_fwd(m, dtype, steps, causal ? 1 : 0, B, L, static_cast<cudaStream_t>(stream), gm, dm, 1);
   }
-  if (steps <= kDaMaxSteps) {
-    // d(alpha), steps 1..4: the one-warp march carrying both wavefronts
-    BldArgs m = blank_bld();
-    m.g = grad_out;
-    m.x = x;
-    m.y = grad_in;
-    m.gsB = g_sB;
-    m.gsL = g_sL;
-    m.xsB = x_sB;
-    m.xsL = x_sL;
-    m.ysB = d_sB;
-    m.ysL = d_sL;
-    m.L = L;
-    m.D = static_cast<int>(D);
-    m.nbatch = static_cast<int>(B);
-    m.global_len = L;
-    m.mask = mask;
-    m.mask_dtype = mask_dtype;
-    m.msB = mask_sB;
-    m.msL = mask_sL;
-    fill_alpha(m, steps, alpha, alpha_dev, alpha_dev_dtype);
-    m.out_begin = 0;
-    m.out_end = L;
-    return launch_dalpha_march(m, dtype, steps, causal ? 1 : 0, B, L, D, workspace, dalpha, false, true,
-                               static_cast<cudaStream_t>(stream));
-  }
-  BldArgs a = blank_bld();
-  a.g = grad_out;
-  a.x = x;
-  a.y = grad_in;
-  a.gsB = g_sB;
-  a.gsL = g_sL;
-  a.xsB = x_sB;
-  a.xsL = x_sL;
-  a.ysB = d_sB;
-  a.ysL = d_sL;
-  a.L = L;
-  a.D = static_cast<int>(D);
-  a.nbatch = static_cast<int>(B);
-  a.global_len = L;
-  a.mask = mask;
-  a.mask_dtype = mask_dtype;
-  a.msB = mask_sB;
-  a.msL = mask_sL;
-  fill_alpha(a, steps, alpha, alpha_dev, alpha_dev_dtype);
-  const int64_t ndt = (D + kBldDT - 1) / kBldDT;
-  a.TL = std::max(pick_tl(L, ndt * B, steps, g_tuning.ctas_per_sm), 32);
-  a.out_begin = 0;
-  a.out_end = L;
-  const int64_t ntl = (L + a.TL - 1) / a.TL;
-  if (ntl > 0x7fffffffLL || ndt > 65535 || B > 65535) return fail(CTA_EUNSUPPORTED, "grid too large");
-  dim3 grid(static_cast<unsigned>(ntl), static_cast<unsigned>(ndt), static_cast<unsigned>(B));
-  CUtensorMap gmap, xmap;
-  std::memset(&gmap, 0, sizeof(gmap));
-  std::memset(&xmap, 0, sizeof(xmap));
-  bool tma = make_map(&gmap, grad_out, dtype, B, L, D, g_sB, g_sL, kBldRC, kBoxCols);
-  if (da) tma = tma && make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kBldRC, kBoxCols);
-  else xmap = gmap;
-  a.use_tma = tma ? 1 : 0;
-  if (da) {
-    a.num_ctas = static_cast<int>(ntl * ndt * B);
-    a.counter = static_cast<unsigned int*>(workspace);
-    a.dalpha_partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kWsHeaderBytes);
-    a.dalpha = dalpha;
-  }
-  const cudaError_t e = launch_bld_bwd(a, &gmap, &xmap, dtype, steps, causal ? 1 : 0, da ? 1 : 0, grid,
-                                       bld_smem_bytes(dtype, da ? 1 : 0), static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "bld backward launch");
-  return ok();
+  // d(alpha), steps 1..8: the one-warp march carrying both wavefronts
+  BldArgs m = blank_bld();
+  m.g = grad_out;
+  m.x = x;
+  m.y = grad_in;
+  m.gsB = g_sB;
+  m.gsL = g_sL;
+  m.xsB = x_sB;
+  m.xsL = x_sL;
+  m.ysB = d_sB;
+  m.ysL = d_sL;
+  m.L = L;
+  m.D = static_cast<int>(D);
+  m.nbatch = static_cast<int>(B);
+  m.global_len = L;
+  m.mask = mask;
+  m.mask_dtype = mask_dtype;
+  m.msB = mask_sB;
+  m.msL = mask_sL;
+  fill_alpha(m, steps, alpha, alpha_dev, alpha_dev_dtype);
+  m.out_begin = 0;
+  m.out_end = L;
+  return launch_dalpha_march(m, dtype, steps, causal ? 1 : 0, B, L, D, workspace, dalpha, false, true,
+                             static_cast<cudaStream_t>(stream));
 }
 
 static int fwd_varlen_impl(const void* x, const void* residual, void* y, int64_t total_rows, int64_t D,
@@ -713,12 +698,14 @@ static int fwd_varlen_impl(const void* x, const void* residual, void* y, int64_t
   a.pad_to_max = pad_to_max ? 1 : 0;
   a.max_len = max_len;
   for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
+  a.contract = contract_for(dtype);
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
   // tiles are cut per sequence: about eight tiles per average sequence keeps
   // the waves balanced across unequal lengths (halo overhead 2*steps/TL)
   const int64_t avg = std::max<int64_t>(1, total_rows / nseq);
   a.TL = g_tuning.tl_override > 0
-             ? pick_tl(avg, ndt * nseq, steps, march_per_sm(dtype, steps, 0, 0, residual != nullptr ? 1 : 0))
+             ? pick_tl(avg, ndt * nseq, steps,
+                       march_per_sm(dtype, steps, 0, 0, residual != nullptr ? 1 : 0, a.contract))
              : static_cast<int>(std::min<int64_t>(512, std::max<int64_t>(64, ((avg / 8 + 15) / 16) * 16)));
   a.out_begin = 0;
   a.out_end = max_len;
@@ -815,9 +802,11 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
     a.hext_hi = a.hi_ext ? static_cast<int>(hi_rows) : 0;
   }
   for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
+  a.contract = backward ? 0 : contract_for(dtype);
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
   a.TL = edge ? static_cast<int>(std::min<int64_t>(kBldMaxTL, ((oe - ob + kBldRC - 1) / kBldRC) * kBldRC))
-              : pick_tl(oe - ob, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, backward ? 1 : 0));
+              : pick_tl(oe - ob, ndt * B, steps,
+                        march_per_sm(dtype, steps, causal ? 1 : 0, backward ? 1 : 0, 0, a.contract));
   a.out_begin = ob;
   a.out_end = oe;
   a.y_quad_ok = quad_ok(out, dtype, B, D, L_local * D, D) ? 1 : 0;

@@ -177,19 +177,33 @@ __device__ __forceinline__ pf2 pfma(pf2 a, pf2 b, pf2 c) {
 // with -fmad=false; measured on B200, 148461 of 1M stencils differed.)
 __device__ __forceinline__ pf2 pmul_sep(pf2 a, pf2 b, pf2 zn) { return pfma(a, b, zn); }
 
-// non-causal update of centre c from l (row i-1) and r (row i+1); m2 = {-2,-2}
+// non-causal update of centre c from l (row i-1) and r (row i+1); m2 = {-2,-2}.
+// FM = false: c + round(alpha * lap), the reference's PyTorch ops (product and
+// sum rounded separately).  FM = true: the product and the sum as ONE fma, the
+// op order the reference's Triton kernels compile to (Triton contracts a
+// multiply feeding an add by default; kernels/diffusion_triton.py:89-90).
+template <bool FM = false>
 __device__ __forceinline__ pf2 pst_nc(pf2 l, pf2 c, pf2 r, pf2 al, pf2 m2, pf2 zn) {
   pf2 t = pfma(c, m2, r);  // r - 2c, one rounding (2c is exact)
   t = padd(t, l);
-  t = pmul_sep(al, t, zn);
-  return padd(c, t);
+  if constexpr (FM) {
+    return pfma(al, t, c);
+  } else {
+    t = pmul_sep(al, t, zn);
+    return padd(c, t);
+  }
 }
 // causal update of c (row i) from p1 (row i-1) and p2 (row i-2)
+template <bool FM = false>
 __device__ __forceinline__ pf2 pst_c(pf2 p2, pf2 p1, pf2 c, pf2 al, pf2 m2, pf2 zn) {
   pf2 t = pfma(p1, m2, c);
   t = padd(t, p2);
-  t = pmul_sep(al, t, zn);
-  return padd(c, t);
+  if constexpr (FM) {
+    return pfma(al, t, c);
+  } else {
+    t = pmul_sep(al, t, zn);
+    return padd(c, t);
+  }
 }
 // (hi - 2 mid) + lo
 __device__ __forceinline__ pf2 plap(pf2 lo, pf2 mid, pf2 hi, pf2 m2) { return padd(pfma(mid, m2, hi), lo); }
@@ -315,13 +329,16 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // Bounded wait on an mbarrier phase: gives up after ~1 s of wall time and
 // reports false, so a lost transaction turns into an error status instead of
 // a hung GPU.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded_ns(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > 1000000000ull) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_bounded_ns(bar, parity, 1000000000ull);
 }
 
 // 3-D tiled TMA load into this CTA's own shared memory: coordinates are (column, row, batch).

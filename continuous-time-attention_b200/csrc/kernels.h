@@ -14,19 +14,12 @@ constexpr int kMaxSteps = 8;
 // ---------------------------------------------------------------------------
 // [B, L, D] layout (feature axis contiguous): TMA-fed march along L
 // ---------------------------------------------------------------------------
-constexpr int kBldThreads = 128;              // 4 warps, all spread along D
-constexpr int kBldVec = 2;                    // columns per thread (one float2)
-constexpr int kBldDT = kBldThreads * kBldVec;  // 256 columns per CTA (TMA box inner extent)
-constexpr int kBldRC = 16;                    // rows per pipeline chunk
-constexpr int kBldStages = 4;                 // chunks in flight per CTA
+constexpr int kBldRC = 16;                    // row granularity of the tile sizes
 constexpr int kBldMaxTL = 2048;               // max output rows per CTA tile
 // forward kernel: one warp per CTA running its own pipeline; 4 columns per
 // lane (two packed pairs) -> 128-column tiles, one TMA box per 8-row chunk
-#ifndef CTA_FWD_VEC
-#define CTA_FWD_VEC 4
-#endif
 constexpr int kFwdThreads = 32;
-constexpr int kFwdVec = CTA_FWD_VEC;  // columns per lane: 4 (two packed pairs) or 2 (one pair)
+constexpr int kFwdVec = 4;  // columns per lane (two packed pairs)
 constexpr int kFwdDT = 32 * kFwdVec;
 constexpr int kFwdRC = 8;
 #ifndef CTA_FWD_STAGES
@@ -40,13 +33,29 @@ constexpr int kFwdRC = 8;
 #endif
 constexpr int kFwdStages = CTA_FWD_STAGES;     // input chunks in flight
 constexpr int kFwdMinCtas = CTA_FWD_MIN_CTAS;  // register budget (one-warp CTAs per SM) of the shallow variants
-constexpr int kFwdOutSlots = 2;  // output staging chunks for the TMA stores
-constexpr int kBoxCols = 256;    // TMA box inner extent of the backward maps (max 256)
+#ifndef CTA_FWD_OUT_SLOTS
+#define CTA_FWD_OUT_SLOTS 2
+#endif
+#ifndef CTA_FWD_DIAG
+#define CTA_FWD_DIAG 1
+#endif
+#ifndef CTA_FWD_EARLY_REFILL
+#define CTA_FWD_EARLY_REFILL 0
+#endif
+// output staging chunks for the TMA stores (0: plain vector stores, no staging)
+constexpr int kFwdOutSlots = CTA_FWD_OUT_SLOTS;
 // d(alpha) workspace: a fixed header of completion counters (so that no shape's
 // partial sums can land where another shape's counters live), then partials
 constexpr int64_t kWsHeaderBytes = 8192;
 constexpr int kWsMaxGroups = static_cast<int>(kWsHeaderBytes / 4) - 1;
-constexpr int kDaMaxSteps = 4;  // steps handled by the march d(alpha) kernel
+constexpr int kDaMaxSteps = 8;  // steps handled by the march d(alpha) kernel
+// march d(alpha) kernel: packed column pairs per lane (1: 64-column tiles, half
+// the per-lane state of two pairs, twice the resident warps)
+#ifndef CTA_DA_PAIRS
+#define CTA_DA_PAIRS 1
+#endif
+constexpr int kDaPairs = CTA_DA_PAIRS;
+constexpr int kDaDT = 64 * kDaPairs;  // columns per CTA (TMA box inner extent)
 constexpr int kBldMaxWords = (kBldMaxTL + 2 * 2 * kMaxSteps + kBldRC + 31) / 32 + 1;
 constexpr int kPoolThreads = 1024;  // masked-pool finish: 32 columns x 32 tile strides
 
@@ -106,6 +115,13 @@ struct BldArgs {
   const void* g_lo_ext;
   const void* g_hi_ext;
   int g_hext_lo, g_hext_hi;
+  // forward diffusion with 16-bit I/O: the contracted update (one fma for
+  // c + alpha * lap, the reference's Triton op order) instead of the exact one
+  int contract;
+  // test hook (forward march only, 0 = off): CTA (0, 0, 0) waits this many
+  // microseconds on an mbarrier phase that nothing completes, then takes the
+  // timeout path (error word, drain of its issued loads, early exit)
+  int debug_stall_us;
 };
 
 // ---------------------------------------------------------------------------
@@ -143,6 +159,8 @@ struct BdlArgs {
   int alpha_dev_dtype;
   // TMA form: windows per CTA and CTAs per row pair
   int tw, nseg;
+  // forward with 16-bit I/O: the contracted update (see BldArgs::contract)
+  int contract;
 };
 
 // launch march kernels with programmatic dependent launch (tuning key 3)
@@ -151,7 +169,7 @@ int pdl_enabled();
 // launchers (return cudaError_t of the launch)
 // resident one-warp CTAs per SM of a march kernel variant on the current device
 // (occupancy query, cached), or -1
-int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual = 0);
+int bld_march_ctas_per_sm(int dtype, int steps, int causal, int adjoint, int residual = 0, int contract = 0);
 // reduces the pooled partials of a POOL march launch with `ntl` row tiles into
 // pooled [nbatch, D] of the tensor dtype
 cudaError_t launch_pool_finish(const BldArgs& a, int dtype, int64_t ntl, void* pooled, cudaStream_t st);
@@ -160,29 +178,25 @@ cudaError_t launch_pool_finish(const BldArgs& a, int dtype, int64_t ntl, void* p
 cudaError_t launch_bld_fwd(const BldArgs& a, const CUtensorMap* xmap, const CUtensorMap* ymap,
                            const CUtensorMap* rmap, int dtype, int steps, int causal, int adjoint, dim3 grid,
                            size_t smem, cudaStream_t st);
-cudaError_t launch_bld_bwd(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap, int dtype,
-                           int steps, int causal, int with_dalpha, dim3 grid, size_t smem, cudaStream_t st);
 cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st);
 // [B, D, L] TMA form: in map box {kBdlWin, kBdlRows}, out map box {kBdlOut, kBdlRows}
 cudaError_t launch_bdl_march(const BdlArgs& a, const CUtensorMap* imap, const CUtensorMap* omap, int dtype,
                              int steps, int causal, int backward, unsigned grid, cudaStream_t st);
-int bdl_march_ctas_per_sm(int dtype, int steps, int causal, int backward);
+int bdl_march_ctas_per_sm(int dtype, int steps, int causal, int backward, int contract = 0);
 size_t bdl_march_smem_bytes(int dtype);
 
 // march kernel with d(alpha), steps 1..kDaMaxSteps
 cudaError_t launch_bld_dalpha(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap,
                               const CUtensorMap* ymap, int dtype, int steps, int causal, dim3 grid, cudaStream_t st);
 int bld_dalpha_ctas_per_sm(int dtype, int steps, int causal);
-size_t dalpha_smem_bytes(int dtype);
+size_t dalpha_smem_bytes(int dtype, int steps, int causal);
 int read_device_error_bld_dalpha(int clear);
 
 // sets the thread-local message returned by cta_last_error()
 void set_last_error(const char* fmt, ...) __attribute__((format(printf, 1, 2)));
 
-size_t bld_smem_bytes(int dtype, int with_x_stream);
 size_t fwd_smem_bytes(int dtype);
 int read_device_error_bld_fwd(int clear);
-int read_device_error_bld_bwd(int clear);
 int read_device_error_bdl(int clear);
 
 }  // namespace cta

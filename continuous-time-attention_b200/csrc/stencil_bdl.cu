@@ -176,9 +176,12 @@ __device__ __forceinline__ void bdl_smem_store_pairs(T* ra, T* rb, const pf2 (&e
 // independent windows packed in the halves of each pair), in registers; the
 // neighbours of a lane's first and last position come from the adjacent lanes.
 // fa / fb: fixed-position bits of the two windows (SLOW only).
-template <int S, bool CAUSAL, bool BWD, bool SLOW>
+// MODE 0: forward; 1: adjoint; 2: forward with the contracted update (pst_nc).
+template <int S, bool CAUSAL, int MODE, bool SLOW>
 __device__ __forceinline__ void window_levels(pf2 (&e)[E8], uint32_t fa, uint32_t fb, const float (&al)[kMaxSteps],
                                               pf2 m2, pf2 zn) {
+  constexpr bool BWD = MODE == 1;
+  constexpr bool FM = MODE == 2;
 #pragma unroll
   for (int s = 0; s < S; ++s) {
     if (!BWD) {
@@ -190,7 +193,7 @@ __device__ __forceinline__ void window_levels(pf2 (&e)[E8], uint32_t fa, uint32_
         for (int i = 0; i < E8; ++i) {
           const pf2 p2 = i >= 2 ? e[i - 2] : (i == 1 ? m1n : m2n);
           const pf2 p1 = i >= 1 ? e[i - 1] : m1n;
-          n[i] = pst_c(p2, p1, e[i], alv, m2, zn);
+          n[i] = pst_c<FM>(p2, p1, e[i], alv, m2, zn);
         }
       } else {
         const pf2 lft = shfl_up_p(e[E8 - 1], 1), rgt = shfl_down_p(e[0], 1);
@@ -198,7 +201,7 @@ __device__ __forceinline__ void window_levels(pf2 (&e)[E8], uint32_t fa, uint32_
         for (int i = 0; i < E8; ++i) {
           const pf2 l = i > 0 ? e[i - 1] : lft;
           const pf2 r = i < E8 - 1 ? e[i + 1] : rgt;
-          n[i] = pst_nc(l, e[i], r, alv, m2, zn);
+          n[i] = pst_nc<FM>(l, e[i], r, alv, m2, zn);
         }
       }
 #pragma unroll
@@ -238,8 +241,9 @@ __device__ __forceinline__ void window_levels(pf2 (&e)[E8], uint32_t fa, uint32_
 
 }  // namespace
 
-template <typename T, int S, bool CAUSAL, bool BWD>
+template <typename T, int S, bool CAUSAL, int MODE>
 __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
+  constexpr bool BWD = MODE == 1;
   // halo lanes: the one-sided causal stencil reaches 2*S <= 16 positions to
   // the left (forward) or right (adjoint); the centred one S <= 8 each side.
   constexpr int HLN = CAUSAL ? (BWD ? 0 : 2) : 1;
@@ -288,8 +292,8 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
   const pf2 m2 = pbc(-2.f);
   const pf2 zn = pbc(a.neg_zero);
 
-  if (slow) window_levels<S, CAUSAL, BWD, true>(e, fa, fb, al, m2, zn);
-  else window_levels<S, CAUSAL, BWD, false>(e, fa, fb, al, m2, zn);
+  if (slow) window_levels<S, CAUSAL, MODE, true>(e, fa, fb, al, m2, zn);
+  else window_levels<S, CAUSAL, MODE, false>(e, fa, fb, al, m2, zn);
 
   if (lane >= HLN && lane < 32 - HRN) {
 #pragma unroll
@@ -308,10 +312,11 @@ __global__ void __launch_bounds__(kBdlThreads) bdl_kernel(const BdlArgs a) {
 // through a staged TMA store, so loads, arithmetic and stores of successive
 // windows overlap inside the warp.
 // ---------------------------------------------------------------------------
-template <typename T, int S, bool CAUSAL, bool BWD>
+template <typename T, int S, bool CAUSAL, int MODE>
 __global__ void __launch_bounds__(32, 16)
     bdl_march_kernel(const __grid_constant__ CUtensorMap imap, const __grid_constant__ CUtensorMap omap,
                      const BdlArgs a) {
+  constexpr bool BWD = MODE == 1;
   constexpr int HLN = CAUSAL ? (BWD ? 0 : 2) : 1;
   constexpr int HRN = CAUSAL ? (BWD ? 2 : 0) : 1;
   constexpr int NST = kBdlStages;
@@ -375,9 +380,9 @@ __global__ void __launch_bounds__(32, 16)
           fb = fixed_bits<CAUSAL>(a, r0 + 2 * q + 1, p, r0 + 2 * q + 1 < a.rows);
         }
         if (!interior && __any_sync(0xffffffffu, (fa | fb) != 0u))
-          window_levels<S, CAUSAL, BWD, true>(e, fa, fb, al, m2, zn);
+          window_levels<S, CAUSAL, MODE, true>(e, fa, fb, al, m2, zn);
         else
-          window_levels<S, CAUSAL, BWD, false>(e, fa, fb, al, m2, zn);
+          window_levels<S, CAUSAL, MODE, false>(e, fa, fb, al, m2, zn);
         if (lane >= HLN && lane < 32 - HRN) {
           T* st = stage + (i & 1) * OUT_SLOT + (2 * q) * kBdlOut + (lane - HLN) * E8;
           bdl_smem_store_pairs<T>(st, st + kBdlOut, e);
@@ -409,80 +414,94 @@ __global__ void __launch_bounds__(32, 16)
 
 namespace {
 
-template <typename T, int S, bool C, bool B>
+template <typename T, int S, bool C, int M>
 cudaError_t launch_t(const BdlArgs& a, cudaStream_t st) {
   const int64_t nwin = (a.L + kBdlOut - 1) / kBdlOut;
   const int64_t pairs = (a.rows * nwin + 1) / 2;
   const int64_t blocks = (pairs * 32 + kBdlThreads - 1) / kBdlThreads;
   if (blocks <= 0) return cudaSuccess;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-  bdl_kernel<T, S, C, B><<<static_cast<unsigned>(blocks), kBdlThreads, 0, st>>>(a);
+  bdl_kernel<T, S, C, M><<<static_cast<unsigned>(blocks), kBdlThreads, 0, st>>>(a);
   return cudaGetLastError();
 }
 
-template <typename T, bool C, bool B>
+template <typename T, bool C, int M>
 cudaError_t by_steps(const BdlArgs& a, int steps, cudaStream_t st) {
   switch (steps) {
-    case 1: return launch_t<T, 1, C, B>(a, st);
-    case 2: return launch_t<T, 2, C, B>(a, st);
-    case 3: return launch_t<T, 3, C, B>(a, st);
-    case 4: return launch_t<T, 4, C, B>(a, st);
-    case 5: return launch_t<T, 5, C, B>(a, st);
-    case 6: return launch_t<T, 6, C, B>(a, st);
-    case 7: return launch_t<T, 7, C, B>(a, st);
-    case 8: return launch_t<T, 8, C, B>(a, st);
+    case 1: return launch_t<T, 1, C, M>(a, st);
+    case 2: return launch_t<T, 2, C, M>(a, st);
+    case 3: return launch_t<T, 3, C, M>(a, st);
+    case 4: return launch_t<T, 4, C, M>(a, st);
+    case 5: return launch_t<T, 5, C, M>(a, st);
+    case 6: return launch_t<T, 6, C, M>(a, st);
+    case 7: return launch_t<T, 7, C, M>(a, st);
+    case 8: return launch_t<T, 8, C, M>(a, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
-template <typename T, int S, bool C, bool B>
+template <typename T, int S, bool C, int M>
 const void* march_ptr_s() {
-  return reinterpret_cast<const void*>(bdl_march_kernel<T, S, C, B>);
+  return reinterpret_cast<const void*>(bdl_march_kernel<T, S, C, M>);
 }
 
-template <typename T, bool C, bool B>
+template <typename T, bool C, int M>
 const void* march_ptr(int steps) {
   switch (steps) {
-    case 1: return march_ptr_s<T, 1, C, B>();
-    case 2: return march_ptr_s<T, 2, C, B>();
-    case 3: return march_ptr_s<T, 3, C, B>();
-    case 4: return march_ptr_s<T, 4, C, B>();
-    case 5: return march_ptr_s<T, 5, C, B>();
-    case 6: return march_ptr_s<T, 6, C, B>();
-    case 7: return march_ptr_s<T, 7, C, B>();
-    case 8: return march_ptr_s<T, 8, C, B>();
+    case 1: return march_ptr_s<T, 1, C, M>();
+    case 2: return march_ptr_s<T, 2, C, M>();
+    case 3: return march_ptr_s<T, 3, C, M>();
+    case 4: return march_ptr_s<T, 4, C, M>();
+    case 5: return march_ptr_s<T, 5, C, M>();
+    case 6: return march_ptr_s<T, 6, C, M>();
+    case 7: return march_ptr_s<T, 7, C, M>();
+    case 8: return march_ptr_s<T, 8, C, M>();
     default: return nullptr;
   }
 }
 
+// mode: 0 forward, 1 adjoint, 2 forward with the contracted update (16-bit I/O only)
 template <typename T>
-const void* march_ptr_t(int steps, int causal, int bwd) {
-  if (causal) return bwd ? march_ptr<T, true, true>(steps) : march_ptr<T, true, false>(steps);
-  return bwd ? march_ptr<T, false, true>(steps) : march_ptr<T, false, false>(steps);
+const void* march_ptr_t(int steps, int causal, int mode) {
+  if (mode == 2) {
+    if constexpr (sizeof(T) == 2) return causal ? march_ptr<T, true, 2>(steps) : march_ptr<T, false, 2>(steps);
+    return nullptr;
+  }
+  if (causal) return mode ? march_ptr<T, true, 1>(steps) : march_ptr<T, true, 0>(steps);
+  return mode ? march_ptr<T, false, 1>(steps) : march_ptr<T, false, 0>(steps);
 }
 
-const void* bdl_march_ptr(int dtype, int steps, int causal, int bwd) {
+const void* bdl_march_ptr(int dtype, int steps, int causal, int mode) {
   switch (dtype) {
-    case kF32: return march_ptr_t<float>(steps, causal, bwd);
-    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, bwd);
-    case kF16: return march_ptr_t<__half>(steps, causal, bwd);
+    case kF32: return march_ptr_t<float>(steps, causal, mode);
+    case kBF16: return march_ptr_t<__nv_bfloat16>(steps, causal, mode);
+    case kF16: return march_ptr_t<__half>(steps, causal, mode);
     default: return nullptr;
   }
 }
 
 template <typename T>
-cudaError_t by_mode(const BdlArgs& a, int steps, int causal, int bwd, cudaStream_t st) {
-  if (causal) return bwd ? by_steps<T, true, true>(a, steps, st) : by_steps<T, true, false>(a, steps, st);
-  return bwd ? by_steps<T, false, true>(a, steps, st) : by_steps<T, false, false>(a, steps, st);
+cudaError_t by_mode(const BdlArgs& a, int steps, int causal, int mode, cudaStream_t st) {
+  if (mode == 2) {
+    if constexpr (sizeof(T) == 2)
+      return causal ? by_steps<T, true, 2>(a, steps, st) : by_steps<T, false, 2>(a, steps, st);
+    return cudaErrorInvalidValue;
+  }
+  if (causal) return mode ? by_steps<T, true, 1>(a, steps, st) : by_steps<T, true, 0>(a, steps, st);
+  return mode ? by_steps<T, false, 1>(a, steps, st) : by_steps<T, false, 0>(a, steps, st);
 }
+
+// kernel mode of a call: the adjoint, or the forward in the call's arithmetic
+int bdl_mode(const BdlArgs& a, int backward) { return backward ? 1 : (a.contract ? 2 : 0); }
 
 }  // namespace
 
 cudaError_t launch_bdl(const BdlArgs& a, int dtype, int steps, int causal, int backward, cudaStream_t st) {
+  const int mode = bdl_mode(a, backward);
   switch (dtype) {
-    case kF32: return by_mode<float>(a, steps, causal, backward, st);
-    case kBF16: return by_mode<__nv_bfloat16>(a, steps, causal, backward, st);
-    case kF16: return by_mode<__half>(a, steps, causal, backward, st);
+    case kF32: return by_mode<float>(a, steps, causal, mode, st);
+    case kBF16: return by_mode<__nv_bfloat16>(a, steps, causal, mode, st);
+    case kF16: return by_mode<__half>(a, steps, causal, mode, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -494,15 +513,15 @@ size_t bdl_march_smem_bytes(int dtype) {
 
 cudaError_t launch_bdl_march(const BdlArgs& a, const CUtensorMap* imap, const CUtensorMap* omap, int dtype,
                              int steps, int causal, int backward, unsigned grid, cudaStream_t st) {
-  const void* kern = bdl_march_ptr(dtype, steps, causal, backward);
+  const void* kern = bdl_march_ptr(dtype, steps, causal, bdl_mode(a, backward));
   if (kern == nullptr) return cudaErrorInvalidValue;
   const size_t smem = bdl_march_smem_bytes(dtype);
   void* args[] = {const_cast<CUtensorMap*>(imap), const_cast<CUtensorMap*>(omap), const_cast<BdlArgs*>(&a)};
   return cudaLaunchKernel(kern, dim3(grid), dim3(32), args, smem, st);
 }
 
-int bdl_march_ctas_per_sm(int dtype, int steps, int causal, int backward) {
-  const void* kern = bdl_march_ptr(dtype, steps, causal, backward);
+int bdl_march_ctas_per_sm(int dtype, int steps, int causal, int backward, int contract) {
+  const void* kern = bdl_march_ptr(dtype, steps, causal, backward ? 1 : (contract ? 2 : 0));
   if (kern == nullptr) return -1;
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 32, bdl_march_smem_bytes(dtype)) != cudaSuccess)

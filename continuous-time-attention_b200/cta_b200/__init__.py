@@ -18,4 +18,22 @@ from .diffusion import (  # noqa: F401
     diffusion_triton_fused,
 )
 
-__version__ = "0.1.0"
+__version__ = "0.2.0"
+
+
+def set_arithmetic(mode: str) -> str:
+    """Process default of the forward update's arithmetic for bf16 / fp16
+    tensors, returning the previous one:
+
+    * ``"contracted"`` (initial): ``c + alpha * lap`` as one fused multiply-add,
+      the op order the reference's Triton kernels compile to
+      (kernels/diffusion_triton.py); within one bf16 / fp16 rounding of the
+      exact result;
+    * ``"exact"``: the product and the sum rounded separately, the reference's
+      PyTorch ops (src/cta/ops/diffusion.py, src/models/pde_layers.py), bit for
+      bit.
+
+    fp32 tensors, the backward kernels and the PDE layers always use the exact
+    arithmetic (the layers replace the reference's PyTorch layers)."""
+    prev = _lib.load().cta_set_arithmetic(_lib.arith_code(mode))
+    return "exact" if prev == _lib.ARITH_EXACT else "contracted"

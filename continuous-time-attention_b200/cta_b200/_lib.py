@@ -26,6 +26,8 @@ CTA_OK, CTA_EINVAL, CTA_EUNSUPPORTED, CTA_ECUDA = 0, 1, 2, 3
 SHARD_INTERIOR, SHARD_LO_EDGE, SHARD_HI_EDGE = 0, 1, 2
 PDE_ADVECTION, PDE_REACTION = 0, 1
 MAX_STEPS = 8
+ARITH_EXACT, ARITH_CONTRACTED = 0, 1
+_ARITH_CODES = {"exact": ARITH_EXACT, "contracted": ARITH_CONTRACTED}
 
 _DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 _MASK_CODES = {
@@ -45,6 +47,8 @@ _SIGNATURES = {
     "cta_last_error": (ctypes.c_char_p, []),
     "cta_device_error": (c_int, [c_int]),
     "cta_set_tuning": (c_int, [c_int, c_int]),
+    "cta_set_arithmetic": (c_int, [c_int]),
+    "cta_set_thread_arithmetic": (c_int, [c_int]),
     "cta_diffusion_fwd_bdl": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_float,
                                       c_void_p]),
     "cta_diffusion_bwd_bdl": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_float,
@@ -205,3 +209,34 @@ def device_error(clear: bool = True) -> int:
 
 def set_tuning(key: int, value: int) -> int:
     return int(load().cta_set_tuning(int(key), int(value)))
+
+
+def arith_code(mode) -> int:
+    """'exact' / 'contracted' (or the integer code) -> the C ABI's code."""
+    if isinstance(mode, int) and mode in (ARITH_EXACT, ARITH_CONTRACTED):
+        return mode
+    try:
+        return _ARITH_CODES[mode]
+    except KeyError:
+        raise ValueError(f"arithmetic must be 'exact' or 'contracted', got {mode!r}") from None
+
+
+class thread_arithmetic:
+    """Run the enclosed calls of this thread with the given forward arithmetic
+    (None: leave the current setting), restoring the previous override after."""
+
+    __slots__ = ("code", "prev")
+
+    def __init__(self, mode):
+        self.code = None if mode is None else arith_code(mode)
+        self.prev = None
+
+    def __enter__(self):
+        if self.code is not None:
+            self.prev = load().cta_set_thread_arithmetic(self.code)
+        return self
+
+    def __exit__(self, *exc):
+        if self.code is not None:
+            load().cta_set_thread_arithmetic(self.prev)
+        return False

@@ -26,7 +26,7 @@ BUILD_DIR = SRC_ROOT / "_build"
 LIB_NAME = "libcta_stencil.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["capi.cu", "bld_fwd.cu", "bld_bwd.cu", "bld_dalpha.cu", "stencil_bdl.cu", "noalloc.cu"]
+SOURCES = ["capi.cu", "bld_fwd.cu", "bld_dalpha.cu", "stencil_bdl.cu", "noalloc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = [
     "-O3",
@@ -66,7 +66,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None, d
           out: Path | None = None) -> Path:
     """Compile every kernel translation unit for sm_100a and link the library.
 
-    `defines` (e.g. ("CTA_FWD_VEC=2",)) and `out` build a tuning variant into
+    `defines` (e.g. ("CTA_FWD_STAGES=4",)) and `out` build a tuning variant into
     another file; the default build is the in-tree libcta_stencil.so.
     """
     target = Path(out) if out is not None else LIB_PATH

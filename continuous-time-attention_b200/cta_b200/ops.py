@@ -91,8 +91,12 @@ def bdl(
     backward: bool = False,
     mask: Optional[torch.Tensor] = None,
     out: Optional[torch.Tensor] = None,
+    arith: Optional[str] = None,
 ) -> torch.Tensor:
-    """`steps` fused steps (or their adjoint) on a contiguous [B, D, L] tensor."""
+    """`steps` fused steps (or their adjoint) on a contiguous [B, D, L] tensor.
+
+    `arith` ("exact" / "contracted", None = the process default) selects the
+    forward update's arithmetic for 16-bit tensors (cta_b200.set_arithmetic)."""
     _require_cuda(x, "x")
     if x.dim() != 3:
         raise ValueError("x must have shape (B, D, L)")
@@ -103,7 +107,7 @@ def bdl(
     fa, pa, pcode, keep = _alpha_args(alphas, steps, x.device)
     m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
     lib = _lib.load()
-    with _lib.on_device(x):
+    with _lib.on_device(x), _lib.thread_arithmetic(arith):
         rc = lib.cta_diffusion_bdl_ex(
             _lib.ptr(x), _lib.ptr(y), B, D, L, x.stride(1), y.stride(1), _lib.dtype_code(x.dtype), steps,
             int(causal), int(backward), fa, pa, pcode, _lib.ptr(m), mcode, msb, msl, _lib.stream_ptr(x),
@@ -114,7 +118,7 @@ def bdl(
 
 
 def bdl_simple(x: torch.Tensor, alpha: float, steps: int, backward: bool = False,
-               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+               out: Optional[torch.Tensor] = None, arith: Optional[str] = None) -> torch.Tensor:
     """Reference kernel API path: one host alpha, no mask, non-causal."""
     _require_cuda(x, "x")
     if not x.is_contiguous():
@@ -123,7 +127,7 @@ def bdl_simple(x: torch.Tensor, alpha: float, steps: int, backward: bool = False
     y = _out(out, x.shape, x, contiguous=True)
     lib = _lib.load()
     fn = lib.cta_diffusion_bwd_bdl if backward else lib.cta_diffusion_fwd_bdl
-    with _lib.on_device(x):
+    with _lib.on_device(x), _lib.thread_arithmetic(arith):
         rc = fn(_lib.ptr(x), _lib.ptr(y), B, D, L, L, _lib.dtype_code(x.dtype), steps, float(alpha),
                 _lib.stream_ptr(x))
     _lib.check(rc)
@@ -148,11 +152,14 @@ def bld_forward(
     mask: Optional[torch.Tensor] = None,
     out: Optional[torch.Tensor] = None,
     residual: Optional[torch.Tensor] = None,
+    arith: Optional[str] = None,
 ) -> torch.Tensor:
     """`steps` fused steps on [B, L, D] (feature axis contiguous), one launch.
 
     With `residual` (non-causal, host alphas) the same launch returns
-    residual + stencil(x), equal bit for bit to the two-pass result."""
+    residual + stencil(x), equal bit for bit to the two-pass result.  `arith`
+    ("exact" / "contracted", None = the process default) selects the update's
+    arithmetic for 16-bit tensors (cta_b200.set_arithmetic)."""
     _require_cuda(x, "x")
     if x.dim() != 3:
         raise ValueError("x must have shape (B, L, D)")
@@ -166,7 +173,7 @@ def bld_forward(
         r = _residual_view(residual, (B, L, D), x)
         if causal or pa is not None:
             raise ValueError("the fused residual add takes the non-causal stencil with host alphas")
-        with _lib.on_device(x):
+        with _lib.on_device(x), _lib.thread_arithmetic(arith):
             rc = lib.cta_diffusion_fwd_bld_residual(
                 _lib.ptr(x), _lib.ptr(r), _lib.ptr(y), B, L, D, x.stride(0), x.stride(1), r.stride(0), r.stride(1),
                 y.stride(0), y.stride(1), _lib.dtype_code(x.dtype), steps, fa, _lib.ptr(m), mcode, msb, msl,
@@ -175,7 +182,7 @@ def bld_forward(
         del keep
         _lib.check(rc)
         return y
-    with _lib.on_device(x):
+    with _lib.on_device(x), _lib.thread_arithmetic(arith):
         rc = lib.cta_diffusion_fwd_bld(
             _lib.ptr(x), _lib.ptr(y), B, L, D, x.stride(0), x.stride(1), y.stride(0), y.stride(1),
             _lib.dtype_code(x.dtype), steps, int(causal), fa, pa, pcode, _lib.ptr(m), mcode, msb, msl,
@@ -186,22 +193,35 @@ def bld_forward(
     return y
 
 
-_WS: dict = {}
+_WS: "OrderedDict" = None  # (device, stream, tag) -> buffer, most recently used last
+_WS_PER_DEVICE = 8
 
 
 def _workspace(device: torch.device, nbytes: int, tag: str = "dalpha") -> torch.Tensor:
-    """Zero-initialised scratch, one per (device, stream, tag).
+    """Zero-initialised scratch, one per (device, stream, tag), at most
+    _WS_PER_DEVICE per device (least recently used dropped first).
 
     "dalpha": the d(alpha) reductions; their kernels leave the completion
     counters at zero, so the buffer stays reusable without clearing between
     calls on the same stream.  Other users take their own tag, so that nothing
-    else ever writes into those counters.
+    else ever writes into those counters.  A buffer is only ever used on the
+    stream it was allocated on, so dropping it hands its memory back to torch's
+    stream-ordered caching allocator without a race against kernels in flight.
     """
+    global _WS
+    if _WS is None:
+        from collections import OrderedDict
+
+        _WS = OrderedDict()
     key = (device, torch.cuda.current_stream(device).cuda_stream, tag)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=device)
         _WS[key] = buf
+        same = [k for k in _WS if k[0] == device]
+        for k in same[: max(0, len(same) - _WS_PER_DEVICE)]:
+            del _WS[k]
+    _WS.move_to_end(key)
     return buf
 
 
@@ -260,6 +280,7 @@ def varlen_forward(
     pad_to_max: bool,
     out: Optional[torch.Tensor] = None,
     residual: Optional[torch.Tensor] = None,
+    arith: Optional[str] = None,
 ) -> torch.Tensor:
     """Packed [T, D] prefill with device cu_seqlens (int32, nseq+1); one launch."""
     _require_cuda(x, "x")
@@ -279,7 +300,7 @@ def varlen_forward(
     lib = _lib.load()
     if residual is not None:
         r = _residual_view(residual, (T, D), x)
-        with _lib.on_device(x):
+        with _lib.on_device(x), _lib.thread_arithmetic(arith):
             rc = lib.cta_diffusion_fwd_varlen_residual(
                 _lib.ptr(x), _lib.ptr(r), _lib.ptr(y), T, D, x.stride(0), r.stride(0), y.stride(0),
                 _lib.ptr(cu_seqlens), nseq, int(max_len), int(pad_to_max), _lib.dtype_code(x.dtype), steps,
@@ -287,7 +308,7 @@ def varlen_forward(
             )
         _lib.check(rc)
         return y
-    with _lib.on_device(x):
+    with _lib.on_device(x), _lib.thread_arithmetic(arith):
         rc = lib.cta_diffusion_fwd_varlen(
             _lib.ptr(x), _lib.ptr(y), T, D, x.stride(0), y.stride(0), _lib.ptr(cu_seqlens), nseq, int(max_len),
             int(pad_to_max), _lib.dtype_code(x.dtype), steps, float(alpha), _lib.stream_ptr(x),
@@ -310,6 +331,7 @@ def shard_part(
     lo_halo: Optional[torch.Tensor] = None,
     hi_halo: Optional[torch.Tensor] = None,
     stream: Optional[torch.cuda.Stream] = None,
+    arith: Optional[str] = None,
 ) -> None:
     """One launch over a part (interior / lo edge / hi edge) of an L-shard."""
     B, Lloc, D = x_local.shape
@@ -320,7 +342,7 @@ def shard_part(
     hi_rows = hi_halo.shape[1] if hi_halo is not None else 0
     st = stream if stream is not None else torch.cuda.current_stream(x_local.device)
     lib = _lib.load()
-    with _lib.on_device(x_local):
+    with _lib.on_device(x_local), _lib.thread_arithmetic(arith):
         rc = lib.cta_diffusion_shard_bld(
             _lib.ptr(x_local), _lib.ptr(out), B, Lloc, D, int(pos_offset), int(global_len), _lib.ptr(lo_halo),
             lo_rows, _lib.ptr(hi_halo), hi_rows, int(part), _lib.dtype_code(x_local.dtype), steps, int(causal),

@@ -23,8 +23,9 @@ Drop-in for the diffusion family of the reference's src/models/pde_layers.py:
 
 Arithmetic follows the reference op by op (fp32, no fused multiply-add), so a
 single fp32 or bf16 diffusion, wave or advection layer step is bit-identical to
-the reference layer; the reaction layer's sigmoid uses CUDA's expf, so it
-matches to fp32 rounding.
+the reference layer; the reaction layer's sigmoid uses the fast intrinsic
+``__expf`` with a rounded reciprocal (``__frcp_rn``), so it matches to fp32
+rounding rather than bit for bit.
 """
 from __future__ import annotations
 
@@ -51,7 +52,7 @@ class _StackBLD(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, mask, causal, *alphas):
         steps = len(alphas)
-        y = ops.bld_forward(x, list(alphas), steps, causal=causal, mask=mask)
+        y = ops.bld_forward(x, list(alphas), steps, causal=causal, mask=mask, arith="exact")
         ctx.causal = causal
         ctx.steps = steps
         ctx.save_for_backward(x, mask, *alphas)
@@ -82,7 +83,7 @@ class _StackBDL(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, mask, causal, *alphas):
         steps = len(alphas)
-        y = ops.bdl(x, list(alphas), steps, causal=causal, mask=mask)
+        y = ops.bdl(x, list(alphas), steps, causal=causal, mask=mask, arith="exact")
         ctx.causal = causal
         ctx.steps = steps
         ctx.save_for_backward(x, mask, *alphas)

@@ -68,6 +68,23 @@ def _to_int(value: object) -> Optional[int]:
     return None
 
 
+def _max_query_len(attn_metadata: object) -> Optional[int]:
+    """max_query_len of the batch as a host int, without a device sync where the
+    metadata allows it.
+
+    vLLM 0.22's v1 metadata (``FlashAttentionMetadata``,
+    ``CommonAttentionMetadata``) carries it as a Python int.  A device tensor is
+    read through the metadata's host copy of the offsets (``query_start_loc_cpu``)
+    when there is one; only otherwise does it cost a ``.item()`` sync, as in the
+    reference (src/cta/serving_vllm.py:64-69, :292)."""
+    value = getattr(attn_metadata, "max_query_len", None)
+    if isinstance(value, torch.Tensor) and value.numel() == 1 and value.device.type != "cpu":
+        host = getattr(attn_metadata, "query_start_loc_cpu", None)
+        if isinstance(host, torch.Tensor) and host.numel() >= 2:
+            return int((host[1:] - host[:-1]).max())
+    return _to_int(value)
+
+
 @dataclass
 class CtaConfig:
     """src/cta/serving_vllm.py:135-150, plus two fields of this build."""
@@ -119,6 +136,17 @@ class CtaPostAttnMixer(nn.Module):
             steps = self.config.steps
         return min(self.config.max_steps, int(steps))
 
+    def _arith(self):
+        """The arithmetic of the reference path this call replaces: its Triton
+        kernels (use_triton, with allow_transpose for the [B, L, D] layout)
+        contract c + alpha * lap into one fma, its PyTorch fallback
+        (src/cta/serving_vllm.py:268-273) rounds the product and the sum
+        separately.  None: the process default."""
+        cfg = self.config
+        if not cfg.use_triton or (cfg.layout == "bld" and not cfg.allow_transpose):
+            return "exact"
+        return None
+
     def _fused_ok(self, steps: int) -> bool:
         if not self.config.fused:
             return False
@@ -166,7 +194,7 @@ class CtaPostAttnMixer(nn.Module):
             return x, False
         ctx = record_function("cta_post_attn_mixer") if self.config.trace else nullcontext()
         alpha = float(self.config.alpha)
-        with ctx:
+        with ctx, _lib.thread_arithmetic(self._arith()):
             if self._fused_ok(steps):
                 out = x
                 for i in range(0, steps, _lib.MAX_STEPS):
@@ -203,6 +231,30 @@ class CtaPostAttnMixer(nn.Module):
         """Packed [T, H] prefill (src/cta/serving_vllm.py:275-303), one launch."""
         return self._mix_packed(x, attn_metadata=attn_metadata, is_prefill=is_prefill, residual=None)[0]
 
+    def _packed_plan(self, attn_metadata: Optional[object], is_prefill: Optional[bool]):
+        """The gate of src/cta/serving_vllm.py:281-298 on the metadata alone:
+        None (x passes through unchanged) or (query_start_loc as given,
+        max_query_len as a host int, steps)."""
+        if not self.config.enabled:
+            return None
+        if attn_metadata is None:
+            return None
+        if self.config.prefill_only:
+            if is_prefill is None:
+                is_prefill = _infer_prefill(attn_metadata)
+            if not is_prefill:
+                return None
+        max_query_len = _max_query_len(attn_metadata)
+        query_start_loc = getattr(attn_metadata, "query_start_loc", None)
+        if max_query_len is None or query_start_loc is None:
+            return None
+        if max_query_len < 3:
+            return None
+        steps = self._resolve_steps(max_query_len)
+        if steps <= 0:
+            return None
+        return query_start_loc, max_query_len, steps
+
     def _mix_packed(
         self,
         x: torch.Tensor,
@@ -212,32 +264,29 @@ class CtaPostAttnMixer(nn.Module):
         residual: Optional[torch.Tensor] = None,
     ):
         """_forward_packed, optionally with the residual add fused into the last
-        launch.  Returns (output, residual already added)."""
-        if not self.config.enabled:
+        launch.  Returns (output, residual already added).
+
+        vLLM 0.22 (v1 engine) metadata has no prefill flag, so, as in the
+        reference's ``_infer_prefill``, a packed batch counts as prefill and every
+        sequence of it goes through the stencil, decodes included.  A decode row
+        (query length 1) is unchanged under both rules: a one-row sequence is its
+        own boundary row.  A speculative-decode sequence of two rows changes
+        under the reference rule (zero padding to max_query_len makes its last
+        row interior) exactly as in the reference, and is unchanged under
+        ``varlen_mode="sequence"`` (sequences shorter than 3 rows are the
+        identity).  Rows after the last sequence (padding tokens of a CUDA-graph
+        batch) are not written, as the reference's unpack leaves them."""
+        plan = self._packed_plan(attn_metadata, is_prefill)
+        if plan is None:
             return x, False
-        if attn_metadata is None:
-            return x, False
-        if self.config.prefill_only:
-            if is_prefill is None:
-                is_prefill = _infer_prefill(attn_metadata)
-            if not is_prefill:
-                return x, False
-        max_query_len = _to_int(getattr(attn_metadata, "max_query_len", None))
-        query_start_loc = getattr(attn_metadata, "query_start_loc", None)
-        if max_query_len is None or query_start_loc is None:
-            return x, False
-        if max_query_len < 3:
-            return x, False
-        steps = self._resolve_steps(max_query_len)
-        if steps <= 0:
-            return x, False
+        query_start_loc, max_query_len, steps = plan
         if x.device.type != "cuda":
             raise ValueError("x must be on CUDA")
         cu = self._device_qsl(query_start_loc, x.device)
         pad = self.config.varlen_mode == "reference"
         alpha = float(self.config.alpha)
         ctx = record_function("cta_post_attn_mixer") if self.config.trace else nullcontext()
-        with ctx:
+        with ctx, _lib.thread_arithmetic(self._arith()):
             out = x
             for i in range(0, steps, _lib.MAX_STEPS):
                 s = min(_lib.MAX_STEPS, steps - i)

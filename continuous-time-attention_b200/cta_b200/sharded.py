@@ -76,6 +76,26 @@ def partition(spec: ShardSpec, steps: int, causal: bool, backward: bool) -> dict
     return {_lib.SHARD_INTERIOR: (ib, ie), _lib.SHARD_LO_EDGE: (0, ib), _lib.SHARD_HI_EDGE: (ie, L)}
 
 
+class _PartEvents:
+    """Records (start, end) CUDA event pairs per part into a caller's dict."""
+
+    def __init__(self, sink: Optional[dict]):
+        self.sink = sink
+        self.open: dict = {}
+
+    def begin(self, name: str, stream) -> None:
+        if self.sink is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            self.open[name] = e
+
+    def end(self, name: str, stream) -> None:
+        if self.sink is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            self.sink.setdefault(name, []).append((self.open.pop(name), e))
+
+
 def _default_compute(part, x_local, out, *, lo_halo, hi_halo, spec, alpha, steps, causal, backward):
     from . import ops
 
@@ -94,11 +114,17 @@ def sharded_diffusion(
     group: Optional[dist.ProcessGroup] = None,
     comm_stream: Optional[torch.cuda.Stream] = None,
     compute: Optional[Callable] = None,
+    timing: Optional[dict] = None,
 ) -> torch.Tensor:
     """Fused `steps`-step stencil (or its adjoint) of this rank's shard.
 
     Every rank must call this with the same steps / causal / backward; ranks
     exchange halos with their neighbours only.  Returns the local output shard.
+    `timing` (CUDA only): a dict that receives pairs of recorded CUDA events per
+    part -- "interior" (the interior kernel), "exchange" (the halo send/recv on the
+    comm stream), "exposed_wait" (compute stream idle between the interior kernel
+    and the halos' arrival) and "edges" (both edge kernels) -- for the caller to
+    read after a synchronize.
     """
     if x_local.dim() != 3:
         raise ValueError("x_local must be (B, L_local, D)")
@@ -140,16 +166,23 @@ def sharded_diffusion(
         return dist.batch_isend_irecv(ops) if ops else []
 
     kw = dict(spec=spec, alpha=alpha, steps=steps, causal=causal, backward=backward)
+    ev = _PartEvents(timing if on_gpu else None)
     if on_gpu:
         comm = comm_stream if comm_stream is not None else torch.cuda.Stream(device=x_local.device)
         comm.wait_stream(cur)
         with torch.cuda.stream(comm):
+            ev.begin("exchange", comm)
             works = post_exchange()
             for w in works:
                 w.wait()
+            ev.end("exchange", comm)
         # interior rows need no halo: overlap them with the exchange
+        ev.begin("interior", cur)
         compute(_lib.SHARD_INTERIOR, x_local, out, lo_halo=None, hi_halo=None, **kw)
+        ev.end("interior", cur)
+        ev.begin("exposed_wait", cur)
         cur.wait_stream(comm)
+        ev.end("exposed_wait", cur)
         for h in (lo_halo, hi_halo):
             if h is not None:
                 h.record_stream(cur)
@@ -158,8 +191,10 @@ def sharded_diffusion(
         compute(_lib.SHARD_INTERIOR, x_local, out, lo_halo=None, hi_halo=None, **kw)
         for w in works:
             w.wait()
+    ev.begin("edges", cur)
     compute(_lib.SHARD_LO_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
     compute(_lib.SHARD_HI_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
+    ev.end("edges", cur)
     return out
 
 

@@ -52,12 +52,37 @@ const char* cta_last_error(void);
  * synchronizes with the device. */
 int cta_device_error(int clear);
 
-/* Benchmark tuning hook: key 0 = target CTAs per SM used to size the [B, L, D]
- * backward tiles (default 6), key 1 = forced tile rows (0 = automatic), key 2 =
- * target CTAs per SM of the [B, L, D] forward (default 16), key 3 = launch
- * the [B, L, D] march kernels with programmatic dependent launch (default 0).  Returns the
- * previous value.  Process-wide, not thread-safe against concurrent launches. */
+/* Benchmark and test hook: key 1 = forced tile rows (0 = automatic), key 2 =
+ * target CTAs per SM of the [B, L, D] march kernels (default 16), key 3 = launch
+ * the [B, L, D] march kernels with programmatic dependent launch (default 0),
+ * key 4 = plain vector stores instead of staged TMA stores in the forward
+ * (default 0), key 5 = test of the timeout path: the first CTA of every
+ * forward march waits this many microseconds (at most 100000) on an mbarrier
+ * phase nothing completes, then reports the timeout in the device error word
+ * and exits (default 0 = off).  Returns the previous value.  Process-wide, not
+ * thread-safe against concurrent launches. */
 int cta_set_tuning(int key, int value);
+
+/* Arithmetic of the forward update c + alpha * lap for 16-bit (bf16 / fp16)
+ * tensors; fp32 tensors always use CTA_ARITH_EXACT.
+ *   CTA_ARITH_EXACT      : the product rounded to fp32, then the sum rounded --
+ *                          the reference's PyTorch path (src/cta/ops/diffusion.py:
+ *                          52-53, src/models/pde_layers.py:141-175), bit for bit;
+ *   CTA_ARITH_CONTRACTED : product and sum as one fused multiply-add -- the op
+ *                          order the reference's Triton kernels compile to
+ *                          (kernels/diffusion_triton.py:89-90, :252-259); within
+ *                          one bf16 / fp16 rounding of the exact result.
+ * Applies to the forward kernels (cta_diffusion_fwd_bdl / _bdl_ex forward,
+ * _fwd_bld, _fwd_bld_residual, _fwd_varlen[_residual], _shard_bld forward); the
+ * backward kernels, the pooled forward and the advection / reaction steps are
+ * always exact.  cta_set_arithmetic sets the process default (initially
+ * CTA_ARITH_CONTRACTED) and returns the previous one (-1: unknown mode).
+ * cta_set_thread_arithmetic overrides it for the calling thread (mode -1 =
+ * follow the process default) and returns the thread's previous override. */
+#define CTA_ARITH_EXACT 0
+#define CTA_ARITH_CONTRACTED 1
+int cta_set_arithmetic(int mode);
+int cta_set_thread_arithmetic(int mode);
 
 /* ---------------------------------------------------------------------------
  * [B, D, L] layout, L contiguous
@@ -223,7 +248,7 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
                             int64_t hi_rows, int part, int dtype, int steps, int causal, int backward, float alpha,
                             void* stream);
 
-/* One part of an L-shard's fused backward WITH d(alpha), steps 1..4 (no
+/* One part of an L-shard's fused backward WITH d(alpha), steps 1..8 (no
  * counterpart in the reference, which is single-device; together with an
  * all-reduce of the per-rank sums it is the sharded form of
  * cta_diffusion_bwd_bld with dalpha).  grad_out, x and grad_in are the local
@@ -233,7 +258,7 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
  * unused).  Halos are read only by the edge parts.  The part's d(alpha) sum is
  * ADDED to dalpha (fp32 [steps], zeroed by the caller before the first part);
  * run the parts in one stream so the sum order is fixed.  `workspace` as for
- * cta_diffusion_bwd_bld with L = L_local.  Returns CTA_EUNSUPPORTED for steps > 4. */
+ * cta_diffusion_bwd_bld with L = L_local. */
 int cta_diffusion_shard_bld_dalpha(const void* grad_out, const void* x, void* grad_in, float* dalpha,
                                    void* workspace, int64_t workspace_bytes, int64_t B, int64_t L_local, int64_t D,
                                    int64_t pos_offset, int64_t global_len, const void* g_lo_halo, int64_t g_lo_rows,

@@ -26,6 +26,28 @@ Alpha = Union[float, torch.Tensor]
 
 
 # ---------------------------------------------------------------------------
+# the update u + alpha * lap in two arithmetics
+# ---------------------------------------------------------------------------
+def _update(u: torch.Tensor, a, lap: torch.Tensor, contracted: bool) -> torch.Tensor:
+    """u + alpha * lap, fp32.
+
+    contracted=False: the reference's PyTorch ops -- the product rounded to fp32,
+    then the sum rounded (src/cta/ops/diffusion.py:52-53).
+    contracted=True: the product and the sum rounded ONCE, a fused multiply-add:
+    the op order the reference's Triton kernels compile to
+    (kernels/diffusion_triton.py:89-90, :252-259; Triton contracts a multiply
+    feeding an add into one fma by default).  Emulated in fp64: the product of
+    two fp32 values is exact there, the sum rounds to fp64 and then to fp32,
+    which equals the single fp32 rounding except in double-rounding ties of
+    probability about 2**-29 per element (absorbed by any 16-bit output rounding).
+    """
+    if not contracted:
+        return u + a * lap
+    a64 = a.double() if isinstance(a, torch.Tensor) else float(torch.tensor(float(a), dtype=torch.float32))
+    return (u.double() + a64 * lap.double()).to(torch.float32)
+
+
+# ---------------------------------------------------------------------------
 # core stencil along the last axis, fp32
 # ---------------------------------------------------------------------------
 def _lap_last(u: torch.Tensor) -> torch.Tensor:
@@ -33,7 +55,8 @@ def _lap_last(u: torch.Tensor) -> torch.Tensor:
     return u[..., 2:] - 2.0 * u[..., 1:-1] + u[..., :-2]
 
 
-def step_bdl(x_bdl: torch.Tensor, *, alpha: float, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+def step_bdl(x_bdl: torch.Tensor, *, alpha: float, out_dtype: Optional[torch.dtype] = None,
+             contracted: bool = False) -> torch.Tensor:
     """One non-causal step on [B, D, L], copy boundary (src/cta/ops/diffusion.py:17-56)."""
     if x_bdl.ndim != 3:
         raise ValueError(f"expected x_bdl.ndim == 3, got {x_bdl.ndim}")
@@ -42,11 +65,12 @@ def step_bdl(x_bdl: torch.Tensor, *, alpha: float, out_dtype: Optional[torch.dty
         return x_bdl.to(dtype=out_dtype)
     u = x_bdl.to(dtype=torch.float32)
     mid = u[:, :, 1:-1]
-    new_mid = mid + float(alpha) * _lap_last(u)
+    new_mid = _update(mid, float(alpha), _lap_last(u), contracted)
     return torch.cat([u[:, :, :1], new_mid, u[:, :, -1:]], dim=2).to(dtype=out_dtype)
 
 
-def steps_bdl(x_bdl: torch.Tensor, *, alpha: float, steps: int, out_dtype: Optional[torch.dtype] = None):
+def steps_bdl(x_bdl: torch.Tensor, *, alpha: float, steps: int, out_dtype: Optional[torch.dtype] = None,
+              contracted: bool = False):
     """`steps` steps, fp32 in between, rounded once (src/cta/ops/diffusion.py:59-77)."""
     if steps < 0:
         raise ValueError(f"expected steps >= 0, got {steps}")
@@ -55,11 +79,11 @@ def steps_bdl(x_bdl: torch.Tensor, *, alpha: float, steps: int, out_dtype: Optio
         return x_bdl.to(dtype=out_dtype)
     u = x_bdl
     for _ in range(steps):
-        u = step_bdl(u, alpha=alpha, out_dtype=torch.float32)
+        u = step_bdl(u, alpha=alpha, out_dtype=torch.float32, contracted=contracted)
     return u.to(dtype=out_dtype)
 
 
-def steps_bld(x_bld: torch.Tensor, *, alpha: float, steps: int) -> torch.Tensor:
+def steps_bld(x_bld: torch.Tensor, *, alpha: float, steps: int, contracted: bool = False) -> torch.Tensor:
     """[B, L, D] form, fp32 in between (src/cta/serving_vllm.py:29-46)."""
     if steps <= 0:
         return x_bld
@@ -70,7 +94,7 @@ def steps_bld(x_bld: torch.Tensor, *, alpha: float, steps: int) -> torch.Tensor:
     u = x_bld.to(dtype=torch.float32)
     for _ in range(steps):
         lap = u[:, 2:, :] - 2.0 * u[:, 1:-1, :] + u[:, :-2, :]
-        u = torch.cat([u[:, :1, :], u[:, 1:-1, :] + float(alpha) * lap, u[:, -1:, :]], dim=1)
+        u = torch.cat([u[:, :1, :], _update(u[:, 1:-1, :], float(alpha), lap, contracted), u[:, -1:, :]], dim=1)
     return u.to(dtype=x_bld.dtype)
 
 
@@ -97,6 +121,7 @@ def layer_step(
     causal: bool = False,
     attention_mask: Optional[torch.Tensor] = None,
     keep_fp32: bool = False,
+    contracted: bool = False,
 ) -> torch.Tensor:
     """One DiffusionPDELayer step (src/models/pde_layers.py:113-188, :218-219).
 
@@ -113,13 +138,13 @@ def layer_step(
     a = _alpha_f32(alpha)
     if causal:
         interior = u[:, :, 2:]
-        upd = interior + a * lap
+        upd = _update(interior, a, lap, contracted)
         if attention_mask is not None:
             upd = torch.where(_valid3(attention_mask, upd.size(2)), upd, interior)
         y = torch.cat([u[:, :, :2], upd], dim=2)
     else:
         interior = u[:, :, 1:-1]
-        upd = interior + a * lap
+        upd = _update(interior, a, lap, contracted)
         if attention_mask is not None:
             upd = torch.where(_valid3(attention_mask, upd.size(2)), upd, interior)
         y = torch.cat([u[:, :, :1], upd, u[:, :, -1:]], dim=2)
@@ -198,6 +223,7 @@ def fused_stack(
     layout: str = "bdl",
     causal: bool = False,
     attention_mask: Optional[torch.Tensor] = None,
+    contracted: bool = False,
 ) -> torch.Tensor:
     """The same layers with fp32 kept between them and one final rounding."""
     seq_dim = 2 if layout == "bdl" else 1
@@ -205,7 +231,8 @@ def fused_stack(
         return x
     y = x.to(torch.float32)
     for a in alphas:
-        y = layer_step(y, a, layout=layout, causal=causal, attention_mask=attention_mask, keep_fp32=True)
+        y = layer_step(y, a, layout=layout, causal=causal, attention_mask=attention_mask, keep_fp32=True,
+                       contracted=contracted)
     return y.to(dtype=x.dtype)
 
 
@@ -242,7 +269,8 @@ def grads(fn, x: torch.Tensor, grad_out: torch.Tensor, params: Sequence[torch.Te
 # ---------------------------------------------------------------------------
 # packed variable-length prefill
 # ---------------------------------------------------------------------------
-def mixer_packed(x_flat: torch.Tensor, qsl: Sequence[int], max_len: int, *, alpha: float, steps: int):
+def mixer_packed(x_flat: torch.Tensor, qsl: Sequence[int], max_len: int, *, alpha: float, steps: int,
+                 contracted: bool = False):
     """Reference packed path: zero-pad every request to max_len, run the [B, L, D]
     stencil, unpack (src/cta/serving_vllm.py:72-111, :292-303)."""
     qsl = [int(v) for v in qsl]
@@ -254,7 +282,7 @@ def mixer_packed(x_flat: torch.Tensor, qsl: Sequence[int], max_len: int, *, alph
         s, e = qsl[i], qsl[i + 1]
         if e > s:
             padded[i, : e - s] = x_flat[s:e]
-    y = steps_bld(padded, alpha=alpha, steps=steps)
+    y = steps_bld(padded, alpha=alpha, steps=steps, contracted=contracted)
     out = torch.empty_like(x_flat)
     for i in range(R):
         s, e = qsl[i], qsl[i + 1]
@@ -263,14 +291,15 @@ def mixer_packed(x_flat: torch.Tensor, qsl: Sequence[int], max_len: int, *, alph
     return out
 
 
-def varlen_per_sequence(x_flat: torch.Tensor, qsl: Sequence[int], *, alpha: float, steps: int):
+def varlen_per_sequence(x_flat: torch.Tensor, qsl: Sequence[int], *, alpha: float, steps: int,
+                        contracted: bool = False):
     """Every sequence refined on its own, with its own copy boundary."""
     qsl = [int(v) for v in qsl]
     out = x_flat.clone()
     for i in range(len(qsl) - 1):
         s, e = qsl[i], qsl[i + 1]
         if e > s:
-            out[s:e] = steps_bld(x_flat[s:e].unsqueeze(0), alpha=alpha, steps=steps)[0]
+            out[s:e] = steps_bld(x_flat[s:e].unsqueeze(0), alpha=alpha, steps=steps, contracted=contracted)[0]
     return out
 
 
@@ -279,7 +308,7 @@ def varlen_per_sequence(x_flat: torch.Tensor, qsl: Sequence[int], *, alpha: floa
 # ---------------------------------------------------------------------------
 def window_bld(
     x_window: torch.Tensor, *, win_start: int, global_len: int, out_start: int, out_stop: int, alpha: float,
-    steps: int,
+    steps: int, contracted: bool = False,
 ) -> torch.Tensor:
     """Rows [out_start, out_stop) of steps_bld over a global sequence, given only the rows
     x_window = global rows [win_start, win_start + len) (which must cover the halo)."""
@@ -289,7 +318,7 @@ def window_bld(
     fixed = ((pos <= 0) | (pos >= global_len - 1)).view(1, n, 1)
     for _ in range(steps):
         lap = u[:, 2:, :] - 2.0 * u[:, 1:-1, :] + u[:, :-2, :]
-        mid = u[:, 1:-1, :] + float(alpha) * lap
+        mid = _update(u[:, 1:-1, :], float(alpha), lap, contracted)
         mid = torch.where(fixed[:, 1:-1, :], u[:, 1:-1, :], mid)
         u = torch.cat([u[:, :1, :], mid, u[:, -1:, :]], dim=1)
     return u[:, out_start - win_start : out_stop - win_start, :].to(x_window.dtype)

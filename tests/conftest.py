@@ -34,6 +34,12 @@ def golden():
     return torch.load(GOLDEN, weights_only=False)
 
 
+def contracted(dtype: torch.dtype) -> bool:
+    """Whether a forward of this dtype runs the contracted update by default
+    (16-bit tensors; fp32 is always exact)."""
+    return dtype in (torch.bfloat16, torch.float16)
+
+
 def assert_close(a: torch.Tensor, b: torch.Tensor, *, fp32_tol: float = 1e-5, half_tol: float = 2e-2) -> None:
     """Parity bar: max-abs error <= fp32_tol * max|ref| in fp32, <= half_tol in bf16/fp16."""
     half = a.dtype in (torch.bfloat16, torch.float16) or b.dtype in (torch.bfloat16, torch.float16)

@@ -5,7 +5,9 @@ source tree) on seeded CPU inputs and stores inputs and outputs in
 ``golden.pt`` next to this script.  Large configurations are stored as the
 SHA-256 of the output bytes plus the seed that regenerates the input.
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>
+
+(or set CTA_REFERENCE_ROOT instead of passing --ref).
 
 Only this script reads the reference; the tests and the GPU box use the
 committed ``golden.pt``.
@@ -14,6 +16,7 @@ from __future__ import annotations
 
 import argparse
 import hashlib
+import os
 import sys
 from pathlib import Path
 from types import SimpleNamespace
@@ -32,8 +35,11 @@ def sha(t: torch.Tensor) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("CTA_REFERENCE_ROOT"),
+                    help="root of the reference checkout (default: $CTA_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("pass --ref <reference checkout> or set CTA_REFERENCE_ROOT")
     ref = Path(args.ref)
     sys.path.insert(0, str(ref / "src"))
     sys.path.insert(0, str(ref))

@@ -124,3 +124,19 @@ def test_mixer_host_logic():
     assert CtaPostAttnMixer(CtaConfig())(flat) is flat  # no metadata -> passthrough (:284-285)
     md = SimpleNamespace(max_query_len=2, query_start_loc=[0, 2, 4])
     assert CtaPostAttnMixer(CtaConfig())(flat, attn_metadata=md) is flat  # max_query_len < 3
+
+
+def test_arithmetic_mode_codes():
+    """Mode names map to the C ABI codes; unknown modes are rejected on the host
+    and by the library."""
+    from cta_b200 import _lib
+
+    assert _lib.arith_code("exact") == _lib.ARITH_EXACT == 0
+    assert _lib.arith_code("contracted") == _lib.ARITH_CONTRACTED == 1
+    with pytest.raises(ValueError):
+        _lib.arith_code("fast")
+    lib = _lib.load()
+    assert lib.cta_set_arithmetic(7) == -1
+    assert lib.cta_set_thread_arithmetic(7) == -2
+    prev = lib.cta_set_thread_arithmetic(0)
+    assert lib.cta_set_thread_arithmetic(prev) == 0

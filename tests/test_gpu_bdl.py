@@ -4,7 +4,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from conftest import assert_close
+from conftest import assert_close, contracted
 from oracle import diffusion_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -24,9 +24,13 @@ def test_fused_bitexact(dtype, steps):
     torch.manual_seed(0)
     x = torch.randn(2, 32, 1024, dtype=dtype)
     y = _api().diffusion_triton_fused(x.cuda(), alpha=0.1, steps=steps)
-    ref = O.steps_bdl(x, alpha=0.1, steps=steps)
+    ref = O.steps_bdl(x, alpha=0.1, steps=steps, contracted=contracted(dtype))
     assert y.dtype == dtype and y.shape == x.shape
     assert torch.equal(y.cpu(), ref), (y.cpu().float() - ref.float()).abs().max()
+    # the exact arithmetic: bit for bit the reference's PyTorch path in every dtype
+    from cta_b200 import ops
+    ye = ops.bdl_simple(x.cuda(), 0.1, steps, arith="exact")
+    assert torch.equal(ye.cpu(), O.steps_bdl(x, alpha=0.1, steps=steps))
 
 
 @pytest.mark.parametrize("shape", [(1, 8, 257), (2, 3, 17), (1, 1, 3), (3, 5, 1000), (2, 4, 4096), (1, 2, 481),
@@ -37,7 +41,7 @@ def test_fused_shapes(shape, steps):
     for dtype in (torch.float32, torch.bfloat16):
         x = torch.randn(*shape, dtype=dtype)
         y = _api().diffusion_triton_fused(x.cuda(), alpha=0.1, steps=steps)
-        assert torch.equal(y.cpu(), O.steps_bdl(x, alpha=0.1, steps=steps))
+        assert torch.equal(y.cpu(), O.steps_bdl(x, alpha=0.1, steps=steps, contracted=contracted(dtype)))
 
 
 def test_noncontiguous_input():
@@ -84,7 +88,7 @@ def test_unfused_loop_rounds_each_step(dtype):
     y = _api().diffusion_triton(x.cuda(), alpha=0.1, steps=4)
     ref = x
     for _ in range(4):
-        ref = O.step_bdl(ref, alpha=0.1)
+        ref = O.step_bdl(ref, alpha=0.1, contracted=contracted(dtype))
     assert torch.equal(y.cpu(), ref)
 
 

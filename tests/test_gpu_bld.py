@@ -4,7 +4,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from conftest import assert_close
+from conftest import assert_close, contracted
 from oracle import diffusion_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -25,8 +25,14 @@ def test_forward_bitexact(dtype, steps):
     torch.manual_seed(0)
     x = torch.randn(2, 1024, 512, dtype=dtype)
     y = _ops().bld_forward(x.cuda(), [0.1] * steps, steps)
-    ref = O.steps_bld(x, alpha=0.1, steps=steps)
+    ref = O.steps_bld(x, alpha=0.1, steps=steps, contracted=contracted(dtype))
     assert torch.equal(y.cpu(), ref), (y.cpu().float() - ref.float()).abs().max()
+    ye = _ops().bld_forward(x.cuda(), [0.1] * steps, steps, arith="exact")
+    assert torch.equal(ye.cpu(), O.steps_bld(x, alpha=0.1, steps=steps))
+    # the contracted update stays within one rounding of the output dtype
+    if contracted(dtype):
+        ex = O.steps_bld(x, alpha=0.1, steps=steps)
+        assert (y.cpu().float() - ex.float()).abs().max().item() <= 2e-2
 
 
 @pytest.mark.parametrize("shape", SHAPES)
@@ -36,7 +42,7 @@ def test_forward_shapes(shape, steps):
     for dtype in (torch.float32, torch.bfloat16):
         x = torch.randn(*shape, dtype=dtype)
         y = _ops().bld_forward(x.cuda(), [0.1] * steps, steps)
-        assert torch.equal(y.cpu(), O.steps_bld(x, alpha=0.1, steps=steps)), (shape, dtype)
+        assert torch.equal(y.cpu(), O.steps_bld(x, alpha=0.1, steps=steps, contracted=contracted(dtype))), (shape, dtype)
 
 
 def test_forward_strided_rows():
@@ -91,7 +97,7 @@ def test_device_alpha_scalars():
 
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("use_mask", [False, True])
-@pytest.mark.parametrize("steps", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("steps", [1, 2, 3, 4, 5, 6, 7, 8])
 @pytest.mark.parametrize("shape", [(2, 300, 512), (2, 23, 6), (1, 700, 264)])
 def test_backward_dx_dalpha(causal, use_mask, steps, shape):
     torch.manual_seed(6)
@@ -186,7 +192,8 @@ def test_varlen_reference_rule(steps, dtype):
     x = torch.randn(qsl[-1], 64).to(dtype)
     cu = torch.tensor(qsl, dtype=torch.int32, device="cuda")
     y = _ops().varlen_forward(x.cuda(), cu, max(lens), 0.1, steps, pad_to_max=True)
-    assert torch.equal(y.cpu(), O.mixer_packed(x, qsl, max(lens), alpha=0.1, steps=steps))
+    assert torch.equal(y.cpu(), O.mixer_packed(x, qsl, max(lens), alpha=0.1, steps=steps,
+                                               contracted=contracted(dtype)))
 
 
 @pytest.mark.parametrize("steps", [1, 2, 4, 8])
@@ -205,7 +212,9 @@ def test_varlen_sequence_rule(steps):
 def test_varlen_golden(golden):
     for c in golden["mixer_packed"]:
         cu = torch.tensor(c["qsl"], dtype=torch.int32, device="cuda")
-        y = _ops().varlen_forward(c["x"].cuda(), cu, c["max_len"], c["alpha"], c["steps"], pad_to_max=True)
+        # the goldens are the reference's PyTorch path: the exact arithmetic
+        y = _ops().varlen_forward(c["x"].cuda(), cu, c["max_len"], c["alpha"], c["steps"], pad_to_max=True,
+                                  arith="exact")
         assert torch.equal(y.cpu(), c["y"])
 
 
@@ -232,7 +241,7 @@ def test_varlen_residual_equals_two_pass(steps, dtype, pad):
     y2 = r.cuda() + ops.varlen_forward(x.cuda(), cu, max(lens), 0.1, steps, pad_to_max=pad)
     assert torch.equal(y1, y2)
     if pad:
-        ref = r + O.mixer_packed(x, qsl, max(lens), alpha=0.1, steps=steps)
+        ref = r + O.mixer_packed(x, qsl, max(lens), alpha=0.1, steps=steps, contracted=contracted(dtype))
         assert torch.equal(y1.cpu(), ref)
 
 
@@ -285,3 +294,71 @@ def test_mixer_residual(varlen_mode):
     assert torch.equal(mixer(x3, is_prefill=True, residual=r3), r3 + mixer(x3, is_prefill=True))
     long_mixer = CtaPostAttnMixer(CtaConfig(steps=11, alpha=0.1, max_steps=16, trace=False))
     assert torch.equal(long_mixer(x3, is_prefill=True, residual=r3), r3 + long_mixer(x3, is_prefill=True))
+
+
+def test_bounded_wait_runs_out_reports_and_recovers():
+    """The timeout path of the pipeline waits, on demand: with the test hook
+    (tuning key 5) the first CTA waits 1 ms on an mbarrier phase that nothing
+    completes, sets the device error word, drains the loads it issued and exits.
+    The call returns, the error reads 1 and clears, the other tiles are right,
+    and the next call is bit-exact."""
+    from cta_b200 import _lib
+
+    lib = _lib.load()
+    torch.manual_seed(9)
+    x = torch.randn(1, 4096, 512, dtype=torch.bfloat16)
+    ref = O.steps_bld(x, alpha=0.1, steps=4, contracted=True)
+    xd = x.cuda()
+    torch.cuda.synchronize()
+    assert lib.cta_device_error(1) == 0
+    prev = lib.cta_set_tuning(5, 1000)
+    try:
+        y = _ops().bld_forward(xd, [0.1] * 4, 4)
+        torch.cuda.synchronize()
+    finally:
+        lib.cta_set_tuning(5, prev)
+    assert lib.cta_device_error(1) == 1
+    assert lib.cta_device_error(0) == 0
+    # the stalled CTA owns row tile 0 of column tile 0; every other column is written
+    assert torch.equal(y[:, :, 128:].cpu(), ref[:, :, 128:])
+    y2 = _ops().bld_forward(xd, [0.1] * 4, 4)
+    assert torch.equal(y2.cpu(), ref)
+    assert lib.cta_device_error(0) == 0
+
+
+def test_arithmetic_modes_process_and_thread():
+    """The process default (cta_b200.set_arithmetic) and the per-call override:
+    bf16 follows them, fp32 is always exact, the layers always exact."""
+    import threading
+
+    import cta_b200
+    from cta_b200.pde_layers import DiffusionPDELayer, diffusion_pde_stack
+
+    torch.manual_seed(21)
+    x = torch.randn(1, 1500, 264, dtype=torch.bfloat16)
+    xd = x.cuda()
+    exact = O.steps_bld(x, alpha=0.1, steps=4)
+    contr = O.steps_bld(x, alpha=0.1, steps=4, contracted=True)
+    assert not torch.equal(exact, contr)  # the inputs tell the two apart
+    ops = _ops()
+    assert cta_b200.set_arithmetic("exact") == "contracted"
+    try:
+        assert torch.equal(ops.bld_forward(xd, [0.1] * 4, 4).cpu(), exact)
+        assert torch.equal(ops.bld_forward(xd, [0.1] * 4, 4, arith="contracted").cpu(), contr)
+        # another thread sees the process default, not this thread's override
+        seen = {}
+        t = threading.Thread(target=lambda: seen.update(y=ops.bld_forward(xd, [0.1] * 4, 4).cpu()))
+        t.start()
+        t.join()
+        assert torch.equal(seen["y"], exact)
+    finally:
+        assert cta_b200.set_arithmetic("contracted") == "exact"
+    assert torch.equal(ops.bld_forward(xd, [0.1] * 4, 4).cpu(), contr)
+    xf = x.float()
+    assert torch.equal(ops.bld_forward(xf.cuda(), [0.1] * 4, 4).cpu(), O.steps_bld(xf, alpha=0.1, steps=4))
+    layers = [DiffusionPDELayer(264, alpha_init=0.1, layout="bld").cuda() for _ in range(4)]
+    with torch.no_grad():
+        y = diffusion_pde_stack(xd, layers)
+    assert torch.equal(y.cpu(), O.fused_stack(x, [0.1] * 4, layout="bld"))
+    with pytest.raises(ValueError):
+        ops.bld_forward(xd, [0.1] * 4, 4, arith="fast")

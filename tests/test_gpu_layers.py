@@ -137,8 +137,14 @@ def test_mixer_dense(layout, steps):
     x = x.to(torch.bfloat16)
     mixer = CtaPostAttnMixer(CtaConfig(steps=steps, alpha=0.1, layout=layout))
     y = mixer(x.cuda())
-    ref = O.steps_bld(x, alpha=0.1, steps=steps) if layout == "bld" else O.steps_bdl(x, alpha=0.1, steps=steps)
+    # use_triton (default): the contracted update of the reference's Triton kernels
+    ref = (O.steps_bld(x, alpha=0.1, steps=steps, contracted=True) if layout == "bld"
+           else O.steps_bdl(x, alpha=0.1, steps=steps, contracted=True))
     assert torch.equal(y.cpu(), ref)
+    # use_triton=False: the reference's PyTorch fallback, bit for bit
+    ye = CtaPostAttnMixer(CtaConfig(steps=steps, alpha=0.1, layout=layout, use_triton=False))(x.cuda())
+    ref = O.steps_bld(x, alpha=0.1, steps=steps) if layout == "bld" else O.steps_bdl(x, alpha=0.1, steps=steps)
+    assert torch.equal(ye.cpu(), ref)
     # decode steps pass through untouched
     assert mixer(x.cuda(), is_prefill=False).data_ptr() != 0
 
@@ -147,7 +153,8 @@ def test_mixer_packed_reference_rule(golden):
     from cta_b200.serving_vllm import CtaConfig, CtaPostAttnMixer
 
     for c in golden["mixer_packed"]:
-        mixer = CtaPostAttnMixer(CtaConfig(steps=c["steps"], alpha=c["alpha"]))
+        # the goldens are the reference's PyTorch path (use_triton=False)
+        mixer = CtaPostAttnMixer(CtaConfig(steps=c["steps"], alpha=c["alpha"], use_triton=False))
         md = SimpleNamespace(max_query_len=c["max_len"], is_prefill=True,
                              query_start_loc=torch.tensor(c["qsl"], dtype=torch.int32, device="cuda"))
         y = mixer(c["x"].cuda(), attn_metadata=md)
@@ -178,7 +185,7 @@ def _two_coef_layer(kind, D, layout, causal, alpha=0.12, beta=0.07):
 
 def test_pde_step_layers_match_reference_golden(golden):
     """The reference's own layer outputs: advection bit for bit, reaction (its
-    sigmoid is CUDA's expf here) to the fp32 / bf16 bar; gradients within tolerance."""
+    sigmoid uses the __expf intrinsic and __frcp_rn here) to the fp32 / bf16 bar; gradients within tolerance."""
     for c in golden["pde_step"]:
         D = c["x"].shape[2] if c["layout"] == "bld" else c["x"].shape[1]
         layer = _two_coef_layer(c["kind"], D, c["layout"], c["causal"], c["alpha"], c["beta"])

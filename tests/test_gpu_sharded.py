@@ -45,7 +45,7 @@ def test_sharded_forward_equals_unsharded(P, steps, D, causal):
     y = _run_sharded(x, P, steps, causal, backward=False)
     assert torch.equal(y, full)
     if not causal:
-        assert torch.equal(y.cpu(), O.steps_bld(x.cpu(), alpha=0.1, steps=steps))
+        assert torch.equal(y.cpu(), O.steps_bld(x.cpu(), alpha=0.1, steps=steps, contracted=True))
 
 
 @pytest.mark.parametrize("P", [2, 4])
@@ -128,11 +128,28 @@ def test_sharded_backward_dalpha_equals_unsharded(P, steps, causal, dtype, D):
     assert _lib.device_error() == 0
 
 
-def test_sharded_dalpha_rejects_deep_steps():
+@pytest.mark.parametrize("P", [2, 3])
+@pytest.mark.parametrize("steps", [5, 6, 7, 8])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 264), (torch.float32, 6)])
+def test_sharded_backward_dalpha_deep_steps(P, steps, causal, dtype, D):
+    """Steps 5..8 (the long-context configuration runs 8 learnable steps):
+    dx bit-identical to the unsharded kernel, d(alpha) to the summation order,
+    and the fp32 case against the oracle's autograd."""
     from cta_b200 import _lib, ops
 
-    g = torch.randn(1, 64, 8, device="cuda")
-    da = torch.zeros(8, device="cuda")
-    with pytest.raises(RuntimeError, match="steps 1..4"):
-        ops.shard_part_dalpha(g, g, torch.empty_like(g), da, _lib.SHARD_INTERIOR, pos_offset=0, global_len=64,
-                              alphas=[0.1] * 8, steps=8)
+    torch.manual_seed(P * 10 + steps + 100)
+    al = [0.1, 0.05, 0.12, 0.02, 0.08, 0.03, 0.11, 0.07][:steps]
+    x = torch.randn(2, 901, D, device="cuda").to(dtype)
+    g = torch.randn(2, 901, D, device="cuda").to(dtype)
+    full_dx, full_da = ops.bld_backward(g, al, steps, x=x, causal=causal, need_dalpha=True)
+    dx, da = _run_sharded_dalpha(g, x, P, steps, causal, al)
+    assert torch.equal(dx, full_dx)
+    scale = max(1.0, full_da.abs().max().item())
+    assert (da - full_da).abs().max().item() <= 1e-5 * scale, (da, full_da)
+    if dtype == torch.float32:
+        dx_ref, da_ref = O.grads(lambda t, *a: O.fused_stack(t, list(a), layout="bld", causal=causal), x.cpu(),
+                                 g.cpu(), [torch.tensor([v]) for v in al])
+        assert (dx.cpu() - dx_ref).abs().max().item() <= 1e-5 * dx_ref.abs().max().item()
+        assert (da.cpu() - torch.cat(da_ref)).abs().max().item() <= 1e-4 * scale
+    assert _lib.device_error() == 0
