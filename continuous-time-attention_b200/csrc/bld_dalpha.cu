@@ -161,11 +161,15 @@ __device__ __forceinline__ pf2 reaction_df(pf2 v, pf2 s) {
             __fmul_rn(__fsub_rn(1.0f, s1), __fsub_rn(1.0f, __fmul_rn(v1, s1))));
 }
 
-template <typename T, int S, bool CAUSAL, int KIND = 0>
+// FM: the contracted arithmetic for 16-bit I/O -- the forward recomputation as
+// u + alpha * lap in one fma (the contracted forward's op order) and the
+// adjoint level as g + alpha * lap(a) in one fma with a = g on updated rows.
+template <typename T, int S, bool CAUSAL, int KIND = 0, bool FM = false>
 __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     bld_dalpha_kernel(const __grid_constant__ CUtensorMap gmap, const __grid_constant__ CUtensorMap xmap,
                       const __grid_constant__ CUtensorMap ymap, const BldArgs a) {
   static_assert(KIND == 0 || S == 1, "the other PDE kinds are single steps");
+  static_assert(!FM || KIND == 0, "the contracted arithmetic is the diffusion step's");
   constexpr int NV = S + (KIND != 0 ? 1 : 0);  // reduced values: d(alpha_k) [, d(beta)]
   constexpr int NP = kDaPairs;                 // packed column pairs per lane
   using Q = ColVec<T, 2 * NP>;
@@ -343,10 +347,10 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
             if (TCT < 0 || TCT >= 2 * q + 2) {
               la[q][p] = plap(F2[q][p], F1[q][p], x[p], m2);
               if (CAUSAL) {
-                n = padd(x[p], pmul_sep(al[q], la[q][p], zn));
+                n = FM ? pfma(al[q], la[q][p], x[p]) : padd(x[p], pmul_sep(al[q], la[q][p], zn));
                 if (SLOW && fxc) n = x[p];
               } else {
-                n = padd(F1[q][p], pmul_sep(al[q], la[q][p], zn));
+                n = FM ? pfma(al[q], la[q][p], F1[q][p]) : padd(F1[q][p], pmul_sep(al[q], la[q][p], zn));
                 if (SLOW && ((fwx >> (S - 1 - q)) & 1u)) n = F1[q][p];
               }
             }
@@ -362,7 +366,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
       pf2 c[NP], q[NP];
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
-        c[p] = pmul_sep(al[S - 1], g[p], zn);
+        c[p] = FM ? g[p] : pmul_sep(al[S - 1], g[p], zn);
         if (SLOW && f0) c[p] = 0ull;
         q[p] = (SLOW && f0) ? 0ull : g[p];  // q at row jg
       }
@@ -407,8 +411,14 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
         for (int p = 0; p < NP; ++p) {
           pf2 n = g[p];
           if (TCT < 0 || TCT >= 2 * m + 2) {
-            if (CAUSAL) n = padd(G2[m][p], plap(c[p], P1[m][p], P2[m][p], m2));
-            else n = padd(G1[m][p], plap(P2[m][p], P1[m][p], c[p], m2));
+            if constexpr (FM) {
+              if (CAUSAL) n = pfma(al[S - 1 - m], plap(c[p], P1[m][p], P2[m][p], m2), G2[m][p]);
+              else n = pfma(al[S - 1 - m], plap(P2[m][p], P1[m][p], c[p], m2), G1[m][p]);
+            } else if (CAUSAL) {
+              n = padd(G2[m][p], plap(c[p], P1[m][p], P2[m][p], m2));
+            } else {
+              n = padd(G1[m][p], plap(P2[m][p], P1[m][p], c[p], m2));
+            }
             if constexpr (KIND != 0) {
               // finished row i = jg-1 (causal jg-2): q[i-1], q[i], q[i+1] are
               // (Q2, Q1, q) non-causal, q[i], q[i+1] are (Q2, Q1) causal
@@ -436,7 +446,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
           if (SLOW) f = CAUSAL ? ((fw >> (2 * S - 2 * m - 2)) & 1u) : ((fw >> (S - 1 - m)) & 1u);
 #pragma unroll
           for (int p = 0; p < NP; ++p) {
-            c[p] = pmul_sep(al[S - 2 - m], g[p], zn);
+            c[p] = FM ? g[p] : pmul_sep(al[S - 2 - m], g[p], zn);
             if (SLOW && f) c[p] = 0ull;
           }
         }
@@ -633,22 +643,31 @@ const void* da_ptr_any(int steps, int causal, int kind) {
   return nullptr;
 }
 
-template <typename T, bool CAUSAL>
+template <typename T, bool CAUSAL, bool FM = false>
 const void* da_ptr(int steps) {
   switch (steps) {
-    case 1: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 1, CAUSAL>);
-    case 2: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 2, CAUSAL>);
-    case 3: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 3, CAUSAL>);
-    case 4: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 4, CAUSAL>);
-    case 5: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 5, CAUSAL>);
-    case 6: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 6, CAUSAL>);
-    case 7: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 7, CAUSAL>);
-    case 8: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 8, CAUSAL>);
+    case 1: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 1, CAUSAL, 0, FM>);
+    case 2: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 2, CAUSAL, 0, FM>);
+    case 3: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 3, CAUSAL, 0, FM>);
+    case 4: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 4, CAUSAL, 0, FM>);
+    case 5: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 5, CAUSAL, 0, FM>);
+    case 6: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 6, CAUSAL, 0, FM>);
+    case 7: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 7, CAUSAL, 0, FM>);
+    case 8: return reinterpret_cast<const void*>(bld_dalpha_kernel<T, 8, CAUSAL, 0, FM>);
     default: return nullptr;
   }
 }
 
-const void* da_kernel(int dtype, int steps, int causal, int kind = 0) {
+const void* da_kernel(int dtype, int steps, int causal, int kind = 0, int fm = 0) {
+  if (fm) {
+    // the contracted arithmetic is built for 16-bit I/O only
+    if (kind != 0) return nullptr;
+    switch (dtype) {
+      case kBF16: return causal ? da_ptr<__nv_bfloat16, true, true>(steps) : da_ptr<__nv_bfloat16, false, true>(steps);
+      case kF16: return causal ? da_ptr<__half, true, true>(steps) : da_ptr<__half, false, true>(steps);
+      default: return nullptr;
+    }
+  }
   if (kind != 0) {
     switch (dtype) {
       case kF32: return da_ptr_any<float>(steps, causal, kind);
@@ -669,7 +688,7 @@ const void* da_kernel(int dtype, int steps, int causal, int kind = 0) {
 
 cudaError_t launch_bld_dalpha(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap,
                               const CUtensorMap* ymap, int dtype, int steps, int causal, dim3 grid, cudaStream_t st) {
-  const void* kern = da_kernel(dtype, steps, causal, a.pde_kind);
+  const void* kern = da_kernel(dtype, steps, causal, a.pde_kind, a.contract);
   if (kern == nullptr) return cudaErrorInvalidValue;
   const size_t smem = dalpha_smem_bytes(dtype, steps, causal);
   cudaError_t e = ensure_smem_attr(kern, smem);
@@ -679,7 +698,7 @@ cudaError_t launch_bld_dalpha(const BldArgs& a, const CUtensorMap* gmap, const C
   return cudaLaunchKernel(kern, grid, dim3(kFwdThreads), args, smem, st);
 }
 
-int bld_dalpha_ctas_per_sm(int dtype, int steps, int causal) {
+int bld_dalpha_ctas_per_sm(int dtype, int steps, int causal, int contract) {
   struct Entry {
     const void* kern;
     int dev;
@@ -688,7 +707,7 @@ int bld_dalpha_ctas_per_sm(int dtype, int steps, int causal) {
   static Entry table[256];
   static int used = 0;
   static std::mutex mu;
-  const void* kern = da_kernel(dtype, steps, causal);
+  const void* kern = da_kernel(dtype, steps, causal, 0, contract);
   if (kern == nullptr) return -1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;

@@ -125,7 +125,7 @@ template <typename T, int S, bool CAUSAL, bool ADJ, bool RES, int KIND = 0, bool
 __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ, RES>()))
     bld_march_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                      const __grid_constant__ CUtensorMap rmap, const BldArgs a) {
-  static_assert(!FM || (!ADJ && KIND == 0 && !POOL), "the contracted update is the diffusion forward");
+  static_assert(!FM || (KIND == 0 && !POOL), "the contracted update is the diffusion forward / adjoint");
   static_assert(!POOL || (!ADJ && !RES && KIND == 0 && !CAUSAL), "the pooled form is the non-causal forward");
   static_assert(!RES || (!ADJ && !CAUSAL), "the residual form is the non-causal forward");
   static_assert(KIND == 0 || (S == 1 && !ADJ && !RES), "the other PDE kinds are single forward steps");
@@ -323,15 +323,25 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       //   non-causal  g_new[i] = g[i] + (a[i+1] - 2 a[i]) + a[i-1],  i = j-1-m
       //   causal      g_new[i] = g[i] + (a[i] - 2 a[i+1]) + a[i+2],  i = j-2-2m
       // with a = alpha * g on updated rows and 0 on fixed rows.
+      // FM (contracted): a = g on updated rows, and the level applies
+      // g + alpha * lap(a) as one fma instead of g + lap(alpha * g)
       const bool f0 = SLOW && rb.fixed(j);
       const uint32_t fw = SLOW ? (CAUSAL ? rb.window16_fixed(j - 2 * S) : rb.window8_fixed(j - S)) : 0u;
-      pf2 ca = pmul_sep(al[S - 1], xa, zn), cb = pmul_sep(al[S - 1], xb, zn);
+      pf2 ca = FM ? xa : pmul_sep(al[S - 1], xa, zn), cb = FM ? xb : pmul_sep(al[S - 1], xb, zn);
       if (SLOW && f0) ca = cb = 0ull;
 #pragma unroll
       for (int m = 0; m < S; ++m) {
         pf2 na = xa, nb = xb;
         if (TCT < 0 || TCT >= 2 * m + 2) {
-          if (CAUSAL) {
+          if constexpr (FM) {
+            if (CAUSAL) {
+              na = pfma(al[S - 1 - m], plap(ca, P1a[m], P2a[m], m2), G2a[m]);
+              nb = pfma(al[S - 1 - m], plap(cb, P1b[m], P2b[m], m2), G2b[m]);
+            } else {
+              na = pfma(al[S - 1 - m], plap(P2a[m], P1a[m], ca, m2), G1a[m]);
+              nb = pfma(al[S - 1 - m], plap(P2b[m], P1b[m], cb, m2), G1b[m]);
+            }
+          } else if (CAUSAL) {
             na = padd(G2a[m], plap(ca, P1a[m], P2a[m], m2));
             nb = padd(G2b[m], plap(cb, P1b[m], P2b[m], m2));
           } else {
@@ -352,8 +362,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
         xa = na;
         xb = nb;
         if (m < S - 1) {
-          ca = pmul_sep(al[S - 2 - m], xa, zn);
-          cb = pmul_sep(al[S - 2 - m], xb, zn);
+          ca = FM ? xa : pmul_sep(al[S - 2 - m], xa, zn);
+          cb = FM ? xb : pmul_sep(al[S - 2 - m], xb, zn);
           if (SLOW) {
             const bool f = CAUSAL ? ((fw >> (2 * S - 2 * m - 2)) & 1u) : ((fw >> (S - 1 - m)) & 1u);
             if (f) ca = cb = 0ull;
@@ -456,13 +466,22 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
           if constexpr (i >= 0 && i < kFwdRC) {
             if constexpr (ADJ) {
               // adjoint level m (forward step S-m) at march row i; see step_row
-              const pf2 ca = pmul_sep(al[S - 1 - m], ua[i], zn), cb = pmul_sep(al[S - 1 - m], ub[i], zn);
+              const pf2 ca = FM ? ua[i] : pmul_sep(al[S - 1 - m], ua[i], zn);
+              const pf2 cb = FM ? ub[i] : pmul_sep(al[S - 1 - m], ub[i], zn);
               pf2 na, nb;
               if (CAUSAL) {
-                na = padd(G2a[m], plap(ca, P1a[m], P2a[m], m2));
-                nb = padd(G2b[m], plap(cb, P1b[m], P2b[m], m2));
+                if constexpr (FM) {
+                  na = pfma(al[S - 1 - m], plap(ca, P1a[m], P2a[m], m2), G2a[m]);
+                  nb = pfma(al[S - 1 - m], plap(cb, P1b[m], P2b[m], m2), G2b[m]);
+                } else {
+                  na = padd(G2a[m], plap(ca, P1a[m], P2a[m], m2));
+                  nb = padd(G2b[m], plap(cb, P1b[m], P2b[m], m2));
+                }
                 G2a[m] = G1a[m];
                 G2b[m] = G1b[m];
+              } else if constexpr (FM) {
+                na = pfma(al[S - 1 - m], plap(P2a[m], P1a[m], ca, m2), G1a[m]);
+                nb = pfma(al[S - 1 - m], plap(P2b[m], P1b[m], cb, m2), G1b[m]);
               } else {
                 na = padd(G1a[m], plap(P2a[m], P1a[m], ca, m2));
                 nb = padd(G1b[m], plap(P2b[m], P1b[m], cb, m2));
@@ -699,9 +718,9 @@ const void* march_ptr_t(int steps, int causal, int adj, int res, int kind, int f
     return kind == 1 ? march_ptr_kind<T, 1>(steps, causal) : kind == 2 ? march_ptr_kind<T, 2>(steps, causal) : nullptr;
   }
   if (fm) {
-    // the contracted forward is built for 16-bit I/O only
+    // the contracted update is built for 16-bit I/O only
     if constexpr (sizeof(T) == 2) {
-      if (adj) return nullptr;
+      if (adj) return causal ? march_ptr<T, true, true, false, true>(steps) : march_ptr<T, false, true, false, true>(steps);
       if (res) return causal ? nullptr : march_ptr<T, false, false, true, true>(steps);
       return causal ? march_ptr<T, true, false, false, true>(steps) : march_ptr<T, false, false, false, true>(steps);
     }

@@ -255,7 +255,8 @@ int launch_dalpha_march(BldArgs& m, int dtype, int steps, int causal, int64_t B,
   const int64_t ndt = (D + kDaDT - 1) / kDaDT;
   const int64_t rows = m.out_end - m.out_begin;
   if (rows <= 0) return ok();
-  const int occ = bld_dalpha_ctas_per_sm(dtype, steps, causal);
+  m.contract = m.pde_kind == 0 ? contract_for(dtype) : 0;
+  const int occ = bld_dalpha_ctas_per_sm(dtype, steps, causal, m.contract);
   // one wave at the occupancy the variant gets (up to 24 one-warp CTAs per SM)
   m.TL = pick_tl(rows, ndt * B, steps, occ > 0 ? occ : 8);
   const int64_t ntl = (rows + m.TL - 1) / m.TL;
@@ -636,8 +637,9 @@ int cta_diffusion_bwd_bld(const void* grad_out, void* grad_in, const void* x, fl
     m.msB = mask_sB;
     m.msL = mask_sL;
     fill_alpha(m, steps, alpha, alpha_dev, alpha_dev_dtype);
+    m.contract = contract_for(dtype);
     const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-    m.TL = pick_tl(L, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, 1));
+    m.TL = pick_tl(L, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, 1, 0, m.contract));
     m.out_begin = 0;
     m.out_end = L;
     m.y_quad_ok = quad_ok(grad_in, dtype, B, D, d_sB, d_sL) ? 1 : 0;
@@ -802,7 +804,7 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
     a.hext_hi = a.hi_ext ? static_cast<int>(hi_rows) : 0;
   }
   for (int k = 0; k < kMaxSteps; ++k) a.alpha[k] = alpha;
-  a.contract = backward ? 0 : contract_for(dtype);
+  a.contract = contract_for(dtype);
   const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
   a.TL = edge ? static_cast<int>(std::min<int64_t>(kBldMaxTL, ((oe - ob + kBldRC - 1) / kBldRC) * kBldRC))
               : pick_tl(oe - ob, ndt * B, steps,

@@ -115,8 +115,9 @@ struct BldArgs {
   const void* g_lo_ext;
   const void* g_hi_ext;
   int g_hext_lo, g_hext_hi;
-  // forward diffusion with 16-bit I/O: the contracted update (one fma for
-  // c + alpha * lap, the reference's Triton op order) instead of the exact one
+  // diffusion with 16-bit I/O: the contracted update (one fma for c + alpha *
+  // lap, the reference's Triton op order; g + alpha * lap(a) in the adjoint)
+  // instead of the exact one
   int contract;
   // test hook (forward march only, 0 = off): CTA (0, 0, 0) waits this many
   // microseconds on an mbarrier phase that nothing completes, then takes the
@@ -188,7 +189,7 @@ size_t bdl_march_smem_bytes(int dtype);
 // march kernel with d(alpha), steps 1..kDaMaxSteps
 cudaError_t launch_bld_dalpha(const BldArgs& a, const CUtensorMap* gmap, const CUtensorMap* xmap,
                               const CUtensorMap* ymap, int dtype, int steps, int causal, dim3 grid, cudaStream_t st);
-int bld_dalpha_ctas_per_sm(int dtype, int steps, int causal);
+int bld_dalpha_ctas_per_sm(int dtype, int steps, int causal, int contract = 0);
 size_t dalpha_smem_bytes(int dtype, int steps, int causal);
 int read_device_error_bld_dalpha(int clear);
 

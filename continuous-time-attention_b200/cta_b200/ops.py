@@ -235,8 +235,10 @@ def bld_backward(
     mask: Optional[torch.Tensor] = None,
     need_dalpha: bool = False,
     out: Optional[torch.Tensor] = None,
+    arith: Optional[str] = None,
 ):
-    """grad_in = A_1^T .. A_S^T grad_out; with need_dalpha also d(alpha_k) (fp32 [steps])."""
+    """grad_in = A_1^T .. A_S^T grad_out; with need_dalpha also d(alpha_k) (fp32 [steps]).
+    `arith` as for bld_forward (16-bit tensors; None = the process default)."""
     _require_cuda(grad_out, "grad_out")
     g = _bld_view(grad_out)
     B, L, D = g.shape
@@ -258,7 +260,7 @@ def bld_backward(
         ws_bytes = int(lib.cta_diffusion_bwd_bld_workspace_bytes(B, L, D, _lib.dtype_code(g.dtype), steps,
                                                                  int(causal)))
         ws = _workspace(g.device, ws_bytes)
-    with _lib.on_device(g):
+    with _lib.on_device(g), _lib.thread_arithmetic(arith):
         rc = lib.cta_diffusion_bwd_bld(
             _lib.ptr(g), _lib.ptr(dx), _lib.ptr(xs), _lib.ptr(dalpha), _lib.ptr(ws), ws_bytes, B, L, D,
             g.stride(0), g.stride(1), xs.stride(0) if xs is not None else 0, xs.stride(1) if xs is not None else 0,
@@ -368,6 +370,7 @@ def shard_part_dalpha(
     x_lo: Optional[torch.Tensor] = None,
     x_hi: Optional[torch.Tensor] = None,
     stream: Optional[torch.cuda.Stream] = None,
+    arith: Optional[str] = None,
 ) -> None:
     """One launch over a part of an L-shard's backward with d(alpha): writes the
     part's rows of dx_out and ADDS the part's d(alpha) sum to `dalpha` (fp32 [steps])."""
@@ -388,7 +391,7 @@ def shard_part_dalpha(
     ws_bytes = int(lib.cta_diffusion_bwd_bld_workspace_bytes(B, Lloc, D, code, steps, int(causal)))
     with torch.cuda.stream(st):
         ws = _workspace(g_local.device, ws_bytes)
-    with _lib.on_device(g_local):
+    with _lib.on_device(g_local), _lib.thread_arithmetic(arith):
         rc = lib.cta_diffusion_shard_bld_dalpha(
             _lib.ptr(g_local), _lib.ptr(x_local), _lib.ptr(dx_out), _lib.ptr(dalpha), _lib.ptr(ws), ws_bytes, B, Lloc,
             D, int(pos_offset), int(global_len), _lib.ptr(g_lo), rows[0], _lib.ptr(g_hi), rows[1], _lib.ptr(x_lo),

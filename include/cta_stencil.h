@@ -73,9 +73,15 @@ int cta_set_tuning(int key, int value);
  *                          (kernels/diffusion_triton.py:89-90, :252-259); within
  *                          one bf16 / fp16 rounding of the exact result.
  * Applies to the forward kernels (cta_diffusion_fwd_bdl / _bdl_ex forward,
- * _fwd_bld, _fwd_bld_residual, _fwd_varlen[_residual], _shard_bld forward); the
- * backward kernels, the pooled forward and the advection / reaction steps are
- * always exact.  cta_set_arithmetic sets the process default (initially
+ * _fwd_bld, _fwd_bld_residual, _fwd_varlen[_residual], _shard_bld) and to the
+ * [B, L, D] backward kernels (cta_diffusion_bwd_bld, its _noalloc form,
+ * _shard_bld backward, _shard_bld_dalpha), where the adjoint level becomes
+ * g + alpha * lap(a) in one fma and the forward recomputation follows the
+ * forward's order; the [B, D, L] adjoint, the pooled forward and the
+ * advection / reaction steps are always exact.  (The reference has no
+ * bit-exact backward to match: its gradients come from autograd or from the
+ * Triton adjoint kernel, kernels/diffusion_triton.py:96-133, each with its own
+ * order.)  cta_set_arithmetic sets the process default (initially
  * CTA_ARITH_CONTRACTED) and returns the previous one (-1: unknown mode).
  * cta_set_thread_arithmetic overrides it for the calling thread (mode -1 =
  * follow the process default) and returns the thread's previous override. */

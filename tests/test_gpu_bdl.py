@@ -154,7 +154,7 @@ def test_tma_form_matches_oracle(causal, backward, use_mask, shape, dtype):
     kw = dict(layout="bdl", causal=causal, attention_mask=mask)
     y = ops.bdl(x.cuda(), al, steps, causal=causal, backward=backward, mask=None if mask is None else mask.cuda())
     if not backward:
-        assert torch.equal(y.cpu(), O.fused_stack(x, al, **kw))
+        assert torch.equal(y.cpu(), O.fused_stack(x, al, **kw, contracted=contracted(dtype)))
     else:
         # the adjoint is applied to x itself as the gradient; reference in fp32
         dx_ref, _ = O.grads(lambda t: O.fused_stack(t, al, **kw), torch.randn(B, D, L), x.float())

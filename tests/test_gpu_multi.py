@@ -50,11 +50,11 @@ def _worker(rank, world, port, q):
             results.append(bool(torch.equal(y, ref)))
         from cta_b200.sharded import sharded_diffusion_backward_dalpha
 
-        for steps, causal in [(4, False), (3, True)]:
+        for steps, causal in [(4, False), (3, True), (8, False), (7, True)]:
             torch.manual_seed(1)
             x = torch.randn(2, 3001, 512, dtype=torch.bfloat16).cuda()
             g = torch.randn(2, 3001, 512, dtype=torch.bfloat16).cuda()
-            al = [0.1, 0.05, 0.12, 0.02][:steps]
+            al = [0.1, 0.05, 0.12, 0.02, 0.08, 0.03, 0.11, 0.07][:steps]
             spec = even_shards(3001, world, rank)
             sl = slice(spec.pos_offset, spec.pos_offset + spec.local_len)
             dx, da = sharded_diffusion_backward_dalpha(g[:, sl], x[:, sl], spec, alphas=al, steps=steps,
@@ -88,4 +88,4 @@ def test_two_gpu_sharded_matches_single_gpu():
     while not q.empty():
         r, v = q.get()
         res[r] = v
-    assert res == {0: [True] * 6, 1: [True] * 6}, res
+    assert res == {0: [True] * 8, 1: [True] * 8}, res
