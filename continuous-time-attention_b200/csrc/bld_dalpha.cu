@@ -125,10 +125,14 @@ __device__ void fill_da_chunk(const BldArgs& a, const void* src, int64_t sB, int
 // minimum resident one-warp CTAs per SM handed to __launch_bounds__ is the
 // largest at which ptxas -v shows no spills for every dtype and direction.
 template <typename T, int S, bool CAUSAL>
+#ifndef CTA_DA_MIN34
+#define CTA_DA_MIN34 16
+#endif
 constexpr int da_min_ctas() {
   // ptxas budgets registers per SM sub-partition (16384 each, warps spread over
   // 4), so 10 or 12 CTAs both cap a lane at 168 registers and 8 at 255
-  return S <= 2 ? 24 : S == 3 ? 16 : S == 4 ? (CAUSAL ? 12 : 16) : S == 5 ? 12 : (S == 6 && !CAUSAL) ? 12 : 8;
+  return S <= 2 ? 24 : S == 3 ? CTA_DA_MIN34 : S == 4 ? (CAUSAL ? 12 : CTA_DA_MIN34) : S == 5 ? 12
+         : (S == 6 && !CAUSAL) ? 12 : 8;
 }
 
 // KIND 1 / 2 (steps 1 only): the backward of one advection- / reaction-
@@ -298,43 +302,11 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
       }
     };
 
-    // One march row: TCT >= 0 is the compile-time march row of a prologue row
-    // (start-up triangles of both wavefronts skipped); I the row in its chunk;
-    // lim = nout + PRO - (first march row of the chunk).
-    auto step_row = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, pf2* g, pf2* x) {
+    // The forward recomputation of one march row: lap(u_q) of the row for every
+    // level q into la, the levels advanced (state F1, F2).
+    auto fwd_levels = [&](auto slow_tag, auto tct_tag, int64_t jx, pf2* x, pf2 (&la)[S][NP]) {
       constexpr bool SLOW = decltype(slow_tag)::value;
       constexpr int TCT = decltype(tct_tag)::value;
-      constexpr int I = decltype(i_tag)::value;
-      const int64_t jg = jbg + t, jx = jbx + t;
-      if (SLOW) {
-        if (rb.zero(jg))
-#pragma unroll
-          for (int p = 0; p < NP; ++p) g[p] = 0ull;
-        if (rb.zero(jx))
-#pragma unroll
-          for (int p = 0; p < NP; ++p) x[p] = 0ull;
-      }
-      // ---- KIND 1/2: the beta term h(x) of the paired row and, for reaction,
-      // f'(x) of the row the adjoint finishes (from the window before its shift) ----
-      pf2 h[NP], fp[NP];
-#pragma unroll
-      for (int p = 0; p < NP; ++p) {
-        h[p] = fp[p] = 0ull;
-        if constexpr (KIND == 1) {
-          h[p] = CAUSAL ? pfma(F1[0][p], n1, x[p]) : pmul(pfma(F2[0][p], n1, x[p]), half);
-        } else if constexpr (KIND == 2) {
-          // the paired row is jg; the finished row jg-1 (causal jg-2), whose x is
-          // F2 and whose sigmoid was taken one (two) march steps ago
-          const pf2 c_ = CAUSAL ? x[p] : F1[0][p];
-          const pf2 sv = psigmoid(c_);
-          h[p] = reaction_f(c_, sv);
-          fp[p] = reaction_df(F2[0][p], CAUSAL ? S2[p] : S1[p]);
-          S2[p] = S1[p];
-          S1[p] = sv;
-        }
-      }
-      // ---- forward recomputation: lap(u_q) of this march row, q = 0..S-1 ----
-      pf2 la[S][NP];
       {
         const bool fxc = SLOW && CAUSAL && rb.fixed(jx);
         const uint32_t fwx = (SLOW && !CAUSAL) ? rb.window8_fixed(jx - S) : 0u;
@@ -360,7 +332,15 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
           }
         }
       }
-      // ---- adjoint march, pairing g_k with lap(u_{k-1}) ----
+    };
+
+    // The adjoint of one march row: g_k paired with lap(u_{k-1}) through the
+    // delay rings into d(alpha), the adjoint levels advanced (state P, G).
+    auto adj_levels = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, int64_t jg, pf2* g,
+                          const pf2 (&la)[S][NP], const pf2* h, const pf2* fp) {
+      constexpr bool SLOW = decltype(slow_tag)::value;
+      constexpr int TCT = decltype(tct_tag)::value;
+      constexpr int I = decltype(i_tag)::value;
       const bool f0 = SLOW && rb.fixed(jg);
       const uint32_t fw = SLOW ? (CAUSAL ? rb.window16_fixed(jg - 2 * S) : rb.window8_fixed(jg - S)) : 0u;
       pf2 c[NP], q[NP];
@@ -453,12 +433,89 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
       });
     };
 
+    // One march row: TCT >= 0 is the compile-time march row of a prologue row
+    // (start-up triangles of both wavefronts skipped); I the row in its chunk;
+    // lim = nout + PRO - (first march row of the chunk).
+    auto step_row = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, pf2* g, pf2* x) {
+      constexpr bool SLOW = decltype(slow_tag)::value;
+      constexpr int TCT = decltype(tct_tag)::value;
+      constexpr int I = decltype(i_tag)::value;
+      const int64_t jg = jbg + t, jx = jbx + t;
+      if (SLOW) {
+        if (rb.zero(jg))
+#pragma unroll
+          for (int p = 0; p < NP; ++p) g[p] = 0ull;
+        if (rb.zero(jx))
+#pragma unroll
+          for (int p = 0; p < NP; ++p) x[p] = 0ull;
+      }
+      // ---- KIND 1/2: the beta term h(x) of the paired row and, for reaction,
+      // f'(x) of the row the adjoint finishes (from the window before its shift) ----
+      pf2 h[NP], fp[NP];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        h[p] = fp[p] = 0ull;
+        if constexpr (KIND == 1) {
+          h[p] = CAUSAL ? pfma(F1[0][p], n1, x[p]) : pmul(pfma(F2[0][p], n1, x[p]), half);
+        } else if constexpr (KIND == 2) {
+          // the paired row is jg; the finished row jg-1 (causal jg-2), whose x is
+          // F2 and whose sigmoid was taken one (two) march steps ago
+          const pf2 c_ = CAUSAL ? x[p] : F1[0][p];
+          const pf2 sv = psigmoid(c_);
+          h[p] = reaction_f(c_, sv);
+          fp[p] = reaction_df(F2[0][p], CAUSAL ? S2[p] : S1[p]);
+          S2[p] = S1[p];
+          S1[p] = sv;
+        }
+      }
+      pf2 la[S][NP];
+      fwd_levels(slow_tag, tct_tag, jx, x, la);
+      adj_levels(slow_tag, tct_tag, i_tag, t, lim, jg, g, la, h, fp);
+    };
+
     // kind: 0..NPRO-1 = prologue chunk, NPRO = full output chunk, NPRO+1 = partial last chunk
     auto march_chunk = [&](auto slow_tag, auto kind_tag, int c, const T* gbuf, const T* xbuf) {
       constexpr int CK = decltype(kind_tag)::value;
       const int t0 = c * kFwdRC;
       const int lim = nrows - t0;
       T* st = stage + ((c - NPRO) & 1) * CHUNK + cb;
+      if constexpr (CTA_DA_SWP && KIND == 0 && CK == NPRO && !decltype(slow_tag)::value) {
+        // Full chunks of tiles without fixed rows, software-pipelined by one row:
+        // the forward recomputation of row i+1 is issued before the adjoint of
+        // row i, so the two independent dependency chains interleave.  Each
+        // level still sees its rows in order: the arithmetic is unchanged.
+        pf2 la0[S][NP], la1[S][NP];
+        auto pick = [&](auto odd) -> pf2 (&)[S][NP] {
+          if constexpr (decltype(odd)::value) return la1;
+          else return la0;
+        };
+        auto load_row = [&](int i, const T* buf, pf2* v) {
+          pf2 hi_;
+          Q::split(*reinterpret_cast<const V*>(buf + cb + i * kDaDT), v[0], NP > 1 ? v[NP - 1] : hi_);
+        };
+        const auto tl = std::integral_constant<int, -1>{};
+        {
+          pf2 x[NP];
+          load_row(0, xbuf, x);
+          fwd_levels(std::false_type{}, tl, jbx + t0, x, la0);
+        }
+        static_for<kFwdRC>([&](auto II) {
+          constexpr int i = decltype(II)::value;
+          if constexpr (i + 1 < kFwdRC) {
+            pf2 x[NP];
+            load_row(i + 1, xbuf, x);
+            fwd_levels(std::false_type{}, tl, jbx + t0 + i + 1, x, pick(std::integral_constant<bool, (i + 1) % 2 == 1>{}));
+          }
+          pf2 g[NP];
+          load_row(i, gbuf, g);
+          const pf2 hz[NP] = {};
+          adj_levels(std::false_type{}, tl, II, t0 + i, lim, jbg + t0 + i, g,
+                     pick(std::integral_constant<bool, i % 2 == 1>{}), hz, hz);
+          if (tstore) *reinterpret_cast<V*>(st + i * kDaDT) = Q::join(g[0], NP > 1 ? g[NP - 1] : 0ull);
+          else store_row(l0 + t0 + i - PRO, g);
+        });
+        return;
+      }
       static_for<kFwdRC>([&](auto II) {
         constexpr int i = decltype(II)::value;
         pf2 g[NP], x[NP], hi_;

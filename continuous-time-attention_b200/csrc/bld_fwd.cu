@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   static_assert(!FM || (KIND == 0 && !POOL), "the contracted update is the diffusion forward / adjoint");
   static_assert(!POOL || (!ADJ && !RES && KIND == 0 && !CAUSAL), "the pooled form is the non-causal forward");
   static_assert(!RES || (!ADJ && !CAUSAL), "the residual form is the non-causal forward");
-  static_assert(KIND == 0 || (S == 1 && !ADJ && !RES), "the other PDE kinds are single forward steps");
+  static_assert(KIND == 0 || (S <= kPdeMaxSteps && !ADJ && !RES), "the other PDE kinds: forward stacks of up to 4 steps");
   constexpr int PKIND = KIND;  // the update kind (the chunk lambdas below name their chunk kind KIND)
   // every global read (cu_seqlens, mask, alphas, the streams) comes after the wait
   pdl_launch_dependents();
@@ -254,10 +254,15 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   const pf2 m2 = pbc(-2.f);
   const pf2 zn = pbc(a.neg_zero);
   // KIND 1/2: beta in coefficient slot 1
-  const float be_s = KIND == 0 ? 0.f
-                               : (a.alpha_dev[1] != nullptr ? load_scalar(a.alpha_dev[1], a.alpha_dev_dtype)
-                                                            : a.alpha[1]);
-  const pf2 be = pbc(be_s);
+  // KIND 1/2: the per-level beta of each layer of the stack (device scalars or host values)
+  float bes[S];
+  pf2 bev[S];
+#pragma unroll
+  for (int k = 0; k < S; ++k) {
+    bes[k] = KIND == 0 ? 0.f
+                       : (a.beta_dev[k] != nullptr ? load_scalar(a.beta_dev[k], a.alpha_dev_dtype) : a.beta[k]);
+    bev[k] = pbc(bes[k]);
+  }
 
   // per-level state, for both pairs.  Forward: the level's input on the two
   // previous march rows (P1, P2).  Adjoint: a = alpha*g on the two previous
@@ -376,8 +381,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       for (int k = 0; k < S; ++k) {
         pf2 na = xa, nb = xb;
         if (TCT < 0 || TCT >= 2 * k + 2) {
-          na = level_update<KIND, true, FM>(P2a[k], P1a[k], xa, al[k], be, be_s, m2, zn);
-          nb = level_update<KIND, true, FM>(P2b[k], P1b[k], xb, al[k], be, be_s, m2, zn);
+          na = level_update<KIND, true, FM>(P2a[k], P1a[k], xa, al[k], bev[k], bes[k], m2, zn);
+          nb = level_update<KIND, true, FM>(P2b[k], P1b[k], xb, al[k], bev[k], bes[k], m2, zn);
           if (SLOW) {
             na = psel(fx, xa, na);
             nb = psel(fx, xb, nb);
@@ -397,8 +402,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       for (int k = 0; k < S; ++k) {
         pf2 na = xa, nb = xb;
         if (TCT < 0 || TCT >= 2 * k + 2) {
-          na = level_update<KIND, false, FM>(P2a[k], P1a[k], xa, al[k], be, be_s, m2, zn);
-          nb = level_update<KIND, false, FM>(P2b[k], P1b[k], xb, al[k], be, be_s, m2, zn);
+          na = level_update<KIND, false, FM>(P2a[k], P1a[k], xa, al[k], bev[k], bes[k], m2, zn);
+          nb = level_update<KIND, false, FM>(P2b[k], P1b[k], xb, al[k], bev[k], bes[k], m2, zn);
           if (SLOW) {
             const bool fx = (fw >> (S - 1 - k)) & 1u;
             na = psel(fx, P1a[k], na);
@@ -495,8 +500,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
               ua[i] = na;
               ub[i] = nb;
             } else {
-              const pf2 na = level_update<PKIND, CAUSAL, FM>(P2a[m], P1a[m], ua[i], al[m], be, be_s, m2, zn);
-              const pf2 nb = level_update<PKIND, CAUSAL, FM>(P2b[m], P1b[m], ub[i], al[m], be, be_s, m2, zn);
+              const pf2 na = level_update<PKIND, CAUSAL, FM>(P2a[m], P1a[m], ua[i], al[m], bev[m], bes[m], m2, zn);
+              const pf2 nb = level_update<PKIND, CAUSAL, FM>(P2b[m], P1b[m], ub[i], al[m], bev[m], bes[m], m2, zn);
               P2a[m] = P1a[m];
               P1a[m] = ua[i];
               ua[i] = na;
@@ -704,11 +709,20 @@ const void* march_ptr(int steps) {
   }
 }
 
+template <typename T, int KIND, bool CAUSAL>
+const void* march_ptr_kind_c(int steps) {
+  switch (steps) {
+    case 1: return reinterpret_cast<const void*>(bld_march_kernel<T, 1, CAUSAL, false, false, KIND>);
+    case 2: return reinterpret_cast<const void*>(bld_march_kernel<T, 2, CAUSAL, false, false, KIND>);
+    case 3: return reinterpret_cast<const void*>(bld_march_kernel<T, 3, CAUSAL, false, false, KIND>);
+    case 4: return reinterpret_cast<const void*>(bld_march_kernel<T, 4, CAUSAL, false, false, KIND>);
+    default: return nullptr;
+  }
+}
+
 template <typename T, int KIND>
 const void* march_ptr_kind(int steps, int causal) {
-  if (steps != 1) return nullptr;
-  return causal ? reinterpret_cast<const void*>(bld_march_kernel<T, 1, true, false, false, KIND>)
-                : reinterpret_cast<const void*>(bld_march_kernel<T, 1, false, false, false, KIND>);
+  return causal ? march_ptr_kind_c<T, KIND, true>(steps) : march_ptr_kind_c<T, KIND, false>(steps);
 }
 
 template <typename T>

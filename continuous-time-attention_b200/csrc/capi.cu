@@ -286,6 +286,25 @@ int launch_dalpha_march(BldArgs& m, int dtype, int steps, int causal, int64_t B,
 
 }  // namespace
 
+namespace {
+
+// The forward of `steps` advection- / reaction-diffusion layer steps (m.pde_kind,
+// coefficients already in m) on the march kernel.
+int pde_forward_launch(BldArgs& m, int dtype, int steps, int causal, int64_t B, int64_t L, int64_t D, int64_t y_sB,
+                       int64_t y_sL, cudaStream_t st) {
+  const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
+  m.TL = pick_tl(L, ndt * B, steps, march_per_sm(dtype, steps, causal ? 1 : 0, 0));
+  m.y_quad_ok = quad_ok(m.y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
+  CUtensorMap xmap, ymap;
+  std::memset(&xmap, 0, sizeof(xmap));
+  std::memset(&ymap, 0, sizeof(ymap));
+  m.use_tma = make_map(&xmap, m.x, dtype, B, L, D, m.xsB, m.xsL, kFwdRC, kFwdDT) ? 1 : 0;
+  m.use_tma_store = make_map(&ymap, m.y, dtype, B, L, D, y_sB, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
+  return launch_fwd(m, dtype, steps, causal ? 1 : 0, B, L, st, xmap, ymap);
+}
+
+}  // namespace
+
 int cta::pdl_enabled() { return g_tuning.pdl; }
 
 void cta::set_last_error(const char* fmt, ...) {
@@ -890,15 +909,56 @@ int cta_pde_step_bld(const void* x, const void* grad_out, void* y, float* dcoef,
     m.gsL = g_sL;
     return launch_dalpha_march(m, dtype, 1, causal ? 1 : 0, B, L, D, workspace, dcoef, false, true, st);
   }
-  const int64_t ndt = (D + kFwdDT - 1) / kFwdDT;
-  m.TL = pick_tl(L, ndt * B, 1, march_per_sm(dtype, 1, causal ? 1 : 0, 0));
-  m.y_quad_ok = quad_ok(y, dtype, B, D, y_sB, y_sL) ? 1 : 0;
-  CUtensorMap xmap, ymap;
-  std::memset(&xmap, 0, sizeof(xmap));
-  std::memset(&ymap, 0, sizeof(ymap));
-  m.use_tma = make_map(&xmap, x, dtype, B, L, D, x_sB, x_sL, kFwdRC, kFwdDT) ? 1 : 0;
-  m.use_tma_store = make_map(&ymap, y, dtype, B, L, D, y_sB, y_sL, kFwdRC, kFwdDT) ? 1 : 0;
-  return launch_fwd(m, dtype, 1, causal ? 1 : 0, B, L, st, xmap, ymap);
+  m.beta_dev[0] = beta_dev;
+  return pde_forward_launch(m, dtype, 1, causal, B, L, D, y_sB, y_sL, st);
+}
+
+int cta_pde_stack_bld(const void* x, void* y, int64_t B, int64_t L, int64_t D, int64_t x_sB, int64_t x_sL,
+                      int64_t y_sB, int64_t y_sL, int dtype, int kind, int steps, int causal,
+                      const void* const* alpha_dev, const void* const* beta_dev, int coef_dtype, const void* mask,
+                      int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream) {
+  int rc = check_common(dtype, steps);
+  if (rc) return rc;
+  if (steps > kPdeMaxSteps)
+    return fail(CTA_EINVAL, "a fused advection / reaction stack takes at most %d steps, got %d", kPdeMaxSteps, steps);
+  if (kind != CTA_PDE_ADVECTION && kind != CTA_PDE_REACTION) return fail(CTA_EINVAL, "bad PDE kind %d", kind);
+  if (alpha_dev == nullptr || beta_dev == nullptr) return fail(CTA_EINVAL, "alpha / beta device scalars missing");
+  for (int k = 0; k < steps; ++k)
+    if (alpha_dev[k] == nullptr || beta_dev[k] == nullptr)
+      return fail(CTA_EINVAL, "alpha_dev[%d] / beta_dev[%d] is NULL", k, k);
+  if (coef_dtype != CTA_F32 && coef_dtype != CTA_BF16 && coef_dtype != CTA_F16)
+    return fail(CTA_EINVAL, "bad coefficient dtype %d", coef_dtype);
+  if (B < 0 || L < 0 || D < 0) return fail(CTA_EINVAL, "negative shape");
+  if (B > 65535) return fail(CTA_EUNSUPPORTED, "at most 65535 batch rows");
+  if (L > 0 && L < 3) return fail(CTA_EINVAL, "L < 3 is the identity; handled by the caller");
+  if (x == nullptr || y == nullptr) return fail(CTA_EINVAL, "null tensor pointer");
+  if (x_sL < D || y_sL < D) return fail(CTA_EINVAL, "row stride smaller than D");
+  if (mask != nullptr && !valid_mask_dtype(mask_dtype)) return fail(CTA_EINVAL, "bad mask dtype %d", mask_dtype);
+  if (B == 0 || L == 0 || D == 0) return ok();
+  BldArgs m = blank_bld();
+  m.x = x;
+  m.y = y;
+  m.xsB = x_sB;
+  m.xsL = x_sL;
+  m.ysB = y_sB;
+  m.ysL = y_sL;
+  m.L = L;
+  m.D = static_cast<int>(D);
+  m.nbatch = static_cast<int>(B);
+  m.global_len = L;
+  m.mask = mask;
+  m.mask_dtype = mask_dtype;
+  m.msB = mask_sB;
+  m.msL = mask_sL;
+  for (int k = 0; k < steps; ++k) {
+    m.alpha_dev[k] = alpha_dev[k];
+    m.beta_dev[k] = beta_dev[k];
+  }
+  m.alpha_dev_dtype = coef_dtype;
+  m.pde_kind = kind == CTA_PDE_ADVECTION ? 1 : 2;
+  m.out_begin = 0;
+  m.out_end = L;
+  return pde_forward_launch(m, dtype, steps, causal, B, L, D, y_sB, y_sL, static_cast<cudaStream_t>(stream));
 }
 
 int cta_diffusion_shard_bld_dalpha(const void* grad_out, const void* x, void* grad_in, float* dalpha,

@@ -49,8 +49,12 @@ constexpr int kFwdOutSlots = CTA_FWD_OUT_SLOTS;
 constexpr int64_t kWsHeaderBytes = 8192;
 constexpr int kWsMaxGroups = static_cast<int>(kWsHeaderBytes / 4) - 1;
 constexpr int kDaMaxSteps = 8;  // steps handled by the march d(alpha) kernel
+constexpr int kPdeMaxSteps = 4;  // advection / reaction layers fused per forward launch
 // march d(alpha) kernel: packed column pairs per lane (1: 64-column tiles, half
 // the per-lane state of two pairs, twice the resident warps)
+#ifndef CTA_DA_SWP
+#define CTA_DA_SWP 0
+#endif
 #ifndef CTA_DA_PAIRS
 #define CTA_DA_PAIRS 1
 #endif
@@ -104,9 +108,12 @@ struct BldArgs {
   // with element strides (rsB, rsL), added as an elementwise add of type T
   const void* residual;
   int64_t rsB, rsL;
-  // 0: diffusion.  1 / 2: advection- / reaction-diffusion layer step (steps 1,
-  // beta in coefficient slot 1)
+  // 0: diffusion.  1 / 2: advection- / reaction-diffusion layer steps.  The
+  // forward reads level k's beta from beta_dev[k] (device scalar of
+  // alpha_dev_dtype) or beta[k]; the backward (steps 1) from coefficient slot 1
   int pde_kind;
+  const void* beta_dev[kMaxSteps];
+  float beta[kMaxSteps];
   // forward only: masked mean pool of the output instead of storing it,
   // per-CTA column sums [nbatch][row tiles][D] (fp32, caller scratch)
   float* pool_partial;

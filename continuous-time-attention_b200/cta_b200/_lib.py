@@ -26,6 +26,7 @@ CTA_OK, CTA_EINVAL, CTA_EUNSUPPORTED, CTA_ECUDA = 0, 1, 2, 3
 SHARD_INTERIOR, SHARD_LO_EDGE, SHARD_HI_EDGE = 0, 1, 2
 PDE_ADVECTION, PDE_REACTION = 0, 1
 MAX_STEPS = 8
+PDE_STACK_MAX_STEPS = 4
 ARITH_EXACT, ARITH_CONTRACTED = 0, 1
 _ARITH_CODES = {"exact": ARITH_EXACT, "contracted": ARITH_CONTRACTED}
 
@@ -77,6 +78,9 @@ _SIGNATURES = {
                                                c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
                                                POINTER(c_float), c_void_p, c_int, c_int64, c_int64, c_void_p]),
     "cta_pde_step_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "cta_pde_stack_bld": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
+                                  c_int64, c_int, c_int, c_int, c_int, POINTER(c_void_p), POINTER(c_void_p), c_int,
+                                  c_void_p, c_int, c_int64, c_int64, c_void_p]),
     "cta_pde_step_bld": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                                  c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int, c_int, c_int,
                                  c_void_p, c_void_p, c_int, c_void_p, c_int, c_int64, c_int64, c_void_p]),

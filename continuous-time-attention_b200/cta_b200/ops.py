@@ -457,6 +457,47 @@ def pde_step(
     return y if grad_out is None else (y, dcoef)
 
 
+def pde_stack(
+    x: torch.Tensor,
+    kind: int,
+    alphas: Sequence[torch.Tensor],
+    betas: Sequence[torch.Tensor],
+    *,
+    causal: bool = False,
+    mask: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Forward of up to 4 consecutive advection- / reaction-diffusion layers of
+    one kind (_lib.PDE_*) on [B, L, D] in one launch, fp32 kept between them.
+    alphas[k], betas[k]: layer k's [1] parameters, read on the device."""
+    _require_cuda(x, "x")
+    if x.dim() != 3:
+        raise ValueError("x must have shape (B, L, D)")
+    steps = len(alphas)
+    if steps != len(betas) or not 1 <= steps <= _lib.PDE_STACK_MAX_STEPS:
+        raise ValueError(f"need 1..{_lib.PDE_STACK_MAX_STEPS} alpha / beta pairs")
+    x = _bld_view(x)
+    B, L, D = x.shape
+    coefs = []
+    for c in list(alphas) + list(betas):
+        c = c.detach()
+        if c.device != x.device:
+            raise ValueError(f"coefficient on {c.device}, expected {x.device}")
+        coefs.append(c.float().contiguous() if c.dtype != torch.float32 else c.contiguous())
+    m, mcode, msb, msl = _mask_args(mask, B, L, x.device)
+    y = _out(out, (B, L, D), x)
+    lib = _lib.load()
+    with _lib.on_device(x):
+        rc = lib.cta_pde_stack_bld(
+            _lib.ptr(x), _lib.ptr(y), B, L, D, x.stride(0), x.stride(1), y.stride(0), y.stride(1),
+            _lib.dtype_code(x.dtype), int(kind), steps, int(causal), _lib.ptr_array(coefs[:steps]),
+            _lib.ptr_array(coefs[steps:]), 0, _lib.ptr(m), mcode, msb, msl, _lib.stream_ptr(x),
+        )
+    del coefs
+    _lib.check(rc)
+    return y
+
+
 def bld_forward_pool(
     x: torch.Tensor, alphas: Sequence[AlphaLike], steps: int, mask: torch.Tensor
 ) -> torch.Tensor:

@@ -43,6 +43,7 @@ __all__ = [
     "diffusion_pde_stack",
     "diffusion_stack_function",
     "diffusion_stack_pool",
+    "pde_stack_forward",
 ]
 
 
@@ -301,6 +302,47 @@ class AdvectionDiffusionPDELayer(_TwoCoefficientLayer):
     def __init__(self, hidden_size: int, alpha_init: float = 0.10, beta_init: float = 0.03, layout: str = "bdl",
                  causal: bool = False):
         super().__init__(hidden_size, alpha_init, beta_init, layout=layout, causal=causal)
+
+
+def pde_stack_forward(
+    x: torch.Tensor,
+    layers: Sequence[nn.Module],
+    attention_mask: Optional[torch.Tensor] = None,
+    layout: Optional[str] = None,
+) -> torch.Tensor:
+    """Inference forward of consecutive advection- or reaction-diffusion layers
+    (one kind, one causality): one launch per 4 layers instead of one per layer,
+    fp32 kept between the layers of a launch (identical to the layer chain in
+    fp32, within one rounding per layer in 16-bit dtypes).  ``layout`` is x's
+    layout (default: the layers'); the kernel runs on [B, L, D].  No autograd
+    graph is recorded: training takes the per-layer path, whose backward needs
+    every layer's input."""
+    layers = list(layers)
+    if not layers:
+        return x
+    kind, causal = layers[0].KIND, layers[0].causal
+    for l in layers:
+        if not isinstance(l, _TwoCoefficientLayer) or l.KIND != kind or l.causal != causal:
+            raise ValueError("a fused stack needs advection- or reaction-diffusion layers of one kind and causality")
+    layout = layers[0].layout if layout is None else layout
+    seq_dim = 2 if layout == "bdl" else 1
+    if x.size(seq_dim) < 3:
+        return x
+    if x.device.type != "cuda":
+        raise ValueError("x must be on CUDA")
+    mask = attention_mask
+    if mask is not None:
+        if mask.device != x.device:
+            mask = mask.to(x.device)
+        if mask.dtype == torch.bool:
+            mask = mask.to(torch.uint8)
+    y = x.transpose(1, 2) if layout == "bdl" else x
+    with torch.no_grad():
+        for i in range(0, len(layers), _lib.PDE_STACK_MAX_STEPS):
+            chunk = layers[i : i + _lib.PDE_STACK_MAX_STEPS]
+            y = ops.pde_stack(y.contiguous(), kind, [l.alpha for l in chunk], [l.beta for l in chunk], causal=causal,
+                              mask=mask)
+    return y.transpose(1, 2).contiguous() if layout == "bdl" else y
 
 
 _PDE_REGISTRY = {

@@ -5,12 +5,17 @@ per rank.  A fused forward (or adjoint) over `steps` steps needs, for every
 output row, the input rows within `steps` of it (2*steps on one side for the
 causal stencil and its adjoint), so each call:
 
-  1. posts the halo exchange -- the rows a neighbour needs are sent with NCCL
-     point-to-point (``batch_isend_irecv``) from a side stream;
-  2. meanwhile runs the interior kernel, which computes every output row whose
-     stencil stays inside the local shard;
-  3. waits for the halos and runs the two small edge kernels, which read the
-     received rows.
+  1. exchanges the halos -- the rows a neighbour needs are sent with NCCL
+     point-to-point (``batch_isend_irecv``), a few tens of microseconds;
+  2. runs the two small edge kernels, which read the received rows, on a side
+     stream;
+  3. meanwhile runs the interior kernel, which computes every output row whose
+     stencil stays inside the local shard.
+
+The exchange comes first because NCCL's kernel needs SMs of its own: queued
+beside the interior kernel, whose one-warp CTAs occupy every SM in one wave, it
+would start only at that kernel's tail (measured on 2 B200s: ~110 us of exposed
+wait per call when the exchange was posted to run under the interior kernel).
 
 Only the two global ends of the sequence use the copy boundary; shard edges
 are interior rows.  The reference has no multi-device path (it runs the
@@ -169,14 +174,21 @@ def sharded_diffusion(
     ev = _PartEvents(timing if on_gpu else None)
     if on_gpu:
         comm = comm_stream if comm_stream is not None else torch.cuda.Stream(device=x_local.device)
+        # The halo exchange runs first, on the caller's stream.  NCCL's kernel
+        # needs SMs: queued beside the interior kernel, whose one-warp CTAs fill
+        # every SM in one wave, it would only start at that kernel's tail.
+        ev.begin("exchange", cur)
+        for w in post_exchange():
+            w.wait()
+        ev.end("exchange", cur)
+        # the edge parts read the halos; on the side stream, launched before the
+        # interior, their few CTAs run beside the interior's wave
         comm.wait_stream(cur)
         with torch.cuda.stream(comm):
-            ev.begin("exchange", comm)
-            works = post_exchange()
-            for w in works:
-                w.wait()
-            ev.end("exchange", comm)
-        # interior rows need no halo: overlap them with the exchange
+            ev.begin("edges", comm)
+            compute(_lib.SHARD_LO_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
+            compute(_lib.SHARD_HI_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
+            ev.end("edges", comm)
         ev.begin("interior", cur)
         compute(_lib.SHARD_INTERIOR, x_local, out, lo_halo=None, hi_halo=None, **kw)
         ev.end("interior", cur)
@@ -185,16 +197,14 @@ def sharded_diffusion(
         ev.end("exposed_wait", cur)
         for h in (lo_halo, hi_halo):
             if h is not None:
-                h.record_stream(cur)
-    else:
-        works = post_exchange()
-        compute(_lib.SHARD_INTERIOR, x_local, out, lo_halo=None, hi_halo=None, **kw)
-        for w in works:
-            w.wait()
-    ev.begin("edges", cur)
+                h.record_stream(comm)
+        return out
+    works = post_exchange()
+    compute(_lib.SHARD_INTERIOR, x_local, out, lo_halo=None, hi_halo=None, **kw)
+    for w in works:
+        w.wait()
     compute(_lib.SHARD_LO_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
     compute(_lib.SHARD_HI_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
-    ev.end("edges", cur)
     return out
 
 
@@ -299,17 +309,11 @@ def sharded_diffusion_backward_dalpha(
     kw = dict(spec=spec, alphas=alphas, steps=steps, causal=causal)
     none = dict(g_lo=None, g_hi=None, x_lo=None, x_hi=None)
     if on_gpu:
-        comm = comm_stream if comm_stream is not None else torch.cuda.Stream(device=dev)
-        comm.wait_stream(cur)
-        with torch.cuda.stream(comm):
-            works = post_exchange()
-            for w in works:
-                w.wait()
+        # exchange first on the caller's stream (see sharded_diffusion); the parts
+        # then add their d(alpha) sums in a fixed order: interior, lo edge, hi edge
+        for w in post_exchange():
+            w.wait()
         compute(_lib.SHARD_INTERIOR, g_local, x_local, dx, dalpha, **none, **kw)
-        cur.wait_stream(comm)
-        for t in halos.values():
-            if t is not None:
-                t.record_stream(cur)
     else:
         works = post_exchange()
         compute(_lib.SHARD_INTERIOR, g_local, x_local, dx, dalpha, **none, **kw)

@@ -14,7 +14,14 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from .pde_layers import _DiffusionFamilyLayer, create_pde_layer, diffusion_pde_stack, diffusion_stack_pool
+from .pde_layers import (
+    _DiffusionFamilyLayer,
+    _TwoCoefficientLayer,
+    create_pde_layer,
+    diffusion_pde_stack,
+    diffusion_stack_pool,
+    pde_stack_forward,
+)
 
 __all__ = ["generate_causal_mask", "PDETransformerClassifier", "PDETransformerLM"]
 
@@ -26,7 +33,12 @@ def generate_causal_mask(seq_len: int, device: torch.device) -> torch.Tensor:
 
 def _refine(x: torch.Tensor, pde_list: nn.ModuleList, layout: str, attention_mask: torch.Tensor) -> torch.Tensor:
     if not all(isinstance(l, _DiffusionFamilyLayer) for l in pde_list):
-        # advection / reaction layers: one step per layer, as the reference loops
+        grad = torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in pde_list.parameters()))
+        kinds = {getattr(l, "KIND", None) for l in pde_list}
+        if not grad and len(kinds) == 1 and all(isinstance(l, _TwoCoefficientLayer) for l in pde_list):
+            # inference: the whole stack in one launch (per 4 layers); x is [B, L, D] here
+            return pde_stack_forward(x, pde_list, attention_mask=attention_mask, layout="bld")
+        # training (or mixed kinds): one step per layer, as the reference loops
         x_t = x.transpose(1, 2).contiguous() if layout == "bdl" else x
         for layer in pde_list:
             x_t = layer(x_t, attention_mask=attention_mask)

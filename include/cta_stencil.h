@@ -254,6 +254,18 @@ int cta_diffusion_shard_bld(const void* in, void* out, int64_t B, int64_t L_loca
                             int64_t hi_rows, int part, int dtype, int steps, int causal, int backward, float alpha,
                             void* stream);
 
+/* The forward of `steps` (1..4) consecutive advection- or reaction-diffusion
+ * layers of one kind (src/models/pde_layers.py:249-318, each with the base
+ * forward of :113-188) in ONE launch, fp32 kept between the layers (a chain of
+ * layer calls rounds to the tensor dtype after each; identical in fp32).
+ * alpha_dev[k], beta_dev[k]: layer k's [1] parameters on the device (dtype
+ * coef_dtype).  Same layout, mask and causality rules as cta_pde_step_bld; no
+ * backward (gradients take one cta_pde_step_bld per layer). */
+int cta_pde_stack_bld(const void* x, void* y, int64_t B, int64_t L, int64_t D, int64_t x_sB, int64_t x_sL,
+                      int64_t y_sB, int64_t y_sL, int dtype, int kind, int steps, int causal,
+                      const void* const* alpha_dev, const void* const* beta_dev, int coef_dtype, const void* mask,
+                      int mask_dtype, int64_t mask_sB, int64_t mask_sL, void* stream);
+
 /* One part of an L-shard's fused backward WITH d(alpha), steps 1..8 (no
  * counterpart in the reference, which is single-device; together with an
  * all-reduce of the per-rank sums it is the sharded form of

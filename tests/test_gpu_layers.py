@@ -320,3 +320,57 @@ def test_stack_pool_matches_stack_then_pool(dtype, steps, shape):
         assert torch.equal(u, v)
     with pytest.raises(ValueError):
         ops.bld_forward_pool(x, [0.1], 1, None)
+
+
+@pytest.mark.parametrize("kind", ["advection", "reaction"])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("steps", [1, 2, 3, 4, 6])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_pde_stack_forward_matches_layer_chain(kind, causal, steps, dtype):
+    """Consecutive advection / reaction layers fused into one launch (per 4
+    layers), fp32 between the layers: against the oracle's layer chain run in
+    fp32 and rounded once (advection bit for bit; reaction to the fp32 bar, its
+    sigmoid uses __expf), and bit for bit against the per-layer kernels in fp32."""
+    from cta_b200.pde_layers import pde_stack_forward
+
+    torch.manual_seed(40 + steps)
+    B, L, D = 2, 700, 264
+    x = (2.0 * torch.randn(B, L, D)).to(dtype)
+    mask = torch.ones(B, L, dtype=torch.long)
+    mask[-1, L - L // 4 :] = 0
+    layers = [_two_coef_layer(kind, D, "bld", causal, 0.1 - 0.01 * k, 0.05 + 0.01 * k) for k in range(steps)]
+    y = pde_stack_forward(x.cuda(), layers, attention_mask=mask.cuda())
+    ref = x.float()
+    for k in range(steps):
+        ref = O.pde_layer_step(ref, kind, 0.1 - 0.01 * k, 0.05 + 0.01 * k, layout="bld", causal=causal,
+                               attention_mask=mask)
+    ref = ref.to(dtype)
+    if kind == "advection":
+        assert torch.equal(y.cpu(), ref)
+    else:
+        assert_close(y, ref)
+    if dtype == torch.float32:
+        yl = x.cuda()
+        with torch.no_grad():
+            for l in layers:
+                yl = l(yl, attention_mask=mask.cuda())
+        assert torch.equal(y, yl)
+
+
+@pytest.mark.parametrize("pde_type", ["advection-diffusion", "reaction-diffusion"])
+def test_model_inference_fuses_two_coefficient_stacks(pde_type):
+    """The PDE-Transformer classifier in fp32 under no_grad takes the fused
+    stack path and returns exactly what the per-layer path (with autograd) does."""
+    from cta_b200.transformers import PDETransformerClassifier
+
+    torch.manual_seed(41)
+    net = PDETransformerClassifier(vocab_size=100, embed_dim=32, num_heads=4, hidden_dim=64, num_layers=2,
+                                   num_classes=2, pde_type=pde_type, pde_steps=3, max_length=128,
+                                   dropout=0.0).cuda().eval()
+    ids = torch.randint(0, 100, (2, 96), device="cuda")
+    mask = torch.ones(2, 96, dtype=torch.long, device="cuda")
+    mask[1, 80:] = 0
+    with torch.no_grad():
+        fused = net(ids, mask)
+    per_layer = net(ids, mask)  # parameters require grad: the per-layer path
+    assert torch.equal(fused, per_layer.detach())
