@@ -39,6 +39,7 @@ for _p in (str(REPO), str(REPO / "continuous-time-attention_b200")):
 
 import torch  # noqa: E402
 
+REF_DIR = REPO / "baseline" / "_ref"  # the unmodified reference install
 METRIC = "fused diffusion stencil tokens/s & HBM GB/s (% of peak) at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
 
@@ -131,37 +132,56 @@ def _cpu_model() -> str:
     return "unknown"
 
 
-def cpu_oracle_times(L: int, D: int, steps: int, timed: int, warmup: int = 2):
-    """Seconds per call of the CPU oracle (a restatement of the reference's
-    `_diffusion_steps_bld`, src/cta/serving_vllm.py:29-46, in torch fp32) on the
-    FULL bf16 [1, L, D] tensor, all host threads, after `warmup` untimed calls."""
+def _cpu_impl():
+    """The CPU implementation the CPU arm times: the reference's own
+    `_diffusion_steps_bld` (src/cta/serving_vllm.py:29-46) from the unmodified
+    install under baseline/_ref ("reference"), else the oracle's restatement of
+    it in torch fp32 ("port").  Returns (fn(x, steps), kind, description)."""
+    if (REF_DIR / "cta" / "serving_vllm.py").is_file():
+        if str(REF_DIR) not in sys.path:
+            sys.path.append(str(REF_DIR))
+        try:
+            from cta.serving_vllm import _diffusion_steps_bld as ref_fn
+
+            return (lambda x, steps: ref_fn(x, alpha=0.1, steps=steps), "reference",
+                    "the reference's own _diffusion_steps_bld (PyTorch CPU, unmodified, from baseline/_ref)")
+        except Exception:  # noqa: BLE001 - fall back to the port below
+            pass
     from oracle import diffusion_oracle as O
 
+    return (lambda x, steps: O.steps_bld(x, alpha=0.1, steps=steps), "port",
+            "the CPU oracle (the reference's _diffusion_steps_bld restated in torch fp32)")
+
+
+def cpu_oracle_times(L: int, D: int, steps: int, timed: int, warmup: int = 2):
+    """Seconds per call of the CPU implementation (`_cpu_impl`) on the FULL bf16
+    [1, L, D] tensor, all host threads, after `warmup` untimed calls."""
+    fn, _, _ = _cpu_impl()
     torch.set_num_threads(os.cpu_count() or 1)
     torch.manual_seed(0)
     x = torch.randn(1, L, D).to(torch.bfloat16)
     for _ in range(warmup):
-        O.steps_bld(x, alpha=0.1, steps=steps)
+        fn(x, steps)
     times = []
     for _ in range(timed):
         t0 = time.perf_counter()
-        O.steps_bld(x, alpha=0.1, steps=steps)
+        fn(x, steps)
         times.append(time.perf_counter() - t0)
     return times
 
 
 def _cpu_line(L: int, D: int, steps: int, times) -> dict:
+    _, kind, desc = _cpu_impl()
     p50 = statistics.median(times)
     return {
         "value": L / p50,
         "unit": "tokens/s",
         "cores": torch.get_num_threads(),
         "cpu_model": _cpu_model(),
-        "kind": "port",
+        "kind": kind,
         "p50_ms": p50 * 1e3,
-        "sample": f"p50 of {len(times)} calls (after 2 warm-ups) of the CPU oracle (the reference's "
-                  f"_diffusion_steps_bld restated in torch fp32) on the full bf16 [1, {L}, {D}] tensor, "
-                  f"steps {steps}",
+        "sample": f"p50 of {len(times)} calls (after 2 warm-ups) of {desc} on the full bf16 [1, {L}, {D}] "
+                  f"tensor, steps {steps}",
     }
 
 
@@ -171,10 +191,10 @@ def cpu_reference_rate(L: int, D: int, steps: int):
 
 
 def run_reference(args, rank: int) -> None:
-    """The reference arm: the reference's algorithm for the path on the host cores
-    (the oracle port; the reference is a Python source tree without packaging, so
-    it cannot be installed under baseline/_ref and does not travel to the GPU box).
-    One step = one call over the full [1, L, D] input; value = tokens / p50 step."""
+    """The reference arm: the reference's CPU implementation of the path on the
+    host cores -- its own `_diffusion_steps_bld` from baseline/_ref when that
+    install exists, else the oracle port (`_cpu_impl`).  One step = one call over
+    the full [1, L, D] input; value = tokens / p50 step."""
     if rank != 0:
         return
     L, D, S = args.L, args.D, args.stencil_steps
@@ -312,6 +332,97 @@ def _eager_host(dev) -> dict:
             torch.cuda.synchronize()
             t2 = time.perf_counter()
             out[name] = {"host_us": round((t1 - t0) / n * 1e6, 2), "wall_us": round((t2 - t0) / n * 1e6, 2)}
+    return out
+
+
+def reference_gpu_modules():
+    """The reference's own GPU path, unmodified, from baseline/_ref (placed there
+    by baseline/install_reference.py): (kernels.diffusion_triton,
+    cta.serving_vllm) and None, or None and the reason it is unavailable."""
+    if not (REF_DIR / "kernels" / "diffusion_triton.py").is_file():
+        return None, "no reference install under baseline/_ref (python baseline/install_reference.py --ref <root>)"
+    if str(REF_DIR) not in sys.path:
+        sys.path.append(str(REF_DIR))
+    try:
+        import cta.serving_vllm as sv
+        import kernels.diffusion_triton as kt
+    except Exception as e:  # noqa: BLE001 - reported, not raised
+        return None, f"reference import failed: {type(e).__name__}: {e}"
+    if getattr(kt, "triton", None) is None:
+        return None, "triton is not importable"
+    return (kt, sv), None
+
+
+def _time_eager(fn, n: int, warmup: int, stream) -> float:
+    """Seconds per eager call (host work included), CUDA events on `stream`."""
+    for i in range(warmup):
+        fn(i)
+    return _time_launches(fn, n, stream) / n
+
+
+def _reference_gpu(dev, full: bool) -> dict:
+    """The reference's GPU path timed beside ours on this GPU, both called
+    eagerly through their public APIs on the same inputs (rotating buffers
+    larger than L2), with a bit-for-bit comparison of the outputs:
+
+      * the vLLM post-attention mixer on bf16 [1, 65536, 512], steps 4: the
+        reference transposes to [B, D, L], runs its fused Triton s4 kernel and
+        transposes back (src/cta/serving_vllm.py:195-266); ours is one
+        [B, L, D] launch;
+      * the kernel API diffusion_triton_fused on bf16 [1, 512, 65536]
+        (kernels/diffusion_triton.py:829-868, 891-910), steps 4 (2, 4, 8 with
+        `full`);
+      * with `full`, the packed prefill of 64 sequences U[512, 8192] x 4096
+        bf16 (src/cta/serving_vllm.py:72-111, 275-303) under the reference rule.
+    """
+    mods, why = reference_gpu_modules()
+    if mods is None:
+        return {"unavailable": why}
+    kt, sv = mods
+    from cta_b200 import diffusion as our_kernels
+    from cta_b200 import serving_vllm as our_sv
+
+    stream = torch.cuda.current_stream(dev)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    out = {"source": "baseline/_ref (the reference tree, unmodified; its Triton kernels JIT-compiled here)",
+           "timing": "eager calls through each public API, CUDA events, rotating inputs > L2", "rows": []}
+
+    def row(name, ref_fn, our_fn, tokens, calls=20):
+        eq = bool(torch.equal(ref_fn(0), our_fn(0)))
+        t_ref = _time_eager(ref_fn, calls, 3, stream)
+        t_our = _time_eager(our_fn, calls, 3, stream)
+        out["rows"].append({"workload": name, "reference_us": round(t_ref * 1e6, 1), "ours_us": round(t_our * 1e6, 1),
+                            "speedup": round(t_ref / t_our, 2), "reference_tokens/s": round(tokens / t_ref),
+                            "ours_tokens/s": round(tokens / t_our), "bit_identical": eq})
+
+    L, D, S = 65536, 512, 4
+    nb = max(2, (4 * l2) // (L * D * 2) + 1)
+    gen = torch.Generator(device=dev).manual_seed(77)
+    xs = [torch.randn(1, L, D, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(nb)]
+    ref_mixer = sv.CtaPostAttnMixer(sv.CtaConfig(steps=S, alpha=0.1, trace=False))
+    our_mixer = our_sv.CtaPostAttnMixer(our_sv.CtaConfig(steps=S, alpha=0.1, trace=False))
+    row(f"mixer bf16 [1, {L}, {D}] steps {S}", lambda i: ref_mixer(xs[i % nb], is_prefill=True),
+        lambda i: our_mixer(xs[i % nb], is_prefill=True), L)
+    xt = [x.view(1, D, L) for x in xs]  # the same bytes read as [B, D, L]
+    for s in ((2, 4, 8) if full else (4,)):
+        row(f"diffusion_triton_fused bf16 [1, {D}, {L}] steps {s}",
+            lambda i, s=s: kt.diffusion_triton_fused(xt[i % nb], alpha=0.1, steps=s),
+            lambda i, s=s: our_kernels.diffusion_triton_fused(xt[i % nb], alpha=0.1, steps=s), L)
+    del xs, xt
+    if full:
+        g = torch.Generator().manual_seed(0)
+        lens = torch.randint(512, 8193, (64,), generator=g)
+        qsl = torch.zeros(65, dtype=torch.int32)
+        qsl[1:] = torch.cumsum(lens, 0)
+        T, Dv = int(qsl[-1]), 4096
+        xv = [torch.randn(T, Dv, device=dev, dtype=torch.bfloat16, generator=gen) for _ in range(2)]
+        from types import SimpleNamespace
+        md = SimpleNamespace(query_start_loc=qsl.to(dev), max_query_len=int(lens.max()))
+        row(f"packed prefill 64 seqs U[512, 8192] x {Dv} bf16 steps {S} (reference rule)",
+            lambda i: ref_mixer(xv[i % 2], attn_metadata=md, is_prefill=True),
+            lambda i: our_mixer(xv[i % 2], attn_metadata=md, is_prefill=True), T, calls=5)
+        del xv
+    torch.cuda.empty_cache()
     return out
 
 
@@ -568,6 +679,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         torch.cuda.empty_cache()
 
     eager = _eager_host(dev) if (rank == 0 and not args.no_sweep) else None
+    ref_gpu = _reference_gpu(dev, full=False) if (world == 1 and not args.no_reference_gpu) else None
     sharded = None if args.no_sharded else _sharded_parts(args, rank, world, dev)
 
     cpu = None
@@ -603,6 +715,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         }
         if eager is not None:
             line["eager_host_us"] = eager
+        if ref_gpu is not None:
+            line["reference_gpu"] = ref_gpu
         if sharded is not None:
             line["sharded"] = sharded
         if sweep is not None:
@@ -871,6 +985,17 @@ def run_kernels(args, rank, world, local_rank):
                  "CUDA events over CUDA-graph replays, inputs rotating over >= 4x L2", "rows": rows})
 
 
+def run_reference_gpu(args, rank, world, local_rank):
+    """The reference's GPU path (its Triton kernels and mixer, unmodified) and
+    ours on the same inputs: the full table of `_reference_gpu`, on rank 0."""
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    res = _reference_gpu(dev, full=True)
+    _emit(rank, {"workload": "reference_gpu", "n_gpus": 1, **res})
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -883,10 +1008,14 @@ def main() -> None:
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sharded", action="store_true", help="skip the L-sharded C5 object of the default line")
-    ap.add_argument("--workload", choices=["fused_fwd", "varlen", "block", "sharded", "kernels"], default="fused_fwd",
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip the reference's Triton GPU path timed beside ours (default line, N=1)")
+    ap.add_argument("--workload", choices=["fused_fwd", "varlen", "block", "sharded", "kernels", "reference_gpu"],
+                    default="fused_fwd",
                     help="fused_fwd: headline single-GPU forward; varlen: 64-sequence packed mixer, D=4096; "
                          "block: PDE-Transformer LM fwd+bwd; sharded: L=1M x 4096 split over the ranks; "
-                         "kernels: per-kernel timing table")
+                         "kernels: per-kernel timing table; reference_gpu: the reference's Triton path "
+                         "timed beside ours (rank 0)")
     ap.add_argument("--kernel", default="bld_forward",
                     choices=["bld_forward", "bld_adjoint", "bld_adjoint_dalpha", "bdl_forward", "bdl_adjoint",
                              "bld_forward_pool"],
@@ -913,7 +1042,7 @@ def main() -> None:
                                 device_id=torch.device("cuda", local_rank))
     try:
         {"fused_fwd": run_ours, "varlen": run_varlen, "block": run_block, "sharded": run_sharded,
-         "kernels": run_kernels}[args.workload](
+         "kernels": run_kernels, "reference_gpu": run_reference_gpu}[args.workload](
             args, rank, world, local_rank)
     finally:
         if world > 1:

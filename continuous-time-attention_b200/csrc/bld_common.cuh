@@ -84,6 +84,17 @@ struct RowBits {
     const uint64_t v = static_cast<uint64_t>(fbits[w]) | (static_cast<uint64_t>(fbits[w + 1]) << 32);
     return static_cast<uint32_t>(v >> sh) & 0xffffu;
   }
+  // Rows row_lo .. row_lo+n-1 (n <= 32): 0 if none is fixed or zero, 2 if all
+  // are fixed and none is zero, 1 otherwise.
+  __device__ __forceinline__ int chunk_class(int64_t row_lo, int n) const {
+    const int64_t p = row_lo - jbits + 32;
+    const int w = static_cast<int>(p >> 5), sh = static_cast<int>(p & 31);
+    const uint32_t m = n >= 32 ? 0xffffffffu : (1u << n) - 1u;
+    const uint64_t f = static_cast<uint64_t>(fbits[w]) | (static_cast<uint64_t>(fbits[w + 1]) << 32);
+    const uint64_t z = static_cast<uint64_t>(zbits[w]) | (static_cast<uint64_t>(zbits[w + 1]) << 32);
+    const uint32_t fw = static_cast<uint32_t>(f >> sh) & m, zw = static_cast<uint32_t>(z >> sh) & m;
+    return (fw | zw) == 0u ? 0 : (fw == m && zw == 0u) ? 2 : 1;
+  }
   __device__ __forceinline__ bool fixed(int64_t row) const {
     const int64_t p = row - jbits + 32;
     return (fbits[p >> 5] >> (p & 31)) & 1u;

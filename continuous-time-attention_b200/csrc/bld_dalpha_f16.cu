@@ -1,0 +1,13 @@
+// Backward-with-d(alpha) kernels of bld_dalpha_kernel.cuh: fp16 tensors, exact arithmetic, with the PDE kinds.
+// One translation unit per (dtype, arithmetic) so that they compile in parallel.
+#include "bld_dalpha_kernel.cuh"
+
+namespace cta {
+
+const void* bld_dalpha_kernel_f16(int steps, int causal, int kind) {
+  return da_select<__half, false>(steps, causal, kind);
+}
+
+int read_device_error_bld_dalpha_f16(int clear) { return read_da_error_word(clear); }
+
+}  // namespace cta

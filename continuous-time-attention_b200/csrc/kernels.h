@@ -50,11 +50,13 @@ constexpr int64_t kWsHeaderBytes = 8192;
 constexpr int kWsMaxGroups = static_cast<int>(kWsHeaderBytes / 4) - 1;
 constexpr int kDaMaxSteps = 8;  // steps handled by the march d(alpha) kernel
 constexpr int kPdeMaxSteps = 4;  // advection / reaction layers fused per forward launch
+// march d(alpha) kernel: full chunks whose pairings all lie inside the tile
+// skip the per-row range test (1) or keep it (0)
+#ifndef CTA_DA_INNER
+#define CTA_DA_INNER 1
+#endif
 // march d(alpha) kernel: packed column pairs per lane (1: 64-column tiles, half
 // the per-lane state of two pairs, twice the resident warps)
-#ifndef CTA_DA_SWP
-#define CTA_DA_SWP 0
-#endif
 #ifndef CTA_DA_PAIRS
 #define CTA_DA_PAIRS 1
 #endif

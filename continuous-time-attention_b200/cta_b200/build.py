@@ -26,7 +26,13 @@ BUILD_DIR = SRC_ROOT / "_build"
 LIB_NAME = "libcta_stencil.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["capi.cu", "bld_fwd.cu", "bld_dalpha.cu", "stencil_bdl.cu", "noalloc.cu"]
+# the kernel units (one per dtype and arithmetic, so that they compile in
+# parallel) first, then the host-side units
+SOURCES = [
+    "bld_fwd_bf16_fm.cu", "bld_fwd_f16_fm.cu", "bld_fwd_bf16.cu", "bld_fwd_f16.cu", "bld_fwd_f32.cu",
+    "bld_dalpha_bf16_fm.cu", "bld_dalpha_f16_fm.cu", "bld_dalpha_bf16.cu", "bld_dalpha_f16.cu",
+    "bld_dalpha_f32.cu", "stencil_bdl.cu", "capi.cu", "bld_fwd.cu", "bld_dalpha.cu", "noalloc.cu",
+]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = [
     "-O3",

@@ -312,8 +312,8 @@ def pde_stack_forward(
 ) -> torch.Tensor:
     """Inference forward of consecutive advection- or reaction-diffusion layers
     (one kind, one causality): one launch per 4 layers instead of one per layer,
-    fp32 kept between the layers of a launch (identical to the layer chain in
-    fp32, within one rounding per layer in 16-bit dtypes).  ``layout`` is x's
+    fp32 kept between all layers (identical to the layer chain in fp32 rounded
+    once; within one rounding per layer of the 16-bit layer chain).  ``layout`` is x's
     layout (default: the layers'); the kernel runs on [B, L, D].  No autograd
     graph is recorded: training takes the per-layer path, whose backward needs
     every layer's input."""
@@ -337,11 +337,19 @@ def pde_stack_forward(
         if mask.dtype == torch.bool:
             mask = mask.to(torch.uint8)
     y = x.transpose(1, 2) if layout == "bdl" else x
+    n = _lib.PDE_STACK_MAX_STEPS
+    # more layers than one launch holds: 16-bit input runs the launches in fp32
+    # and is rounded once at the end, so fp32 is kept between every two layers
+    widen = len(layers) > n and y.dtype != torch.float32
     with torch.no_grad():
-        for i in range(0, len(layers), _lib.PDE_STACK_MAX_STEPS):
-            chunk = layers[i : i + _lib.PDE_STACK_MAX_STEPS]
+        if widen:
+            y = y.float()
+        for i in range(0, len(layers), n):
+            chunk = layers[i : i + n]
             y = ops.pde_stack(y.contiguous(), kind, [l.alpha for l in chunk], [l.beta for l in chunk], causal=causal,
                               mask=mask)
+        if widen:
+            y = y.to(x.dtype)
     return y.transpose(1, 2).contiguous() if layout == "bdl" else y
 
 
