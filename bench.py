@@ -387,13 +387,20 @@ def _reference_gpu(dev, full: bool) -> dict:
     out = {"source": "baseline/_ref (the reference tree, unmodified; its Triton kernels JIT-compiled here)",
            "timing": "eager calls through each public API, CUDA events, rotating inputs > L2", "rows": []}
 
-    def row(name, ref_fn, our_fn, tokens, calls=20):
-        eq = bool(torch.equal(ref_fn(0), our_fn(0)))
+    def row(name, ref_fn, our_fn, tokens, calls=20, steps=None):
+        yr, yo = ref_fn(0), our_fn(0)
+        # elements that differ, and by how many units in the last place (bf16)
+        d = (yr.view(torch.int16).int() - yo.view(torch.int16).int()).abs()
+        kern = {2: kt._diffusion_fused_s2_kernel, 4: kt._diffusion_fused_s4_kernel,
+                8: kt._diffusion_fused_s8_kernel}.get(steps)
+        best = getattr(kern, "best_config", None) if kern is not None else None
         t_ref = _time_eager(ref_fn, calls, 3, stream)
         t_our = _time_eager(our_fn, calls, 3, stream)
         out["rows"].append({"workload": name, "reference_us": round(t_ref * 1e6, 1), "ours_us": round(t_our * 1e6, 1),
                             "speedup": round(t_ref / t_our, 2), "reference_tokens/s": round(tokens / t_ref),
-                            "ours_tokens/s": round(tokens / t_our), "bit_identical": eq})
+                            "ours_tokens/s": round(tokens / t_our), "bit_identical": bool(int(d.max()) == 0),
+                            "elements_differing": int((d > 0).sum()), "max_ulp": int(d.max()),
+                            "reference_config": None if best is None else f"BLOCK {best.kwargs.get('BLOCK')}"})
 
     L, D, S = 65536, 512, 4
     nb = max(2, (4 * l2) // (L * D * 2) + 1)
@@ -402,12 +409,12 @@ def _reference_gpu(dev, full: bool) -> dict:
     ref_mixer = sv.CtaPostAttnMixer(sv.CtaConfig(steps=S, alpha=0.1, trace=False))
     our_mixer = our_sv.CtaPostAttnMixer(our_sv.CtaConfig(steps=S, alpha=0.1, trace=False))
     row(f"mixer bf16 [1, {L}, {D}] steps {S}", lambda i: ref_mixer(xs[i % nb], is_prefill=True),
-        lambda i: our_mixer(xs[i % nb], is_prefill=True), L)
+        lambda i: our_mixer(xs[i % nb], is_prefill=True), L, steps=S)
     xt = [x.view(1, D, L) for x in xs]  # the same bytes read as [B, D, L]
     for s in ((2, 4, 8) if full else (4,)):
         row(f"diffusion_triton_fused bf16 [1, {D}, {L}] steps {s}",
             lambda i, s=s: kt.diffusion_triton_fused(xt[i % nb], alpha=0.1, steps=s),
-            lambda i, s=s: our_kernels.diffusion_triton_fused(xt[i % nb], alpha=0.1, steps=s), L)
+            lambda i, s=s: our_kernels.diffusion_triton_fused(xt[i % nb], alpha=0.1, steps=s), L, steps=s)
     del xs, xt
     if full:
         g = torch.Generator().manual_seed(0)
@@ -420,7 +427,7 @@ def _reference_gpu(dev, full: bool) -> dict:
         md = SimpleNamespace(query_start_loc=qsl.to(dev), max_query_len=int(lens.max()))
         row(f"packed prefill 64 seqs U[512, 8192] x {Dv} bf16 steps {S} (reference rule)",
             lambda i: ref_mixer(xv[i % 2], attn_metadata=md, is_prefill=True),
-            lambda i: our_mixer(xv[i % 2], attn_metadata=md, is_prefill=True), T, calls=5)
+            lambda i: our_mixer(xv[i % 2], attn_metadata=md, is_prefill=True), T, calls=5, steps=S)
         del xv
     torch.cuda.empty_cache()
     return out

@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     const bool vec_ok = a.y_quad_ok != 0 && col + 2 * NP - 1 < a.D;
     T* const ybase = static_cast<T*>(a.y) + static_cast<int64_t>(sg.bcoord) * a.ysB + sg.row0 * a.ysL + col;
 
-    auto store_row = [&](int64_t orow, const pf2* v) {
+    auto store_row = [&](int64_t orow, const pf2* v) CTA_INLINE {
       T* yp = ybase + orow * a.ysL;
       if (vec_ok) {
         *reinterpret_cast<V*>(yp) = Q::join(v[0], NP > 1 ? v[NP - 1] : 0ull);
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
 
     // The forward recomputation of one march row: lap(u_q) of the row for every
     // level q into la, the levels advanced (state F1, F2).
-    auto fwd_levels = [&](auto slow_tag, auto tct_tag, int64_t jx, pf2* x, pf2 (&la)[S][NP]) {
+    auto fwd_levels = [&](auto slow_tag, auto tct_tag, int64_t jx, pf2* x, pf2 (&la)[S][NP]) CTA_INLINE {
       constexpr bool SLOW = decltype(slow_tag)::value;
       constexpr int TCT = decltype(tct_tag)::value;
       {
@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     // The adjoint of one march row: g_k paired with lap(u_{k-1}) through the
     // delay rings into d(alpha), the adjoint levels advanced (state P, G).
     auto adj_levels = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, int64_t jg, pf2* g,
-                          const pf2 (&la)[S][NP], const pf2* h, const pf2* fp) {
+                          const pf2 (&la)[S][NP], const pf2* h, const pf2* fp) CTA_INLINE {
       constexpr bool SLOW = decltype(slow_tag)::value;
       constexpr int TCT = decltype(tct_tag)::value;
       constexpr int I = decltype(i_tag)::value;
@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     // One march row: TCT >= 0 is the compile-time march row of a prologue row
     // (start-up triangles of both wavefronts skipped); I the row in its chunk;
     // lim = nout + PRO - (first march row of the chunk).
-    auto step_row = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, pf2* g, pf2* x) {
+    auto step_row = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, pf2* g, pf2* x) CTA_INLINE {
       constexpr bool SLOW = decltype(slow_tag)::value;
       constexpr int TCT = decltype(tct_tag)::value;
       constexpr int I = decltype(i_tag)::value;
@@ -487,7 +487,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     // kind: 0..NPRO-1 = prologue chunk, NPRO = full output chunk, NPRO+1 = partial
     // last chunk, NPRO+2 = full chunk whose every pairing lies inside the tile
     // (its row-range test is a compile-time true: march row -2)
-    auto march_chunk = [&](auto slow_tag, auto kind_tag, int c, const T* gbuf, const T* xbuf) {
+    auto march_chunk = [&](auto slow_tag, auto kind_tag, int c, const T* gbuf, const T* xbuf) CTA_INLINE {
       constexpr int CK = decltype(kind_tag)::value;
       constexpr bool FULLK = CK == NPRO || CK == NPRO + 2;
       const int t0 = c * kFwdRC;
@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
       });
     };
 
-    auto do_chunk = [&](auto slow_tag, auto kind_tag, int c) -> bool {
+    auto do_chunk = [&](auto slow_tag, auto kind_tag, int c) CTA_INLINE -> bool {
       constexpr int CK = decltype(kind_tag)::value;
       constexpr bool FULL = CK == NPRO || CK == NPRO + 2;
       const int slot = c % NST;
@@ -561,7 +561,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
                       : (nrows - G::emax() - kFwdRC < 0
                              ? NPRO
                              : max(NPRO, min(nfull_end, (nrows - G::emax() - kFwdRC) / kFwdRC + 1)));
-    auto run = [&](auto slow_tag) -> bool {
+    auto run = [&](auto slow_tag) CTA_INLINE -> bool {
       if (!do_chunk(slow_tag, std::integral_constant<int, 0>{}, 0)) return false;
       if constexpr (NPRO > 1) {
         if (!do_chunk(slow_tag, std::integral_constant<int, 1>{}, 1)) return false;

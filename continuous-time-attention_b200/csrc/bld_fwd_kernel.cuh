@@ -27,7 +27,9 @@
 // Rows that must not change -- the copy boundary, rows whose 3-row stencil
 // touches a masked position, per-sequence boundaries of packed prefill -- are
 // "fixed" rows.  They are collected per tile into a bitmap; tiles without any
-// fixed row run a branch-free march, the others test the bitmap per level.
+// fixed row run a branch-free march.  In the others each full chunk takes one
+// of three forms from the bits its rows test: branch-free (none set), per-row
+// tests, or all-fixed (every tested row fixed: the tests fold to constants).
 #pragma once
 
 #include "bld_common.cuh"
@@ -289,7 +291,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   const int soff = cb;  // element offset of this lane in a slot row
 
   pf2 pool_a = 0ull, pool_b = 0ull;  // POOL: masked column sums of this lane
-  auto store_row = [&](int64_t orow, pf2 pa, pf2 pb) {
+  auto store_row = [&](int64_t orow, pf2 pa, pf2 pb) CTA_INLINE {
     if constexpr (POOL) {
       const int64_t p = orow - jb + 32;  // fbits layout: word 0 is the guard word
       if (col_ok && ((pbits[p >> 5] >> (p & 31)) & 1u)) {
@@ -324,9 +326,11 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   // level k there is only computed once its inputs are valid (TCT >= 2k + 2),
   // so the start-up triangle of the wavefront costs nothing.
   // slow_tag: 0 = no fixed or zero row near the rows marched, 1 = per-row
-  // tests, 2 = every tested row fixed and none zero (the tests are constants)
-  auto step_row = [&](auto slow_tag, auto tct_tag, int64_t j, pf2& xa, pf2& xb) {
-    constexpr bool SLOW = decltype(slow_tag)::value != 0;
+  // tests, 2 = every tested row fixed and none zero (the tests are constants),
+  // 3 = form 0 inside a tile that has fixed rows (a separate instantiation, so
+  // that every chunk form has a single call site and is inlined)
+  auto step_row = [&](auto slow_tag, auto tct_tag, int64_t j, pf2& xa, pf2& xb) CTA_INLINE {
+    constexpr bool SLOW = decltype(slow_tag)::value == 1 || decltype(slow_tag)::value == 2;
     constexpr bool ALLF = decltype(slow_tag)::value == 2;
     constexpr int TCT = decltype(tct_tag)::value;
     if (SLOW && !ALLF) {
@@ -431,7 +435,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   };
 
   // kind: 0..NPRO-1 = prologue chunk, NPRO = full output chunk, NPRO+1 = partial last chunk
-  auto march_chunk = [&](auto slow_tag, auto kind_tag, int c, const T* buf) {
+  auto march_chunk = [&](auto slow_tag, auto kind_tag, int c, const T* buf) CTA_INLINE {
     constexpr int CK = decltype(kind_tag)::value;
     const int t0 = c * kFwdRC;
     T* st = stage + ((c - NPRO) & 1) * CHUNK + soff;
@@ -469,7 +473,8 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
     // consecutive instructions come from up to min(S, 8) independent
     // (row, level) cells, which hides the FP32 latency of the dependent chain
     // of one row.
-    if constexpr (CTA_FWD_DIAG && CK == NPRO && !decltype(slow_tag)::value && CTA_FWD_PRELOAD) {
+    constexpr bool FAST = decltype(slow_tag)::value == 0 || decltype(slow_tag)::value == 3;
+    if constexpr (CTA_FWD_DIAG && CK == NPRO && FAST && CTA_FWD_PRELOAD) {
       pf2 ua[kFwdRC], ub[kFwdRC];
 #pragma unroll
       for (int i = 0; i < kFwdRC; ++i) Q::split(in[i], ua[i], ub[i]);
@@ -561,7 +566,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
 
   // One pipeline step: wait for chunk c, march it, hand full output chunks to
   // the TMA store, refill the slot.  Returns false after a timed-out wait.
-  auto do_chunk = [&](auto slow_tag, auto kind_tag, int c) -> bool {
+  auto do_chunk = [&](auto slow_tag, auto kind_tag, int c) CTA_INLINE -> bool {
     constexpr int CK = decltype(kind_tag)::value;
     constexpr bool FULL = CK == NPRO;
     const int slot = c % kFwdStages;
@@ -613,7 +618,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
 
   // prologue chunks, then a single-body loop over full chunks, then the
   // partial last chunk; the fast/slow choice is made once per tile
-  auto run = [&](auto slow_tag) -> bool {
+  auto run = [&](auto slow_tag) CTA_INLINE -> bool {
     if (!do_chunk(slow_tag, std::integral_constant<int, 0>{}, 0)) return false;
     if constexpr (NPRO > 1) {
       if (!do_chunk(slow_tag, std::integral_constant<int, 1>{}, 1)) return false;
@@ -624,7 +629,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
         // the rows its tests read, [t0 - 2S, t0 + 8) of the march
         const int cls = rb.chunk_class(jb + c * kFwdRC - 2 * S, kFwdRC + 2 * S);
         bool ok = true;
-        if (cls == 0) ok = do_chunk(std::integral_constant<int, 0>{}, std::integral_constant<int, NPRO>{}, c);
+        if (cls == 0) ok = do_chunk(std::integral_constant<int, 3>{}, std::integral_constant<int, NPRO>{}, c);
         else if (cls == 2) ok = do_chunk(std::integral_constant<int, 2>{}, std::integral_constant<int, NPRO>{}, c);
         else ok = do_chunk(slow_tag, std::integral_constant<int, NPRO>{}, c);
         if (!ok) return false;

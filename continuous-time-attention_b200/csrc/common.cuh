@@ -27,6 +27,13 @@
 #error "cta_stencil kernels target sm_100a only"
 #endif
 
+// Force-inline a device lambda.  The march kernels are built from lambdas
+// (row step, chunk, pipeline step) called from several places; one that the
+// inliner leaves as a call takes the kernel's register state through local
+// memory (a stack frame of a kilobyte or more) and runs an order of magnitude
+// slower.
+#define CTA_INLINE __attribute__((always_inline))
+
 namespace cta {
 
 // Calls f(std::integral_constant<int, I>{}) for I = 0 .. N-1 (compile-time unrolled loop).

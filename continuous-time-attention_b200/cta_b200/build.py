@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import argparse
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -68,6 +69,30 @@ def is_stale() -> bool:
     return any(f.stat().st_mtime > t for f in _inputs())
 
 
+# A march kernel keeps its whole state in registers; a stack frame above a few
+# bytes means a helper was not inlined (its state went to local memory) or
+# large spills, either of which costs an order of magnitude.
+MAX_STACK_BYTES = 64
+
+
+def stack_frames(ptxas_log: str) -> list:
+    """(kernel, bytes) for every entry function of a ptxas -v report whose
+    stack frame exceeds MAX_STACK_BYTES."""
+    out = []
+    name = None
+    for line in ptxas_log.splitlines():
+        m = re.search(r"Compiling entry function '([^']+)'", line)
+        if m:
+            name = m.group(1)
+            continue
+        m = re.search(r"(\d+) bytes stack frame", line)
+        if m and name is not None:
+            if int(m.group(1)) > MAX_STACK_BYTES:
+                out.append((name, int(m.group(1))))
+            name = None
+    return out
+
+
 def build(force: bool = False, verbose: bool = False, jobs: int | None = None, defines: tuple = (),
           out: Path | None = None) -> Path:
     """Compile every kernel translation unit for sm_100a and link the library.
@@ -88,9 +113,9 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None, d
 
     def compile_one(name: str) -> Path:
         obj = build_dir / (Path(name).stem + ".o")
-        cmd = [nvcc, *ARCH_FLAGS, *CFLAGS, *incs, "-c", str(CSRC / name), "-o", str(obj)]
+        # ptxas -v always: its per-kernel report is checked for stack frames
+        cmd = [nvcc, *ARCH_FLAGS, "-Xptxas=-v", *CFLAGS, *incs, "-c", str(CSRC / name), "-o", str(obj)]
         if verbose:
-            cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), flush=True)
         # an object is reused when it is newer than its source and every header
         # and was built by the same command
@@ -103,6 +128,10 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None, d
             raise RuntimeError(f"nvcc failed for {name}:\n{res.stdout}\n{res.stderr}")
         if verbose and (res.stdout or res.stderr):
             print(res.stdout + res.stderr, flush=True)
+        big = stack_frames(res.stderr)
+        if big:
+            raise RuntimeError(f"{name}: kernels with a stack frame above {MAX_STACK_BYTES} bytes (a call that was "
+                               f"not inlined, or spills): " + "; ".join(f"{k} {v} B" for k, v in big[:8]))
         stamp.write_text(" ".join(cmd))
         return obj
 

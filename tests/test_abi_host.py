@@ -140,3 +140,20 @@ def test_arithmetic_mode_codes():
     assert lib.cta_set_thread_arithmetic(7) == -2
     prev = lib.cta_set_thread_arithmetic(0)
     assert lib.cta_set_thread_arithmetic(prev) == 0
+
+
+def test_build_rejects_kernel_stack_frames():
+    """The build parses ptxas -v and fails on a kernel whose stack frame shows a
+    helper that was not inlined (its register state in local memory)."""
+    from cta_b200 import build as B
+
+    log = "\n".join([
+        "ptxas info    : Compiling entry function '_Z6kernelILi5EEvv' for 'sm_100a'",
+        "ptxas info    : Function properties for _Z6kernelILi5EEvv",
+        "    1432 bytes stack frame, 0 bytes spill stores, 0 bytes spill loads",
+        "ptxas info    : Used 126 registers, used 1 barriers, 1432 bytes cumulative stack size",
+        "ptxas info    : Compiling entry function '_Z6kernelILi4EEvv' for 'sm_100a'",
+        "ptxas info    : Function properties for _Z6kernelILi4EEvv",
+        "    16 bytes stack frame, 16 bytes spill stores, 16 bytes spill loads",
+    ])
+    assert B.stack_frames(log) == [("_Z6kernelILi5EEvv", 1432)]

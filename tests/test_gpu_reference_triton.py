@@ -5,8 +5,11 @@ mixer (src/cta/serving_vllm.py) are imported unmodified from baseline/_ref
 (placed there by baseline/install_reference.py) and JIT-compiled by Triton.
 The default arithmetic for 16-bit tensors (the contracted update
 c + alpha*lap as one fma, lap = (r - 2c) + l with the first two as one fma) is
-meant to be the op order those kernels compile to, so bf16 / fp16 outputs must
-be bit-identical to theirs:
+the op order those kernels compile to, so bf16 / fp16 outputs are
+bit-identical to theirs -- exactly so for the BLOCK 64 and 128 builds of the
+fused kernels; the BLOCK 256 build rounds a few elements in 10^5 differently
+at steps 4 and 8, by one unit in the last place (test_fused_against_each_
+triton_config), so where the autotuner picked it the bar is that:
 
   * diffusion_triton_fused, steps 2 / 4 / 8 (:829-868 and the s2/s4/s8 kernels);
   * diffusion_step_triton and the per-step-rounding loop diffusion_triton
@@ -53,6 +56,24 @@ def _ours():
     return diffusion, serving_vllm
 
 
+def _fused_kernel(ref, steps):
+    return {2: ref.kt._diffusion_fused_s2_kernel, 4: ref.kt._diffusion_fused_s4_kernel,
+            8: ref.kt._diffusion_fused_s8_kernel}.get(steps)
+
+
+def _assert_matches(got, want, ref, steps):
+    """Bit for bit, unless the autotuner ran the BLOCK 256 build of the fused
+    kernel: then within one unit in the last place on at most 1e-4 of the
+    elements."""
+    kern = _fused_kernel(ref, steps)
+    best = getattr(kern, "best_config", None) if kern is not None else None
+    if best is None or best.kwargs.get("BLOCK") != 256:
+        assert torch.equal(got, want), (got.float() - want.float()).abs().max().item()
+        return
+    diff = (got.view(torch.int16).int() - want.view(torch.int16).int()).abs()
+    assert int(diff.max()) <= 1 and int((diff > 0).sum()) <= max(1, 1e-4 * got.numel())
+
+
 SHAPES = [(2, 48, 1000), (1, 64, 4099), (3, 8, 5)]
 
 
@@ -66,7 +87,7 @@ def test_fused_bit_identical_to_triton(ref, shape, steps, dtype):
     for alpha in (0.1, 0.23):
         want = ref.kt.diffusion_triton_fused(x, alpha=alpha, steps=steps)
         got = ours.diffusion_triton_fused(x, alpha=alpha, steps=steps)
-        assert torch.equal(got, want), (alpha, (got.float() - want.float()).abs().max().item())
+        _assert_matches(got, want, ref, steps)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -110,14 +131,44 @@ def test_mixer_bit_identical_to_reference_mixer(ref, dtype):
     ref_m = ref.sv.CtaPostAttnMixer(ref.sv.CtaConfig(steps=4, alpha=0.1, trace=False))
     our_m = ours_sv.CtaPostAttnMixer(ours_sv.CtaConfig(steps=4, alpha=0.1, trace=False))
     x = torch.randn(2, 777, 96, device="cuda").to(dtype)
-    assert torch.equal(our_m(x, is_prefill=True), ref_m(x, is_prefill=True))
+    _assert_matches(our_m(x, is_prefill=True), ref_m(x, is_prefill=True), ref, 4)
     lens = [700, 1, 1, 300, 2, 41]
     qsl = torch.zeros(len(lens) + 1, dtype=torch.int32)
     qsl[1:] = torch.cumsum(torch.tensor(lens), 0)
     md = SimpleNamespace(query_start_loc=qsl.cuda(), max_query_len=max(lens))
     xp = torch.randn(int(qsl[-1]), 96, device="cuda").to(dtype)
-    assert torch.equal(our_m(xp, attn_metadata=md, is_prefill=True), ref_m(xp, attn_metadata=md, is_prefill=True))
+    _assert_matches(our_m(xp, attn_metadata=md, is_prefill=True), ref_m(xp, attn_metadata=md, is_prefill=True),
+                    ref, 4)
     for steps in (2, 8):
         ref_s = ref.sv.CtaPostAttnMixer(ref.sv.CtaConfig(steps=steps, alpha=0.1, trace=False))
         our_s = ours_sv.CtaPostAttnMixer(ours_sv.CtaConfig(steps=steps, alpha=0.1, trace=False))
-        assert torch.equal(our_s(x, is_prefill=True), ref_s(x, is_prefill=True)), steps
+        _assert_matches(our_s(x, is_prefill=True), ref_s(x, is_prefill=True), ref, steps)
+
+
+@pytest.mark.parametrize("steps", [2, 4, 8])
+def test_fused_against_each_triton_config(ref, steps):
+    """The reference's fused kernel under each of its own autotune configs
+    (kernels/diffusion_triton.py:50-55), launched directly: the BLOCK 64 and
+    128 builds are bit-identical to the contracted arithmetic; the BLOCK 256
+    build (which the autotuner picks at large L) rounds a handful of elements
+    differently at steps 4 and 8 (4 and 180 of 33.5 M at bf16 [1, 512, 65536]),
+    so the reference's own result depends on its config.  Those elements are
+    within one bf16 unit in the last place."""
+    import triton
+
+    ours, _ = _ours()
+    kern = _fused_kernel(ref, steps)
+    torch.manual_seed(100 + steps)
+    L = 65536
+    x = torch.randn(1, 64, L, device="cuda").to(torch.bfloat16)
+    want_ours = ours.diffusion_triton_fused(x, alpha=0.1, steps=steps)
+    for cfg in ref.kt._DIFFUSION_FUSED_CONFIGS:
+        block = cfg.kwargs["BLOCK"]
+        y = torch.empty_like(x)
+        kern.fn[(x.shape[0] * x.shape[1], triton.cdiv(L, block))](
+            x.view(-1), y.view(-1), 0.1, L, BLOCK=block, num_warps=cfg.num_warps, num_stages=cfg.num_stages)
+        if block in (64, 128):
+            assert torch.equal(y, want_ours), block
+        else:
+            diff = (y.view(torch.int16).int() - want_ours.view(torch.int16).int()).abs()
+            assert int(diff.max()) <= 1 and int((diff > 0).sum()) <= 1e-4 * x.numel(), block
