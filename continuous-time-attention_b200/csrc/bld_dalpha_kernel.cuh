@@ -316,11 +316,12 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     // The forward recomputation of one march row: lap(u_q) of the row for every
     // level q into la, the levels advanced (state F1, F2).
     auto fwd_levels = [&](auto slow_tag, auto tct_tag, int64_t jx, pf2* x, pf2 (&la)[S][NP]) CTA_INLINE {
-      constexpr bool SLOW = decltype(slow_tag)::value;
+      constexpr bool SLOW = decltype(slow_tag)::value == 1 || decltype(slow_tag)::value == 2;
+      constexpr bool ALLF = decltype(slow_tag)::value == 2;
       constexpr int TCT = decltype(tct_tag)::value;
       {
-        const bool fxc = SLOW && CAUSAL && rb.fixed(jx);
-        const uint32_t fwx = (SLOW && !CAUSAL) ? rb.window8_fixed(jx - S) : 0u;
+        const bool fxc = SLOW && CAUSAL && (ALLF || rb.fixed(jx));
+        const uint32_t fwx = (SLOW && !CAUSAL) ? (ALLF ? 0xffu : rb.window8_fixed(jx - S)) : 0u;
 #pragma unroll
         for (int q = 0; q < S; ++q) {
 #pragma unroll
@@ -349,11 +350,13 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
     // delay rings into d(alpha), the adjoint levels advanced (state P, G).
     auto adj_levels = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, int64_t jg, pf2* g,
                           const pf2 (&la)[S][NP], const pf2* h, const pf2* fp) CTA_INLINE {
-      constexpr bool SLOW = decltype(slow_tag)::value;
+      constexpr bool SLOW = decltype(slow_tag)::value == 1 || decltype(slow_tag)::value == 2;
+      constexpr bool ALLF = decltype(slow_tag)::value == 2;
       constexpr int TCT = decltype(tct_tag)::value;
       constexpr int I = decltype(i_tag)::value;
-      const bool f0 = SLOW && rb.fixed(jg);
-      const uint32_t fw = SLOW ? (CAUSAL ? rb.window16_fixed(jg - 2 * S) : rb.window8_fixed(jg - S)) : 0u;
+      const bool f0 = SLOW && (ALLF || rb.fixed(jg));
+      const uint32_t fw =
+          !SLOW ? 0u : ALLF ? 0xffffffffu : (CAUSAL ? rb.window16_fixed(jg - 2 * S) : rb.window8_fixed(jg - S));
       pf2 c[NP], q[NP];
 #pragma unroll
       for (int p = 0; p < NP; ++p) {
@@ -369,7 +372,7 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
         // d(alpha_k): g_k is g, lap(u_{k-1}) is la[k-1]
         // paired row - l0 = t - PRO + e, in [0, nout); only updated rows count
         bool take = (TCT < 0 || TCT + e >= PRO) && (TCT == -2 || I + e < lim);
-        if (SLOW) take = take && !rb.fixed(l0 + t - PRO + e);
+        if (SLOW) take = take && !ALLF && !rb.fixed(l0 + t - PRO + e);
 #pragma unroll
         for (int p = 0; p < NP; ++p) {
           pf2 pg = g[p], pl = la[k - 1][p];
@@ -444,15 +447,19 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
       });
     };
 
+    // slow_tag: 0 = no fixed or zero row near the rows marched, 1 = per-row
+    // tests, 2 = every tested row fixed and none zero (the tests are constants),
+    // 3 = form 0 inside a tile that has fixed rows (its own instantiation).
     // One march row: TCT >= 0 is the compile-time march row of a prologue row
     // (start-up triangles of both wavefronts skipped); I the row in its chunk;
     // lim = nout + PRO - (first march row of the chunk).
     auto step_row = [&](auto slow_tag, auto tct_tag, auto i_tag, int t, int lim, pf2* g, pf2* x) CTA_INLINE {
-      constexpr bool SLOW = decltype(slow_tag)::value;
+      constexpr bool SLOW = decltype(slow_tag)::value == 1 || decltype(slow_tag)::value == 2;
+      constexpr bool ALLF = decltype(slow_tag)::value == 2;
       constexpr int TCT = decltype(tct_tag)::value;
       constexpr int I = decltype(i_tag)::value;
       const int64_t jg = jbg + t, jx = jbx + t;
-      if (SLOW) {
+      if (SLOW && !ALLF) {
         if (rb.zero(jg))
 #pragma unroll
           for (int p = 0; p < NP; ++p) g[p] = 0ull;
@@ -570,8 +577,21 @@ __global__ void __launch_bounds__(kFwdThreads, (da_min_ctas<T, S, CAUSAL>()))
         if (!do_chunk(slow_tag, std::integral_constant<int, 2>{}, 2)) return false;
       }
       int c = NPRO;
-      for (; c < ninner_end; ++c)
-        if (!do_chunk(slow_tag, std::integral_constant<int, NPRO + 2>{}, c)) return false;
+      for (; c < ninner_end; ++c) {
+        if constexpr (decltype(slow_tag)::value) {
+          // a tile with fixed or zero rows picks the form of each inner chunk
+          // from the rows its tests read (the g rows [t0 - 2S - 2, t0 + 10) of
+          // the march cover the x rows and the pairing rows too)
+          const int cls = rb.chunk_class(jbg + c * kFwdRC - 2 * S - 2, kFwdRC + 2 * S + 4);
+          bool ok = true;
+          if (cls == 0) ok = do_chunk(std::integral_constant<int, 3>{}, std::integral_constant<int, NPRO + 2>{}, c);
+          else if (cls == 2) ok = do_chunk(std::integral_constant<int, 2>{}, std::integral_constant<int, NPRO + 2>{}, c);
+          else ok = do_chunk(slow_tag, std::integral_constant<int, NPRO + 2>{}, c);
+          if (!ok) return false;
+        } else if (!do_chunk(slow_tag, std::integral_constant<int, NPRO + 2>{}, c)) {
+          return false;
+        }
+      }
       for (; c < nfull_end; ++c)
         if (!do_chunk(slow_tag, std::integral_constant<int, NPRO>{}, c)) return false;
       if (nfull_end < nch)

@@ -167,10 +167,16 @@ int contract_for(int dtype) {
   return (mode == CTA_ARITH_CONTRACTED && dtype != CTA_F32) ? 1 : 0;
 }
 
+// Tile rows of a march grid: the fewest full waves of `per_sm` CTAs per SM whose
+// tiles fit kBldMaxTL, and tiles sized so that the grid fills those waves
+// evenly (a grid a little over a whole number of waves would run one short
+// extra wave, its duration set by a full tile).
 int pick_tl(int64_t rows, int64_t parallel_ctas, int steps, int per_sm) {
   if (g_tuning.tl_override > 0) return std::min(kBldMaxTL, ((g_tuning.tl_override + kBldRC - 1) / kBldRC) * kBldRC);
   const int64_t target = static_cast<int64_t>(num_sms()) * per_sm;
-  int64_t tl = (rows * std::max<int64_t>(parallel_ctas, 1) + target - 1) / target;
+  const int64_t work = rows * std::max<int64_t>(parallel_ctas, 1);  // tile rows over all column tiles
+  const int64_t waves = std::max<int64_t>(1, (work + target * kBldMaxTL - 1) / (target * kBldMaxTL));
+  int64_t tl = (work + waves * target - 1) / (waves * target);
   tl = ((tl + kBldRC - 1) / kBldRC) * kBldRC;
   const int64_t min_tl = steps >= 6 ? 64 : 32;
   tl = std::max(tl, min_tl);

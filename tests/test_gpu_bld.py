@@ -362,3 +362,50 @@ def test_arithmetic_modes_process_and_thread():
     assert torch.equal(y.cpu(), O.fused_stack(x, [0.1] * 4, layout="bld"))
     with pytest.raises(ValueError):
         ops.bld_forward(xd, [0.1] * 4, 4, arith="fast")
+
+
+def _long_mask(B, L):
+    """Masks whose long tiles hold every chunk form: a padded tail of 3000 rows
+    and a 400-row hole (chunks with every tested row fixed), isolated one-row
+    holes (per-row chunks) and long valid runs (branch-free chunks)."""
+    m = torch.ones(B, L, dtype=torch.long)
+    m[0, L - 3000 :] = 0
+    m[0, 2000:2400] = 0
+    m[-1, 517::700] = 0
+    return m
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("steps", [2, 4, 8])
+@pytest.mark.parametrize("tile", [256, 1024])
+def test_chunk_forms_in_masked_tiles(causal, steps, tile):
+    """Tiles of 256 / 1024 rows (forced) with fixed rows: the forward bit for bit
+    in both dtypes and the backward with d(alpha) against the oracle, so each
+    of the three chunk forms runs next to the others in one tile."""
+    from cta_b200 import _lib
+
+    torch.manual_seed(30 + steps)
+    B, L, D = 2, 8192, 64
+    m = _long_mask(B, L)
+    alphas = [0.1, 0.03, 0.12, 0.05, 0.08, 0.02, 0.11, 0.07][:steps]
+    prev = _lib.set_tuning(1, tile)
+    try:
+        ops = _ops()
+        for dtype in (torch.float32, torch.bfloat16):
+            x = (2.0 * torch.randn(B, L, D)).to(dtype)
+            y = ops.bld_forward(x.cuda(), alphas, steps, causal=causal, mask=m.cuda())
+            ref = O.fused_stack(x, [torch.tensor([a]) for a in alphas], layout="bld", causal=causal,
+                                attention_mask=m, contracted=contracted(dtype))
+            assert torch.equal(y.cpu(), ref), dtype
+        x = torch.randn(B, L, D)
+        g = torch.randn(B, L, D)
+        kw = dict(layout="bld", causal=causal, attention_mask=m)
+        dx_ref, da_ref = O.grads(lambda t, *al: O.fused_stack(t, list(al), **kw), x, g,
+                                 [torch.tensor([a]) for a in alphas])
+        dx, da = ops.bld_backward(g.cuda(), alphas, steps, x=x.cuda(), causal=causal, mask=m.cuda(),
+                                  need_dalpha=True)
+        assert_close(dx, dx_ref)
+        da_ref = torch.cat(da_ref)
+        assert (da.cpu() - da_ref).abs().max().item() <= 1e-4 * max(1.0, da_ref.abs().max().item())
+    finally:
+        _lib.set_tuning(1, prev)
