@@ -447,12 +447,14 @@ def _sharded_parts(args, rank: int, world: int, dev) -> dict:
     gen = torch.Generator(device=dev).manual_seed(1000 + rank)
     x = torch.randn(1, spec.local_len, D, device=dev, dtype=torch.bfloat16, generator=gen)
     g = torch.randn(1, spec.local_len, D, device=dev, dtype=torch.bfloat16, generator=gen)
-    comm = torch.cuda.Stream(device=dev)
+    comm = torch.cuda.Stream(device=dev, priority=-1)
     stream = torch.cuda.current_stream(dev)
+    overlap = args.shard_exchange == "overlap"
 
     def step(timing=None):
-        y = sharded_diffusion(x, spec, alpha=0.1, steps=S, comm_stream=comm, timing=timing)
-        dx = sharded_diffusion(g, spec, alpha=0.1, steps=S, backward=True, comm_stream=comm, timing=timing)
+        y = sharded_diffusion(x, spec, alpha=0.1, steps=S, comm_stream=comm, timing=timing, overlap=overlap)
+        dx = sharded_diffusion(g, spec, alpha=0.1, steps=S, backward=True, comm_stream=comm, timing=timing,
+                               overlap=overlap)
         return y, dx
 
     for _ in range(3):
@@ -481,7 +483,8 @@ def _sharded_parts(args, rank: int, world: int, dev) -> dict:
     bytes_rank = 4 * spec.local_len * D * 2
     nranks = dist.get_world_size() if world > 1 else 1
     return {"workload": "sharded_fwd_adjoint", "L": L, "D": D, "steps": S, "ranks": world,
-            "comm_nranks": nranks, "scaling": "strong", "ms_per_step": t * 1e3, "tokens/s": L / t,
+            "comm_nranks": nranks, "exchange": args.shard_exchange, "scaling": "strong", "ms_per_step": t * 1e3,
+            "tokens/s": L / t,
             "hbm_frac_per_gpu": bytes_rank / t / 1e9 / peak, "parts_us": parts,
             "oracle_windows_ok": not bad, "bad_windows": bad[:4]}
 
@@ -873,12 +876,13 @@ def run_sharded(args, rank, world, local_rank):
     torch.manual_seed(1000 + rank)
     x = torch.randn(1, spec.local_len, D, device=dev, dtype=torch.bfloat16)
     g = torch.randn_like(x)
-    comm = torch.cuda.Stream(device=dev)
+    comm = torch.cuda.Stream(device=dev, priority=-1)
+    overlap = args.shard_exchange == "overlap"
     stream = torch.cuda.current_stream(dev)
 
     def step(_i):
-        sharded_diffusion(x, spec, alpha=0.1, steps=S, comm_stream=comm)
-        sharded_diffusion(g, spec, alpha=0.1, steps=S, backward=True, comm_stream=comm)
+        sharded_diffusion(x, spec, alpha=0.1, steps=S, comm_stream=comm, overlap=overlap)
+        sharded_diffusion(g, spec, alpha=0.1, steps=S, backward=True, comm_stream=comm, overlap=overlap)
 
     for i in range(args.warmup):
         step(i)
@@ -1015,6 +1019,9 @@ def main() -> None:
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sharded", action="store_true", help="skip the L-sharded C5 object of the default line")
+    ap.add_argument("--shard-exchange", choices=["overlap", "first"], default="overlap",
+                    help="sharded object: halo exchange beside the interior kernel on high-priority streams "
+                         "(overlap) or before it on the compute stream (first)")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip the reference's Triton GPU path timed beside ours (default line, N=1)")
     ap.add_argument("--workload", choices=["fused_fwd", "varlen", "block", "sharded", "kernels", "reference_gpu"],
@@ -1045,8 +1052,12 @@ def main() -> None:
         import torch.distributed as dist
 
         torch.cuda.set_device(local_rank)
+        # NCCL on high-priority streams: the halo exchange of the sharded path is
+        # scheduled ahead of the interior kernel's pending CTAs
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
+                                device_id=torch.device("cuda", local_rank), pg_options=opts)
     try:
         {"fused_fwd": run_ours, "varlen": run_varlen, "block": run_block, "sharded": run_sharded,
          "kernels": run_kernels, "reference_gpu": run_reference_gpu}[args.workload](

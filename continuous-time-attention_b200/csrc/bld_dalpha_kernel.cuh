@@ -154,7 +154,7 @@ constexpr int da_min_ctas() {
 //   d(beta) = sum over updated rows of g[i] * h(x)[i], next to d(alpha)
 // At steps 1 the adjoint and the recomputed stencil of a row meet in the same
 // march step (delay 0), so no delay line is needed.
-__device__ __forceinline__ float da_sigmoid(float v) { return __frcp_rn(__fadd_rn(1.0f, __expf(-v))); }
+__device__ __forceinline__ float da_sigmoid(float v) { return __fdividef(1.0f, __fadd_rn(1.0f, __expf(-v))); }
 
 // per element of a pair: s = sigmoid(v); f(v) = v * (1 - s); f'(v) = (1 - s) * (1 - v s)
 __device__ __forceinline__ pf2 psigmoid(pf2 v) {

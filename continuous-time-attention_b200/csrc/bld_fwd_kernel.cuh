@@ -93,7 +93,7 @@ constexpr int march_min_ctas() {
 // op order: c + (alpha*lap + beta-term), beta-term = beta * (x[i+1] - x[i-1]) / 2
 // (causal beta * (x[i] - x[i-1])) or (beta * c) * (1 - sigmoid(c)).
 // (p2, p1, x) = rows (i-1, i, i+1) non-causal, (i-2, i-1, i) causal.
-__device__ __forceinline__ float fast_sigmoid(float v) { return __frcp_rn(__fadd_rn(1.0f, __expf(-v))); }
+__device__ __forceinline__ float fast_sigmoid(float v) { return __fdividef(1.0f, __fadd_rn(1.0f, __expf(-v))); }
 
 template <int KIND, bool CAUSAL, bool FM = false>
 __device__ __forceinline__ pf2 level_update(pf2 p2, pf2 p1, pf2 x, pf2 al, pf2 be, float be_s, pf2 m2, pf2 zn) {
@@ -291,10 +291,12 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
   const int soff = cb;  // element offset of this lane in a slot row
 
   pf2 pool_a = 0ull, pool_b = 0ull;  // POOL: masked column sums of this lane
-  auto store_row = [&](int64_t orow, pf2 pa, pf2 pb) CTA_INLINE {
+  // allv_tag true: the row is known to be a valid row of the sequence (a chunk
+  // with no fixed row near it), so the pooled form skips its mask bit
+  auto store_row = [&](int64_t orow, pf2 pa, pf2 pb, auto allv_tag) CTA_INLINE {
     if constexpr (POOL) {
       const int64_t p = orow - jb + 32;  // fbits layout: word 0 is the guard word
-      if (col_ok && ((pbits[p >> 5] >> (p & 31)) & 1u)) {
+      if (col_ok && (decltype(allv_tag)::value || ((pbits[p >> 5] >> (p & 31)) & 1u))) {
         pf2 ra, rb2;
         Q::split(Q::join(pa, pb), ra, rb2);  // the values the stored tensor would hold
         pool_a = padd(pool_a, ra);
@@ -534,7 +536,7 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
           if constexpr (RES) y = vec_add_round<Q>(y, *reinterpret_cast<const V*>(st + i * kFwdDT));
           *reinterpret_cast<V*>(st + i * kFwdDT) = y;
         } else {
-          store_row(l0 + t0 + i - PRO, ua[i], ub[i]);
+          store_row(l0 + t0 + i - PRO, ua[i], ub[i], std::true_type{});
         }
       }
       return;
@@ -555,10 +557,10 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
             if constexpr (RES) y = vec_add_round<Q>(y, *reinterpret_cast<const V*>(st + i * kFwdDT));
             *reinterpret_cast<V*>(st + i * kFwdDT) = y;
           } else {
-            store_row(orow, xa, xb);
+            store_row(orow, xa, xb, std::false_type{});
           }
         } else {
-          if (t0 + i < nrows) store_row(orow, xa, xb);
+          if (t0 + i < nrows) store_row(orow, xa, xb, std::false_type{});
         }
       }
     });

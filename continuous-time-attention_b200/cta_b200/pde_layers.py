@@ -23,9 +23,9 @@ Drop-in for the diffusion family of the reference's src/models/pde_layers.py:
 
 Arithmetic follows the reference op by op (fp32, no fused multiply-add), so a
 single fp32 or bf16 diffusion, wave or advection layer step is bit-identical to
-the reference layer; the reaction layer's sigmoid uses the fast intrinsic
-``__expf`` with a rounded reciprocal (``__frcp_rn``), so it matches to fp32
-rounding rather than bit for bit.
+the reference layer; the reaction layer's sigmoid uses the fast intrinsics
+``__expf`` and ``__fdividef``, so it matches to fp32 rounding rather than bit
+for bit.
 """
 from __future__ import annotations
 

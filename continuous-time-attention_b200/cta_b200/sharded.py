@@ -120,15 +120,27 @@ def sharded_diffusion(
     comm_stream: Optional[torch.cuda.Stream] = None,
     compute: Optional[Callable] = None,
     timing: Optional[dict] = None,
+    overlap: bool = True,
 ) -> torch.Tensor:
     """Fused `steps`-step stencil (or its adjoint) of this rank's shard.
 
     Every rank must call this with the same steps / causal / backward; ranks
     exchange halos with their neighbours only.  Returns the local output shard.
+
+    `overlap` (CUDA): True posts the halo exchange and then the two edge kernels
+    on the side stream `comm_stream` before the interior kernel is launched on
+    the caller's stream, so the exchange runs beside the interior.  It needs
+    NCCL on high-priority streams (ProcessGroupNCCL.Options with
+    is_high_priority_stream, or TORCH_NCCL_HIGH_PRIORITY=1) and a high-priority
+    `comm_stream` (the default one is): otherwise the interior's CTAs, which
+    fill every SM, are scheduled ahead of NCCL's and the exchange waits for the
+    interior to drain.  False exchanges first on the caller's stream (fully
+    exposed, ~one NCCL round trip), then runs the edges beside the interior.
+
     `timing` (CUDA only): a dict that receives pairs of recorded CUDA events per
-    part -- "interior" (the interior kernel), "exchange" (the halo send/recv on the
-    comm stream), "exposed_wait" (compute stream idle between the interior kernel
-    and the halos' arrival) and "edges" (both edge kernels) -- for the caller to
+    part -- "interior" (the interior kernel), "exchange" (the halo send/recv),
+    "exposed_wait" (caller stream idle after the interior kernel until the side
+    stream's work is done) and "edges" (both edge kernels) -- for the caller to
     read after a synchronize.
     """
     if x_local.dim() != 3:
@@ -173,17 +185,23 @@ def sharded_diffusion(
     kw = dict(spec=spec, alpha=alpha, steps=steps, causal=causal, backward=backward)
     ev = _PartEvents(timing if on_gpu else None)
     if on_gpu:
-        comm = comm_stream if comm_stream is not None else torch.cuda.Stream(device=x_local.device)
-        # The halo exchange runs first, on the caller's stream.  NCCL's kernel
-        # needs SMs: queued beside the interior kernel, whose one-warp CTAs fill
-        # every SM in one wave, it would only start at that kernel's tail.
-        ev.begin("exchange", cur)
-        for w in post_exchange():
-            w.wait()
-        ev.end("exchange", cur)
-        # the edge parts read the halos; on the side stream, launched before the
-        # interior, their few CTAs run beside the interior's wave
+        comm = comm_stream if comm_stream is not None else torch.cuda.Stream(device=x_local.device, priority=-1)
         comm.wait_stream(cur)
+        if overlap:
+            # exchange and edges on the side stream, queued ahead of the interior
+            with torch.cuda.stream(comm):
+                ev.begin("exchange", comm)
+                for w in post_exchange():
+                    w.wait()
+                ev.end("exchange", comm)
+        else:
+            # the exchange first, on the caller's stream
+            ev.begin("exchange", cur)
+            for w in post_exchange():
+                w.wait()
+            ev.end("exchange", cur)
+            comm.wait_stream(cur)
+        # the edge parts read the halos; their few CTAs run beside the interior
         with torch.cuda.stream(comm):
             ev.begin("edges", comm)
             compute(_lib.SHARD_LO_EDGE, x_local, out, lo_halo=lo_halo, hi_halo=hi_halo, **kw)
@@ -249,10 +267,15 @@ def sharded_diffusion_backward_dalpha(
     group: Optional[dist.ProcessGroup] = None,
     comm_stream: Optional[torch.cuda.Stream] = None,
     compute: Optional[Callable] = None,
+    overlap: bool = True,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Backward of `steps` fused steps with per-step `alphas` on this rank's
     shard: returns (dx_local, dalpha), dalpha (fp32 [steps]) summed over all
-    ranks of `group`.  Every rank must call this with the same arguments."""
+    ranks of `group`.  Every rank must call this with the same arguments.
+    `overlap` as in `sharded_diffusion`: the exchange on the side stream beside
+    the interior kernel (True) or first on the caller's stream (False); the
+    edge parts run after the interior either way, because the three parts add
+    their d(alpha) sums to one buffer in a fixed order."""
     if g_local.dim() != 3 or tuple(x_local.shape) != tuple(g_local.shape):
         raise ValueError("g_local and x_local must both be (B, L_local, D)")
     if not 1 <= steps <= _lib.MAX_STEPS:
@@ -308,9 +331,20 @@ def sharded_diffusion_backward_dalpha(
 
     kw = dict(spec=spec, alphas=alphas, steps=steps, causal=causal)
     none = dict(g_lo=None, g_hi=None, x_lo=None, x_hi=None)
-    if on_gpu:
-        # exchange first on the caller's stream (see sharded_diffusion); the parts
-        # then add their d(alpha) sums in a fixed order: interior, lo edge, hi edge
+    if on_gpu and overlap:
+        comm = comm_stream if comm_stream is not None else torch.cuda.Stream(device=dev, priority=-1)
+        comm.wait_stream(cur)
+        with torch.cuda.stream(comm):
+            for w in post_exchange():
+                w.wait()
+        compute(_lib.SHARD_INTERIOR, g_local, x_local, dx, dalpha, **none, **kw)
+        cur.wait_stream(comm)
+        for t in halos.values():
+            if t is not None:
+                t.record_stream(comm)
+    elif on_gpu:
+        # exchange first on the caller's stream; the parts then add their
+        # d(alpha) sums in a fixed order: interior, lo edge, hi edge
         for w in post_exchange():
             w.wait()
         compute(_lib.SHARD_INTERIOR, g_local, x_local, dx, dalpha, **none, **kw)

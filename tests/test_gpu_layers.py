@@ -185,7 +185,7 @@ def _two_coef_layer(kind, D, layout, causal, alpha=0.12, beta=0.07):
 
 def test_pde_step_layers_match_reference_golden(golden):
     """The reference's own layer outputs: advection bit for bit, reaction (its
-    sigmoid uses the __expf intrinsic and __frcp_rn here) to the fp32 / bf16 bar; gradients within tolerance."""
+    sigmoid uses the __expf and __fdividef intrinsics here) to the fp32 / bf16 bar; gradients within tolerance."""
     for c in golden["pde_step"]:
         D = c["x"].shape[2] if c["layout"] == "bld" else c["x"].shape[1]
         layer = _two_coef_layer(c["kind"], D, c["layout"], c["causal"], c["alpha"], c["beta"])
