@@ -208,6 +208,14 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
     tma_load_3d(ring + slot * CHUNK, &xmap, &full_bar[slot], d0, static_cast<int>(sg.row0 + jb + c * kFwdRC),
                 sg.bcoord);
   };
+  // the same, executed by the whole warp and issued by lane 0 only
+  auto issue_lane0 = [&](int c) {
+    const int slot = c % kFwdStages;
+    const bool lead = tid == 0;
+    mbar_arrive_expect_tx_if(lead, &full_bar[slot], CHUNK * sizeof(T));
+    tma_load_3d_if(lead, ring + slot * CHUNK, &xmap, &full_bar[slot], d0,
+                   static_cast<int>(sg.row0 + jb + c * kFwdRC), sg.bcoord);
+  };
   // the first loads fly while the fixed-row bitmap is built
   if (use_tma && tid == 0) {
     for (int c = 0; c < nch && c < kFwdStages; ++c) issue(c);
@@ -586,8 +594,9 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
     if (!err) march_chunk(slow_tag, kind_tag, c, buf);
     if (FULL && tstore) fence_proxy_async_smem();
     // the store issued after the previous chunk must have finished reading the
-    // staging slot that the next chunk overwrites
-    if (tstore && tid == 0) bulk_wait_read_all();
+    // staging slot that the next chunk overwrites (lanes without bulk groups
+    // pass at once)
+    if (tstore && (CTA_FWD_PRED || tid == 0)) bulk_wait_read_all();
     __syncwarp();
     if (__any_sync(0xffffffffu, err)) {
       if (tid == 0) {
@@ -604,7 +613,15 @@ __global__ void __launch_bounds__(kFwdThreads, (march_min_ctas<T, S, CAUSAL, ADJ
       __syncwarp();
       return false;
     }
-    if (tid == 0) {
+    if constexpr (CTA_FWD_PRED && !RES) {
+      // warp-uniform conditions, lane-0 predicated instructions: no divergence
+      if (FULL && tstore) {
+        const int orow0 = static_cast<int>(sg.row0 + l0 + c * kFwdRC - PRO);
+        tma_store_3d_if(tid == 0, &ymap, stage + ((c - NPRO) & 1) * CHUNK, d0, orow0, sg.bcoord);
+        bulk_commit_if(tid == 0);
+      }
+      if (!(CTA_FWD_PRELOAD && CTA_FWD_EARLY_REFILL) && use_tma && c + kFwdStages < nch) issue_lane0(c + kFwdStages);
+    } else if (tid == 0) {
       if (FULL && tstore) {
         const int orow0 = static_cast<int>(sg.row0 + l0 + c * kFwdRC - PRO);
         tma_store_3d(&ymap, stage + ((c - NPRO) & 1) * CHUNK, d0, orow0, sg.bcoord);

@@ -368,6 +368,41 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
       : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Predicated forms for one-warp CTAs: every lane executes the instruction and
+// only a lane whose `p` is true issues it, so a lane-0 TMA section costs no
+// divergent branch and no reconvergence.
+__device__ __forceinline__ void mbar_arrive_expect_tx_if(bool p, uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t"
+      "@q mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n\t}" ::"r"(smem_addr(bar)),
+      "r"(bytes), "r"(static_cast<uint32_t>(p))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_if(bool p, void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                               int c1, int c2) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %6, 0;\n\t"
+      "@q cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];\n\t}" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(static_cast<uint32_t>(p))
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_3d_if(bool p, const CUtensorMap* map, const void* src, int c0, int c1,
+                                                int c2) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %5, 0;\n\t"
+      "@q cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];\n\t}" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_addr(src)), "r"(c0), "r"(c1), "r"(c2), "r"(static_cast<uint32_t>(p))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_if(bool p) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %0, 0;\n\t@q cp.async.bulk.commit_group;\n\t}" ::"r"(
+                   static_cast<uint32_t>(p))
+               : "memory");
+}
 // all committed bulk stores have finished READING their shared-memory source
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // all committed bulk stores are complete

@@ -39,6 +39,11 @@ constexpr int kFwdMinCtas = CTA_FWD_MIN_CTAS;  // register budget (one-warp CTAs
 #ifndef CTA_FWD_DIAG
 #define CTA_FWD_DIAG 1
 #endif
+// forward march: lane 0's per-chunk TMA issue as predicated instructions of the
+// whole warp (1) or inside a lane-0 branch (0)
+#ifndef CTA_FWD_PRED
+#define CTA_FWD_PRED 1
+#endif
 #ifndef CTA_FWD_EARLY_REFILL
 #define CTA_FWD_EARLY_REFILL 0
 #endif
